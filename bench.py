@@ -1,0 +1,360 @@
+"""Training-step benchmark of go-tensor's B200 backend.
+
+Workload: the wide MLP Linear(4096,4096)-ReLU-Linear(4096,4096)-ReLU-
+Linear(4096,1000), float32, global batch 8192 (N(0,1) inputs, labels uniform
+in 0..999), CrossEntropyLoss, SGD lr 0.01 momentum 0.9 weight decay 1e-4;
+the batch is sharded over the GPUs (strong scaling), gradients averaged with
+NCCL. A step is one forward + backward + optimizer update of the whole batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU. Rank 0 prints one JSON line.
+`--impl reference` times go-tensor's CPU path (the oracle's restatement of
+internal/cpu and the tensor/nn/optim layers, all host threads) on a bounded
+sample of the same workload and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "go-tensor_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "train samples/sec (fwd+bwd+step)"
+WORKLOAD = "wide_mlp_4096-4096-4096-1000_b8192_sgd"
+GLOBAL_BATCH = 8192
+IN, HID, OUT = 4096, 4096, 1000
+LR, MOM, WD = 0.01, 0.9, 1e-4
+# fwd + dW for every layer + dX for layers 2-3, per sample (2 flops per MAC)
+GEMM_FLOPS_PER_SAMPLE = 2 * (3 * IN * HID + 3 * HID * HID + 3 * HID * OUT - IN * HID)
+BWD_GEMM_FLOPS_PER_SAMPLE = 2 * (2 * IN * HID + 2 * HID * HID + 2 * HID * OUT - IN * HID)
+CPU_SAMPLE_ROWS = 256
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def clocks_sampler(index: int):
+    fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    out = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+    try:
+        p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                              "-lms", "200"], stdout=out, stderr=subprocess.DEVNULL)
+    except OSError:
+        p = None
+    return p, out.name
+
+
+def clocks_summary(proc, path):
+    if proc is None:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    proc.terminate()
+    try:
+        proc.wait(timeout=5)
+    except subprocess.TimeoutExpired:
+        proc.kill()
+    sm, smax, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    with open(path) as f:
+        for line in f:
+            c = [x.strip() for x in line.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                sm.append(float(c[1]))
+                smax.append(float(c[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, c[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+    os.unlink(path)
+    if not sm:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+    loaded = [s for s in sm if s >= 0.5 * max(sm)] or sm
+    return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+            "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle's restatement of go-tensor's CPU path
+
+def cpu_step_time(rows: int, steps: int, warmup: int, threads: int):
+    from oracle import gotensor_ref as T
+    from oracle import nn_ref as nn
+    from oracle import optim_ref as optim
+    T.SetDefaultDType(T.Float32)
+    T._factories[T.CPU_TYPE] = lambda index: T.CPUBackend(threads)
+    T._backends.clear()
+    T.ManualSeed(1)
+    model = nn.NewSequential(nn.NewLinear(IN, HID), nn.NewReLU(), nn.NewLinear(HID, HID), nn.NewReLU(),
+                             nn.NewLinear(HID, OUT))
+    opt = optim.NewSGD(model.Parameters(), optim.SGDConfig(LR=LR, Momentum=MOM, WeightDecay=WD))
+    rng = np.random.default_rng(1)
+    x = T.New(rng.standard_normal(rows * IN), rows, IN)
+    y = list(rng.integers(0, OUT, rows))
+    times = []
+    for i in range(warmup + steps):
+        t = time.perf_counter()
+        loss = nn.CrossEntropyLoss(model.Forward(x), y)
+        opt.ZeroGrad()
+        loss.Backward()
+        opt.Step()
+        loss.Item()
+        if i >= warmup:
+            times.append(time.perf_counter() - t)
+    return times
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    times = cpu_step_time(CPU_SAMPLE_ROWS, args.steps, args.warmup, threads)
+    total = sum(times)
+    value = CPU_SAMPLE_ROWS * len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) inputs, uniform labels)",
+        "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "sample_rows_per_step": CPU_SAMPLE_ROWS},
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
+                         "sample": f"{CPU_SAMPLE_ROWS} rows of the batch per step, {len(times)} steps, oracle "
+                                   "restatement of go-tensor's CPU backend and tensor/nn/optim (Go absent)"},
+        "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+
+def init_dist(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def allgather_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def run_ours(args):
+    import torch
+
+    from gotensor import model as gm
+    from gotensor._lib import check, cuda_lib
+    rank, world, local = init_dist(args.gpus)
+    torch.cuda.set_device(local)
+    if GLOBAL_BATCH % world:
+        raise SystemExit("the global batch must divide evenly over the GPUs")
+    B = GLOBAL_BATCH // world
+    layers = [gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, HID), gm.ReLU(), gm.Linear(HID, OUT)]
+    model = gm.Model(layers, [B, IN], device=local)
+    lib, ctx = cuda_lib(), model.ctx.ptr
+    rng = np.random.default_rng(1)  # same weights on every rank
+    sd = {}
+    for name, shape, _ in model.params:
+        fan_in = IN if name.startswith("0.") else HID
+        sd[name] = rng.uniform(-1 / np.sqrt(fan_in), 1 / np.sqrt(fan_in), shape).astype(np.float32)
+    model.load_state_dict(sd)
+    model.sgd(LR, MOM, WD)
+    if world > 1:
+        import torch.distributed as dist
+        obj = [gm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        model.dp_init(rank, world, obj[0], timeout_ms=120000, bucket_bytes=args.bucket_mb << 20)
+    model.enable_graph(not args.no_graph)
+
+    # This rank's shard of the batch, in pinned host memory for the e2e leg.
+    drng = np.random.default_rng(100 + rank)
+    x_np = drng.standard_normal((B, IN)).astype(np.float32)
+    y_np = drng.integers(0, OUT, B).astype(np.int32)
+    xh = torch.from_numpy(x_np).pin_memory()
+    yh = torch.from_numpy(y_np).pin_memory()
+    loss_h = torch.zeros(1, dtype=torch.float32).pin_memory()
+    h2d = xh.numel() * 4 + yh.numel() * 4
+    model.set_batch(x_np, y_np)
+
+    def step_resident():
+        model.train_step()
+
+    def step_e2e():
+        check(lib.gt_upload_async(ctx, model.input_device, xh.data_ptr(), xh.numel() * 4))
+        check(lib.gt_upload_async(ctx, model.labels_device, yh.data_ptr(), yh.numel() * 4))
+        model.train_step()
+        check(lib.gt_download_async(ctx, loss_h.data_ptr(), model.lib.gth_loss_device(model.ptr), 4))
+
+    def timed(fn, k):
+        barrier(world)
+        model.ctx.sync()
+        torch.cuda.synchronize()
+        check(lib.gt_mark(ctx, 0))
+        for _ in range(k):
+            fn()
+        check(lib.gt_mark(ctx, 1))
+        ms = ctypes.c_float()
+        check(lib.gt_elapsed_ms(ctx, 0, 1, ctypes.byref(ms)))
+        model.ctx.sync()
+        torch.cuda.synchronize()
+        barrier(world)
+        return allgather_max(ms.value, world)
+
+    for _ in range(max(args.warmup, 3)):
+        step_resident()
+    model.ctx.sync()
+    launches_per_step = model.step_launches
+    before = lib.gt_launch_count()
+    proc, cpath = clocks_sampler(local)
+    ms_total = timed(step_resident, args.steps)
+    clocks = clocks_summary(proc, cpath)
+    launches = lib.gt_launch_count() - before
+    if launches == 0:  # graph replays launch without passing through the library's counter
+        launches = launches_per_step * args.steps
+    value = GLOBAL_BATCH * args.steps / (ms_total / 1e3)
+    loss = model.loss()
+
+    for _ in range(2):
+        step_e2e()
+    ms_e2e = timed(step_e2e, args.steps)
+    e2e = GLOBAL_BATCH * args.steps / (ms_e2e / 1e3)
+
+    # Roofline of the dominant kernel: the backward GEMMs (3xTF32 tcgen05) of
+    # the two 4096x4096 layers, launched alone on the model's stream with the
+    # same shapes, timed with CUDA events.
+    roof = gemm_roofline(lib, model, B)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        threads = os.cpu_count() or 1
+        times = cpu_step_time(CPU_SAMPLE_ROWS, 3, 1, threads)
+        cpu = {"value": CPU_SAMPLE_ROWS * len(times) / sum(times), "unit": "samples/s", "cores": threads,
+               "kind": "port", "sample": f"{CPU_SAMPLE_ROWS} rows per step, {len(times)} timed steps after 1 "
+                                         "warm-up; oracle restatement of go-tensor's CPU path (Go absent)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) inputs, uniform labels, PyTorch-style uniform init)",
+            "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "per_gpu_batch": B,
+                       "parallelism": f"dp{world}", "optimizer": "sgd(lr=0.01, momentum=0.9, wd=1e-4)",
+                       "graph": not args.no_graph,
+                       "l2": "per-step working set (weights, grads, momentum 452 MB + activations) exceeds L2",
+                       "gemm": "tcgen05 3xTF32" if roof.get("path") == "tc" else "SIMT fp32"},
+            "loss_after": loss,
+            "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+            "gpu_launches": int(launches),
+            "roofline": roof["roofline"],
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    del model
+    return 0
+
+
+def gemm_roofline(lib, model, B):
+    from gotensor._lib import check
+    ctx = model.ctx
+    hbm, bf16, kind = peaks()
+    # 3xTF32: three TF32 products per fp32 MAC; TF32 runs at half the bf16 rate.
+    peak = bf16 / 2 / 3
+    fp = model.ctx.alloc
+    x = fp(B * HID * 4)
+    dy = fp(B * HID * 4)
+    w = fp(HID * HID * 4)
+    dw = fp(HID * HID * 4)
+    dx = fp(B * HID * 4)
+    rng = np.random.default_rng(5)
+    for p, n in ((x, B * HID), (dy, B * HID), (w, HID * HID)):
+        # realistic operands: tensor-core power (and so clocks) depend on the data
+        h = rng.standard_normal(n, dtype=np.float32)
+        check(lib.gt_upload(ctx.ptr, p, h.ctypes.data, n * 4))
+    reps = 10
+    for _ in range(2):
+        check(lib.gt_linear_bwd_weight(ctx.ptr, 0, x, dy, dw, None, B, HID, HID))
+        check(lib.gt_linear_bwd_data(ctx.ptr, 0, dy, w, x, 1, dx, B, HID, HID))
+    check(lib.gt_mark(ctx.ptr, 2))
+    for _ in range(reps):
+        check(lib.gt_linear_bwd_weight(ctx.ptr, 0, x, dy, dw, None, B, HID, HID))
+        check(lib.gt_linear_bwd_data(ctx.ptr, 0, dy, w, x, 1, dx, B, HID, HID))
+    check(lib.gt_mark(ctx.ptr, 3))
+    ms = ctypes.c_float()
+    check(lib.gt_elapsed_ms(ctx.ptr, 2, 3, ctypes.byref(ms)))
+    per_launch_ms = ms.value / (2 * reps)
+    flops = 2.0 * B * HID * HID
+    achieved = flops / (per_launch_ms / 1e3) / 1e12
+    for p in (x, dy, w, dw, dx):
+        ctx.release(p)
+    return {"path": "tc" if os.environ.get("GT_GEMM_PATH", "") != "simt" else "simt",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": f"backward GEMMs of a 4096x4096 layer (dW and dX, M=K=4096, batch {B})",
+                         "per_launch_ms": per_launch_ms, "flops_per_launch": flops,
+                         "peak_note": f"3xTF32 peak = {kind} bf16 burst {bf16:.0f} TF/s / 2 (TF32) / 3 (products)"}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--bucket-mb", type=int, default=32)
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

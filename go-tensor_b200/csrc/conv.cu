@@ -1,0 +1,346 @@
+// Convolution helpers and pooling: Backend.Im2col/Col2im/MaxPool2d/
+// MaxPool2dBackward (internal/backend/backend.go:152-156), restated from
+// internal/cpu/linalg.go:94-191, plus the fused Conv2d and pool-with-argmax
+// entry points.
+//
+// The reference scatters (col2im adds every patch entry into the input;
+// the pool backward adds every window's gradient into its first maximum).
+// Here each output element gathers instead, visiting its contributions in the
+// same order the reference adds them, so both are bit-exact and need no
+// atomics.
+#include "gemm.cuh"
+
+namespace gt {
+
+// cols[(n*OH + oh)*OW + ow][(c*KH + kh)*KW + kw] = x[n][c][ih][iw] or 0.
+template <typename T>
+__global__ void im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, gt_geom g, int64_t total) {
+  const int64_t K = g.C * g.KH * g.KW;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = e / K, k = e - row * K;
+    int64_t ow = row % g.OW, t = row / g.OW;
+    int64_t oh = t % g.OH, n = t / g.OH;
+    int64_t kw = k % g.KW, t2 = k / g.KW;
+    int64_t kh = t2 % g.KH, c = t2 / g.KH;
+    int64_t ih = oh * g.stride - g.pad + kh, iw = ow * g.stride - g.pad + kw;
+    T v = (T)0;
+    if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) v = x[((n * g.C + c) * g.H + ih) * g.W + iw];
+    cols[e] = v;
+  }
+}
+
+// x[n][c][ih][iw] = sum over the patches (oh, ow) that read it, in row order.
+template <typename T>
+__global__ void col2im_kernel(const T* __restrict__ cols, T* __restrict__ x, gt_geom g, int64_t total) {
+  const int64_t K = g.C * g.KH * g.KW;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t iw = e % g.W, t = e / g.W;
+    int64_t ih = t % g.H, t2 = t / g.H;
+    int64_t c = t2 % g.C, n = t2 / g.C;
+    int64_t hp = ih + g.pad, wp = iw + g.pad;
+    // oh*stride <= hp and oh*stride > hp - KH
+    int64_t oh_lo = hp - g.KH + 1 > 0 ? (hp - g.KH + 1 + g.stride - 1) / g.stride : 0;
+    int64_t oh_hi = hp / g.stride < g.OH - 1 ? hp / g.stride : g.OH - 1;
+    int64_t ow_lo = wp - g.KW + 1 > 0 ? (wp - g.KW + 1 + g.stride - 1) / g.stride : 0;
+    int64_t ow_hi = wp / g.stride < g.OW - 1 ? wp / g.stride : g.OW - 1;
+    T acc = (T)0;
+    for (int64_t oh = oh_lo; oh <= oh_hi; oh++) {
+      int64_t kh = hp - oh * g.stride;
+      for (int64_t ow = ow_lo; ow <= ow_hi; ow++) {
+        int64_t kw = wp - ow * g.stride;
+        int64_t row = (n * g.OH + oh) * g.OW + ow;
+        acc = add_rn(acc, cols[row * K + (c * g.KH + kh) * g.KW + kw]);
+      }
+    }
+    x[e] = acc;
+  }
+}
+
+// First maximum of a window, as internal/cpu/linalg.go:169-176:
+// `if v > best || bestIdx < 0`.
+template <typename T>
+__device__ __forceinline__ int window_argmax(const T* __restrict__ plane, const gt_geom& g, int64_t oh, int64_t ow,
+                                             T* best_out) {
+  T best = (T)(-INFINITY);
+  int best_k = -1;
+  for (int64_t kh = 0; kh < g.KH; kh++)
+    for (int64_t kw = 0; kw < g.KW; kw++) {
+      T v = plane[(oh * g.stride + kh) * g.W + ow * g.stride + kw];
+      if (v > best || best_k < 0) {
+        best = v;
+        best_k = (int)(kh * g.KW + kw);
+      }
+    }
+  *best_out = best;
+  return best_k;
+}
+
+template <typename T>
+__global__ void maxpool_fwd_kernel(const T* __restrict__ x, T* __restrict__ out, uint8_t* __restrict__ idx, gt_geom g,
+                                   int64_t total) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t ow = e % g.OW, t = e / g.OW;
+    int64_t oh = t % g.OH, pl = t / g.OH;
+    T best;
+    int k = window_argmax(x + pl * g.H * g.W, g, oh, ow, &best);
+    out[e] = best;
+    if (idx) idx[e] = (uint8_t)k;
+  }
+}
+
+// dx[pl][ih][iw] = sum of grad over the windows whose first maximum is this
+// element, visited in increasing window order (the reference's order).
+template <typename T>
+__global__ void maxpool_bwd_kernel(const T* __restrict__ x, const T* __restrict__ grad, T* __restrict__ dx, gt_geom g,
+                                   int64_t total) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t iw = e % g.W, t = e / g.W;
+    int64_t ih = t % g.H, pl = t / g.H;
+    const T* plane = x + pl * g.H * g.W;
+    int64_t oh_lo = ih - g.KH + 1 > 0 ? (ih - g.KH + 1 + g.stride - 1) / g.stride : 0;
+    int64_t oh_hi = ih / g.stride < g.OH - 1 ? ih / g.stride : g.OH - 1;
+    int64_t ow_lo = iw - g.KW + 1 > 0 ? (iw - g.KW + 1 + g.stride - 1) / g.stride : 0;
+    int64_t ow_hi = iw / g.stride < g.OW - 1 ? iw / g.stride : g.OW - 1;
+    T acc = (T)0;
+    for (int64_t oh = oh_lo; oh <= oh_hi; oh++)
+      for (int64_t ow = ow_lo; ow <= ow_hi; ow++) {
+        T best;
+        int k = window_argmax(plane, g, oh, ow, &best);
+        if ((ih - oh * g.stride) * g.KW + (iw - ow * g.stride) == k)
+          acc = add_rn(acc, grad[(pl * g.OH + oh) * g.OW + ow]);
+      }
+    dx[e] = acc;
+  }
+}
+
+// Non-overlapping windows: each input element lies in at most one window, so
+// dx is grad at the recorded maximum (times relu'(pooled) when the pool
+// follows a ReLU) and zero elsewhere.
+template <typename T>
+__global__ void maxpool_bwd_idx_kernel(const T* __restrict__ grad, const uint8_t* __restrict__ idx,
+                                       const T* __restrict__ pooled, int relu_mask, T* __restrict__ dx, gt_geom g,
+                                       int64_t total) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t iw = e % g.W, t = e / g.W;
+    int64_t ih = t % g.H, pl = t / g.H;
+    int64_t oh = ih / g.stride, ow = iw / g.stride;
+    int64_t kh = ih - oh * g.stride, kw = iw - ow * g.stride;
+    T v = (T)0;
+    if (oh < g.OH && ow < g.OW && kh < g.KH && kw < g.KW) {
+      int64_t w = (pl * g.OH + oh) * g.OW + ow;
+      if (idx[w] == (uint8_t)(kh * g.KW + kw)) {
+        v = grad[w];
+        if (relu_mask) v = mul_rn(v, pooled[w] > (T)0 ? (T)1 : (T)0);
+      }
+    }
+    dx[e] = v;
+  }
+}
+
+static char* check_geom(const gt_geom* g, const char* what) {
+  if (!g) return errorf("%s: null geometry", what);
+  if (g->N < 0 || g->C < 0 || g->H < 0 || g->W < 0 || g->KH <= 0 || g->KW <= 0 || g->stride < 1 || g->pad < 0 ||
+      g->OH < 0 || g->OW < 0)
+    return errorf("%s: invalid geometry", what);
+  if (g->OH != (g->H + 2 * g->pad - g->KH) / g->stride + 1 || g->OW != (g->W + 2 * g->pad - g->KW) / g->stride + 1)
+    return errorf("%s: OH/OW do not match the geometry", what);
+  return nullptr;
+}
+
+template <typename T>
+static char* im2col_launch(gt_ctx* ctx, const T* x, T* cols, const gt_geom& g) {
+  int64_t total = g.N * g.OH * g.OW * g.C * g.KH * g.KW;
+  if (total == 0) return nullptr;
+  im2col_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(x, cols, g, total);
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+template <typename T>
+static char* col2im_launch(gt_ctx* ctx, const T* cols, T* x, const gt_geom& g) {
+  int64_t total = g.N * g.C * g.H * g.W;
+  if (total == 0) return nullptr;
+  col2im_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(cols, x, g, total);
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+}  // namespace gt
+
+using namespace gt;
+
+extern "C" {
+
+char* gt_im2col(gt_ctx* ctx, int dtype, const void* x, void* cols, const gt_geom* g) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_im2col"));
+  GT_DISPATCH(dtype, { return im2col_launch<T>(ctx, (const T*)x, (T*)cols, *g); });
+  return nullptr;
+}
+
+char* gt_col2im(gt_ctx* ctx, int dtype, const void* cols, void* x, const gt_geom* g) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_col2im"));
+  GT_DISPATCH(dtype, { return col2im_launch<T>(ctx, (const T*)cols, (T*)x, *g); });
+  return nullptr;
+}
+
+char* gt_maxpool_fwd(gt_ctx* ctx, int dtype, const void* x, void* out, const gt_geom* g) {
+  return gt_maxpool_fwd_idx(ctx, dtype, x, out, nullptr, g);
+}
+
+char* gt_maxpool_fwd_idx(gt_ctx* ctx, int dtype, const void* x, void* out, uint8_t* idx, const gt_geom* g) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_maxpool_fwd"));
+  if (g->pad != 0) return errorf("gt_maxpool_fwd: pooling has no padding");
+  if (idx && g->KH * g->KW > 256) return errorf("gt_maxpool_fwd_idx: window larger than 256 elements");
+  int64_t total = g->N * g->C * g->OH * g->OW;
+  if (total == 0) return nullptr;
+  GT_DISPATCH(dtype, {
+    maxpool_fwd_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>((const T*)x, (T*)out, idx, *g, total);
+  });
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+char* gt_maxpool_bwd(gt_ctx* ctx, int dtype, const void* x, const void* grad, void* dx, const gt_geom* g) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_maxpool_bwd"));
+  if (g->pad != 0) return errorf("gt_maxpool_bwd: pooling has no padding");
+  int64_t total = g->N * g->C * g->H * g->W;
+  if (total == 0) return nullptr;
+  GT_DISPATCH(dtype, {
+    maxpool_bwd_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>((const T*)x, (const T*)grad, (T*)dx, *g,
+                                                                             total);
+  });
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t* idx, const void* pooled,
+                         int relu_mask, void* dx, const gt_geom* g) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_maxpool_bwd_idx"));
+  if (g->pad != 0) return errorf("gt_maxpool_bwd_idx: pooling has no padding");
+  if (g->stride < g->KH || g->stride < g->KW) return errorf("gt_maxpool_bwd_idx: windows overlap; use gt_maxpool_bwd");
+  if (relu_mask && !pooled) return errorf("gt_maxpool_bwd_idx: relu_mask needs the pooled output");
+  int64_t total = g->N * g->C * g->H * g->W;
+  if (total == 0) return nullptr;
+  GT_DISPATCH(dtype, {
+    maxpool_bwd_idx_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(
+        (const T*)grad, idx, (const T*)pooled, relu_mask, (T*)dx, *g, total);
+  });
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+// Conv2d forward: cols = im2col(x) (scratch), then C (O, N*L) = W (O, CKK) @
+// cols^T stored straight into NCHW with the bias and activation fused.
+char* gt_conv_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y, const gt_geom* g,
+                  int64_t O, int act) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_conv_fwd"));
+  if (O <= 0) return errorf("gt_conv_fwd: out_channels must be positive");
+  const int64_t L = g->OH * g->OW, NL = g->N * L, CKK = g->C * g->KH * g->KW;
+  if (NL == 0) return nullptr;
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  void* cols = nullptr;
+  GT_TRY(scratch(ctx, (size_t)(NL * CKK) * es, &cols));
+  char* err = nullptr;
+  GT_DISPATCH(dtype, {
+    err = im2col_launch<T>(ctx, (const T*)x, (T*)cols, *g);
+    if (!err) {
+      // B(k, j) = cols[j * CKK + k]
+      GemmShape s{O, NL, CKK, false, true, CKK, CKK};
+      Epi<T> e;
+      e.out = (T*)y;
+      e.bias = (const T*)bias;
+      e.bias_by_row = true;
+      e.act = act;
+      e.nchw_L = L;
+      e.nchw_M = O;
+      err = gemm<T>(ctx, s, (const T*)w, (const T*)cols, e);
+    }
+  });
+  release(ctx, cols);
+  return err;
+}
+
+// dy (N, O, L) -> dyp (O, N*L): the layout of the GEMMs below.
+static char* permute_nol(gt_ctx* ctx, int dtype, const void* dy, void* dyp, int64_t N, int64_t O, int64_t L) {
+  gt_view v{};
+  v.ndim = 3;
+  v.shape[0] = O, v.shape[1] = N, v.shape[2] = L;
+  v.strides[0] = L, v.strides[1] = O * L, v.strides[2] = 1;
+  return gt_copy(ctx, dtype, dy, &v, dyp);
+}
+
+char* gt_conv_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db, const gt_geom* g,
+                         int64_t O) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_conv_bwd_weight"));
+  if (O <= 0) return errorf("gt_conv_bwd_weight: out_channels must be positive");
+  const int64_t L = g->OH * g->OW, NL = g->N * L, CKK = g->C * g->KH * g->KW;
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  if (NL == 0) {
+    GT_CUDA(cudaMemsetAsync(dw, 0, O * CKK * es, ctx->stream));
+    if (db) GT_CUDA(cudaMemsetAsync(db, 0, O * es, ctx->stream));
+    return nullptr;
+  }
+  void *cols = nullptr, *dyp = nullptr;
+  GT_TRY(scratch(ctx, (size_t)(NL * CKK) * es, &cols));
+  char* err = scratch(ctx, (size_t)(O * NL) * es, &dyp);
+  if (!err) err = permute_nol(ctx, dtype, dy, dyp, g->N, O, L);
+  GT_DISPATCH(dtype, {
+    if (!err) err = im2col_launch<T>(ctx, (const T*)x, (T*)cols, *g);
+    if (!err) {
+      // dW (O, CKK) = dyp (O, NL) @ cols (NL, CKK)
+      GemmShape s{O, CKK, NL, false, false, NL, CKK};
+      Epi<T> e;
+      e.out = (T*)dw;
+      e.ldc = CKK;
+      err = gemm<T>(ctx, s, (const T*)dyp, (const T*)cols, e);
+    }
+  });
+  if (!err && db) err = gt_reduce(ctx, dtype, GT_SUM, dyp, db, O, NL, 1);
+  release(ctx, cols);
+  release(ctx, dyp);
+  return err;
+}
+
+char* gt_conv_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, void* dx, const gt_geom* g, int64_t O) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_conv_bwd_data"));
+  if (O <= 0) return errorf("gt_conv_bwd_data: out_channels must be positive");
+  const int64_t L = g->OH * g->OW, NL = g->N * L, CKK = g->C * g->KH * g->KW;
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  if (NL == 0) return nullptr;
+  void *dcols = nullptr, *dyp = nullptr;
+  GT_TRY(scratch(ctx, (size_t)(NL * CKK) * es, &dcols));
+  char* err = scratch(ctx, (size_t)(O * NL) * es, &dyp);
+  if (!err) err = permute_nol(ctx, dtype, dy, dyp, g->N, O, L);
+  GT_DISPATCH(dtype, {
+    if (!err) {
+      // dcols (NL, CKK) = dyp^T (NL, O) @ W (O, CKK): A(m=j, k=o) = dyp[o*NL + j]
+      GemmShape s{NL, CKK, O, true, false, NL, CKK};
+      Epi<T> e;
+      e.out = (T*)dcols;
+      e.ldc = CKK;
+      err = gemm<T>(ctx, s, (const T*)dyp, (const T*)w, e);
+    }
+    if (!err) err = col2im_launch<T>(ctx, (const T*)dcols, (T*)dx, *g);
+  });
+  release(ctx, dcols);
+  release(ctx, dyp);
+  return err;
+}
+
+}  // extern "C"

@@ -1,0 +1,123 @@
+// GEMM dispatch and the entry points built on it: Backend.MatMul
+// (internal/backend/backend.go:150) and the fused Linear forward/backward.
+#include "gemm.cuh"
+
+namespace gt {
+
+static int g_gemm_path = 0;
+static int g_gemm_taken = 0;
+void set_gemm_path(int path) { g_gemm_path = path; }
+int gemm_path() { return g_gemm_path; }
+
+template <>
+char* gemm<double>(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
+  if (g_gemm_path == 2) return errorf("gemm: the tcgen05 path has no float64 kind");
+  return gemm_simt<double>(ctx, s, A, B, epi);
+}
+
+template <>
+char* gemm<float>(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {
+  if (g_gemm_path != 1) {
+    bool done = false;
+    GT_TRY(gemm_tc_f32(ctx, s, A, B, epi, &done));
+    if (done) {
+      g_gemm_taken = 2;
+      return nullptr;
+    }
+    if (g_gemm_path == 2)
+      return errorf("gemm: shape M=%lld N=%lld K=%lld does not qualify for the tcgen05 path", (long long)s.M,
+                    (long long)s.N, (long long)s.K);
+  }
+  g_gemm_taken = 1;
+  return gemm_simt<float>(ctx, s, A, B, epi);
+}
+
+}  // namespace gt
+
+using namespace gt;
+
+extern "C" {
+
+void gt_debug_set_gemm_path(int path) { set_gemm_path(path); }
+int gt_gemm_path_taken(void) { return g_gemm_taken; }
+
+char* gt_matmul(gt_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t m, int64_t k, int64_t n,
+                int trans_a, int trans_b) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (m < 0 || k < 0 || n < 0) return errorf("gt_matmul: negative size");
+  if (m == 0 || n == 0) return nullptr;
+  if (k == 0) {  // empty inner dimension: the product is zero
+    GT_CUDA(cudaMemsetAsync(c, 0, m * n * (dtype == GT_FLOAT64 ? 8 : 4), ctx->stream));
+    return nullptr;
+  }
+  // C = op(A) @ op(B); B(k, n) = trans_b ? B[n*K + k] : B[k*N + n].
+  GemmShape s{m, n, k, trans_a != 0, trans_b != 0, trans_a ? m : k, trans_b ? k : n};
+  GT_DISPATCH(dtype, {
+    Epi<T> e;
+    e.out = (T*)c;
+    e.ldc = n;
+    return gemm<T>(ctx, s, (const T*)a, (const T*)b, e);
+  });
+  return nullptr;
+}
+
+char* gt_linear_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y, int64_t M,
+                    int64_t K, int64_t N, int act) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M < 0 || K < 0 || N < 0) return errorf("gt_linear_fwd: negative size");
+  if (M == 0 || N == 0) return nullptr;
+  // y = x (M, K) @ w (N, K)^T: B(k, n) = w[n*K + k].
+  GemmShape s{M, N, K, false, true, K, K};
+  GT_DISPATCH(dtype, {
+    Epi<T> e;
+    e.out = (T*)y;
+    e.ldc = N;
+    e.bias = (const T*)bias;
+    e.act = act;
+    if (K == 0) return errorf("gt_linear_fwd: K must be positive");
+    return gemm<T>(ctx, s, (const T*)x, (const T*)w, e);
+  });
+  return nullptr;
+}
+
+char* gt_linear_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, const void* y_prev, int act_prev,
+                         void* dx, int64_t M, int64_t K, int64_t N) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M <= 0 || K <= 0 || N <= 0) return errorf("gt_linear_bwd_data: sizes must be positive");
+  // dx (M, K) = dy (M, N) @ w (N, K): B(k=N-index, n=K-index) = w[k*K + n].
+  GemmShape s{M, K, N, false, false, N, K};
+  GT_DISPATCH(dtype, {
+    Epi<T> e;
+    e.out = (T*)dx;
+    e.ldc = K;
+    if (y_prev && act_prev != GT_ACT_NONE) {
+      e.dmask = (const T*)y_prev;
+      e.dact = act_prev;
+      e.ldm = K;
+    }
+    return gemm<T>(ctx, s, (const T*)dy, (const T*)w, e);
+  });
+  return nullptr;
+}
+
+char* gt_linear_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db, int64_t M,
+                           int64_t K, int64_t N) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M <= 0 || K <= 0 || N <= 0) return errorf("gt_linear_bwd_weight: sizes must be positive");
+  // dw (N, K) = dy (M, N)^T @ x (M, K): A(m=N-index, k=M-index) = dy[k*N + m].
+  GemmShape s{N, K, M, true, false, N, K};
+  GT_DISPATCH(dtype, {
+    Epi<T> e;
+    e.out = (T*)dw;
+    e.ldc = K;
+    GT_TRY(gemm<T>(ctx, s, (const T*)dy, (const T*)x, e));
+  });
+  if (db) GT_TRY(gt_reduce(ctx, dtype, GT_SUM, dy, db, 1, M, N));
+  return nullptr;
+}
+
+}  // extern "C"

@@ -1,0 +1,562 @@
+// tcgen05 (5th-generation tensor core) float32 GEMM with 3xTF32 split
+// emulation, for sm_100a.
+//
+// Precision. fp32 has no tensor-core kind, so each operand value x is split
+// into two tf32 values, hi = round_tf32(x) and lo = x - hi (exact in fp32):
+//   a*b ~= hi(a)*hi(b) + hi(a)*lo(b) + lo(a)*hi(b)        (lo*lo dropped)
+// Tensor-core accumulation truncates, so a long K loop into one accumulator
+// drifts; instead the MMAs accumulate a *partial* over GROUP K-slices (256
+// values of K) in tensor memory, and promoter warps fold each partial into
+// the total with correctly rounded fp32 adds. The result has fp32-class error
+// (the same order as a plain fp32 dot product).
+//
+// Work split. Two CTAs on a pair of SMs (a cluster of 2, cta_group::2)
+// compute a 256 x 256 tile of C: each CTA stages 128 rows of A and 128 rows
+// of B per K-slice and receives 128 rows x 256 columns of the accumulator in
+// its own TMEM. The CTAs are persistent and walk the tiles of C in a fixed
+// order. Roles per CTA (16 warps):
+//   warp 0      TMA producer: fp32 slices of A and B (16 elements of K) into
+//               a 6-stage shared-memory ring, K-major or M/N-major;
+//   warp 1      (leader CTA) MMA issuer: 3 x 2 tcgen05.mma per slice into the
+//               partial accumulator, commits that free the slot in both CTAs;
+//   warps 2-7   splitters, one per ring slot: warp 2+j rewrites every slice
+//               landing in slot j as tf32 hi (in place) and lo (beside it),
+//               then signals the leader's MMA, so six slices are split
+//               concurrently and each warp's fence/arrive latency is hidden;
+//   warps 8-15  promoters: total += partial after every group, and at the end
+//               of a tile the epilogue (bias, activation or activation
+//               derivative, store) straight from registers.
+// Tensor memory: columns [0,256) hold the total, [256,512) the partial.
+//
+// Every barrier wait is bounded in time; on expiry the kernel records the
+// waiting site in an error word (reported by gt_sync), stops its loops,
+// waits (bounded) for its copies and MMAs in flight, frees its tensor memory
+// and returns instead of hanging the GPU. No thread returns early, so the
+// closing cluster barrier is always reached by every thread.
+#include <cuda.h>
+
+#include "gemm.cuh"
+
+namespace gt {
+
+__device__ int g_tc_error = 0;
+
+namespace tc {
+
+constexpr int BM = 128;    // A rows per CTA (a pair covers 256)
+constexpr int BN = 256;    // C columns per tile
+constexpr int BNH = 128;   // B rows per CTA
+constexpr int BK = 16;     // K elements per slice
+constexpr int STAGES = 6;
+constexpr int GROUP = 16;  // K slices per promotion group
+constexpr int THREADS = 512;
+constexpr int SPLIT_WARP0 = 2;  // warps 2..2+STAGES-1 split; warp 2+j owns slot j
+constexpr int PROMOTERS = 256;
+constexpr uint32_t A_BYTES = BM * BK * 4;
+constexpr uint32_t B_BYTES = BNH * BK * 4;
+constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // A hi, A lo, B hi, B lo
+constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
+constexpr uint32_t SMEM_BYTES = BAR_OFFSET + 512 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t PARTIAL_COL = 256;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s; a healthy wait takes microseconds
+
+static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t num_clusters() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of a local shared-memory object in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// Arrival on the barrier at the same offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void mbar_arrive_rank(uint64_t* bar, uint32_t rank) {
+  uint32_t remote = map_to_rank(smem_u32(bar), rank);
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase of `bar` with the given parity; false (and the error
+// word set to `site`) once kTimeoutNs has passed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kTimeoutNs) {
+      atomicCAS(&g_tc_error, 0, site);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (tcgen05 "version 1").
+//   K-major operands: 64-byte rows (16 fp32 of K) with the 64-byte swizzle;
+//     8-row groups 512 B apart (SBO); one K step (8 tf32) is +32 bytes.
+//   M/N-major operands (tf32 supports only the 128-byte swizzle with 32-byte
+//     atoms there): 128-byte rows of 32 M/N elements, one per k; 32-element
+//     groups LBO = BK*128 bytes apart, 4-row groups 512 B apart (SBO); one K
+//     step (8 rows) is +1024 bytes.
+constexpr uint32_t kLayoutSw64 = 4, kLayoutSw128Atom32 = 1;
+constexpr uint32_t kLboMN = BK * 128;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for tcgen05
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
+  return MN ? smem_desc(base + kk * 1024, kLboMN, 512, kLayoutSw128Atom32)
+            : smem_desc(base + kk * 32, 16, 512, kLayoutSw64);
+}
+
+// Instruction descriptor for kind::tf32, fp32 accumulate, M = 256 (pair), N = 256.
+template <bool A_MN, bool B_MN>
+__device__ __forceinline__ uint32_t instr_desc() {
+  uint32_t d = 0;
+  d |= 1u << 4;                 // D format: F32
+  d |= 2u << 7;                 // A format: TF32
+  d |= 2u << 10;                // B format: TF32
+  d |= (A_MN ? 1u : 0u) << 15;  // A major
+  d |= (B_MN ? 1u : 0u) << 16;  // B major
+  d |= (uint32_t)(BN >> 3) << 17;
+  d |= (uint32_t)((2 * BM) >> 4) << 24;
+  return d;
+}
+
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0),
+      "r"(0)
+      : "memory");
+}
+
+// Arrives on `bar` in both CTAs of the pair once the MMAs issued so far complete.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  // Load and wait in one asm block: the registers are valid only after the wait.
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_store32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+      "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
+      "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
+      "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+}
+
+// Rounds to the nearest tf32 value (ties away from zero) on the integer ALU:
+// add half a tf32 ulp to the magnitude bits, clear the 13 dropped bits. (The
+// cvt instruction for this runs on the narrow XU pipe, which capped the
+// splitters at a third of the tensor rate.) Infinities stay infinities; a
+// NaN stays NaN or becomes an infinity whose lo part is NaN, so the product
+// is NaN either way.
+__device__ __forceinline__ float tf32_round(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// One warp splits n16 float4s of a staged slice.
+__device__ __forceinline__ void split_tf32(float4* hi, float4* lo, int n16, int lane) {
+#pragma unroll 8
+  for (int i = lane; i < n16; i += 32) {
+    float4 v = hi[i], h, l;
+    h.x = tf32_round(v.x), h.y = tf32_round(v.y), h.z = tf32_round(v.z), h.w = tf32_round(v.w);
+    l.x = __fsub_rn(v.x, h.x), l.y = __fsub_rn(v.y, h.y), l.z = __fsub_rn(v.z, h.z), l.w = __fsub_rn(v.w, h.w);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+struct Shared {
+  uint64_t full[STAGES];   // TMA -> splitters (local)
+  uint64_t split[STAGES];  // splitters of both CTAs -> leader's MMA
+  uint64_t empty[STAGES];  // MMA -> producers of both CTAs
+  uint64_t pfull;          // MMA -> promoters of both CTAs: a partial is complete
+  uint64_t pempty;         // promoters of both CTAs -> leader's MMA: the partial was read
+  uint64_t mma_done;       // leader: every MMA issued has completed
+  uint32_t tmem_base;
+  int failed;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            GemmShape s, Epi<float> epi) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  Shared* sh = (Shared*)(smem + BAR_OFFSET);
+  volatile int* failed = &sh->failed;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int num_k = (int)((s.K + BK - 1) / BK);
+  const int m_tiles = (int)((s.M + 2 * BM - 1) / (2 * BM));
+  const int n_tiles = (int)((s.N + BN - 1) / BN);
+  const int tiles = m_tiles * n_tiles;
+  const int pair = (int)cluster_id(), pairs = (int)num_clusters();
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; i++) {
+      mbar_init(&sh->full[i], 1);
+      mbar_init(&sh->split[i], 2 * 32);  // one splitter warp per CTA per slice
+      mbar_init(&sh->empty[i], 1);
+    }
+    mbar_init(&sh->pfull, 1);
+    mbar_init(&sh->pempty, 2 * PROMOTERS);
+    mbar_init(&sh->mma_done, 1);
+    sh->failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // both CTAs of the pair allocate together
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh->tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer (both CTAs)
+      int it = 0, issued_to = 0;
+      for (int t = pair; t < tiles && !*failed; t += pairs) {
+        const int mt = t / n_tiles, nt = t % n_tiles;
+        const int a_row = mt * 2 * BM + (int)rank * BM;
+        const int b_row = nt * BN + (int)rank * BNH;
+        for (int kt = 0; kt < num_k; kt++, it++) {
+          const int st = it % STAGES;
+          if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1)) {
+            *failed = 1;
+            break;
+          }
+          uint8_t* a_hi = smem + st * STAGE_BYTES;
+          uint8_t* b_hi = a_hi + 2 * A_BYTES;
+          mbar_expect_tx(&sh->full[st], A_BYTES + B_BYTES);
+          const int k0 = kt * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 32; j++) tma_load_2d(a_hi + j * kLboMN, &tmA, &sh->full[st], a_row + 32 * j, k0);
+          } else {
+            tma_load_2d(a_hi, &tmA, &sh->full[st], k0, a_row);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BNH / 32; j++)
+              tma_load_2d(b_hi + j * kLboMN, &tmB, &sh->full[st], b_row + 32 * j, k0);
+          } else {
+            tma_load_2d(b_hi, &tmB, &sh->full[st], k0, b_row);
+          }
+          issued_to = it + 1;
+        }
+      }
+      if (*failed) {  // let copies in flight land before the CTA tears down
+        for (int i = issued_to > STAGES ? issued_to - STAGES : 0; i < issued_to; i++)
+          mbar_wait(&sh->full[i % STAGES], (i / STAGES) & 1, 5);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
+      const uint32_t idesc = instr_desc<A_MN, B_MN>();
+      int it = 0, group = 0;
+      bool stop = false;
+      for (int t = pair; t < tiles && !stop; t += pairs) {
+        for (int kt = 0; kt < num_k; kt++, it++) {
+          const bool group_start = kt % GROUP == 0;
+          if (group_start) {  // the promoters must have read the previous partial
+            if (!mbar_wait(&sh->pempty, (group & 1) ^ 1, 2)) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+          }
+          const int st = it % STAGES;
+          if (!mbar_wait(&sh->split[st], (it / STAGES) & 1, 3)) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + st * STAGE_BYTES), a_lo = a_hi + A_BYTES;
+          const uint32_t b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; kk++) {
+            const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+            const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
+            mma_tf32_pair(tmem + PARTIAL_COL, dal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
+            mma_tf32_pair(tmem + PARTIAL_COL, dah, dbl, idesc, 1u);
+            mma_tf32_pair(tmem + PARTIAL_COL, dah, dbh, idesc, 1u);
+          }
+          mma_commit_pair(&sh->empty[st]);  // frees the slot in both CTAs
+          if (kt % GROUP == GROUP - 1 || kt == num_k - 1) {
+            mma_commit_pair(&sh->pfull);
+            group++;
+          }
+        }
+      }
+      if (stop) *failed = 1;
+      // Every MMA must be complete before the pair frees its tensor memory.
+      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(&sh->mma_done))
+                   : "memory");
+      mbar_wait(&sh->mma_done, 0, 6);
+    }
+  } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + STAGES) {
+    // ---- splitters (both CTAs): this warp owns ring slot st, i.e. every
+    // STAGES-th slice, starting with slice st.
+    const int st = warp - SPLIT_WARP0;
+    const int total = ((tiles - pair + pairs - 1) / pairs) * num_k;  // slices this pair streams
+    for (int it = st; it < total; it += STAGES) {
+      if (__shfl_sync(0xffffffffu, *failed, 0)) break;
+      if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4)) {
+        *failed = 1;
+        break;
+      }
+      uint8_t* stage = smem + st * STAGE_BYTES;
+      split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
+      split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + B_BYTES), B_BYTES / 16, lane);
+      fence_async_shared();  // generic-proxy writes -> visible to the tensor core
+      mbar_arrive_rank(&sh->split[st], 0);
+    }
+  } else if (warp >= 8) {
+    // ---- promoters and epilogue (both CTAs): TMEM lanes 32*(warp%4)..+31 are
+    // this warp's rows, columns [128*h, 128*h + 128) its half of the tile.
+    // Every decision below is warp-uniform: tcgen05.ld/st are .sync.aligned.
+    const int q = warp & 3, h = (warp - 8) >> 2;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    int group = 0;
+    for (int t = pair; t < tiles && !__shfl_sync(0xffffffffu, *failed, 0); t += pairs) {
+      const int mt = t / n_tiles, nt = t % n_tiles;
+      const int64_t row = (int64_t)mt * 2 * BM + rank * BM + 32 * q + lane;
+      const int groups = (num_k + GROUP - 1) / GROUP;
+      for (int g = 0; g < groups; g++, group++) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&sh->pfull, group & 1, 7))) {
+          *failed = 1;
+          break;
+        }
+        tc_fence_after();
+        const bool last = g == groups - 1;
+#pragma unroll 1
+        for (int j = 0; j < 4; j++) {
+          const uint32_t col = 128 * h + 32 * j;
+          float p[32];
+          tmem_load32(lane_base + PARTIAL_COL + col, p);
+          if (g > 0) {
+            float tot[32];
+            tmem_load32(lane_base + col, tot);
+#pragma unroll
+            for (int i = 0; i < 32; i++) p[i] = __fadd_rn(tot[i], p[i]);
+          }
+          if (!last) {
+            tmem_store32(lane_base + col, p);
+          } else if (row < s.M) {
+            const int64_t n0 = (int64_t)nt * BN + col;
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+              if (n0 + i < s.N) epi.store(row, n0 + i, p[i]);
+          }
+        }
+        if (!last) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive_rank(&sh->pempty, 0);  // the partial may be overwritten
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  cluster_sync();  // no TMEM access remains anywhere in the pair
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// 2-D fp32 tensor map over `outer` rows of `inner` contiguous elements with a
+// pitch of `ld` elements; zero fill outside. K-major operands: box 16 x 128
+// with the 64-byte swizzle; M/N-major: box 32 x 16 with the 128-byte swizzle
+// of 32-byte atoms.
+static char* make_map(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t inner, int64_t outer, int64_t ld,
+                      bool mn_major) {
+  auto encode = (EncodeTiledFn)ctx->encode_tiled;
+  if (!encode) return errorf("gemm_tc: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {mn_major ? 32u : (cuuint32_t)BK, mn_major ? (cuuint32_t)BK : (cuuint32_t)BM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return errorf("gemm_tc: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return nullptr;
+}
+
+template <bool A_MN, bool B_MN>
+static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {
+  CUtensorMap ta, tb;
+  if (A_MN)
+    GT_TRY(make_map(ctx, &ta, A, s.M, s.K, s.lda, true));
+  else
+    GT_TRY(make_map(ctx, &ta, A, s.K, s.M, s.lda, false));
+  if (B_MN)
+    GT_TRY(make_map(ctx, &tb, B, s.N, s.K, s.ldb, true));
+  else
+    GT_TRY(make_map(ctx, &tb, B, s.K, s.N, s.ldb, false));
+  auto kern = gemm_tf32x3_pair_kernel<A_MN, B_MN>;
+  static bool configured[64] = {};
+  if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
+    GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
+  }
+  const int64_t tiles = ceil_div(s.M, 2 * BM) * ceil_div(s.N, BN);
+  const int64_t pairs = tiles < ctx->sm_count / 2 ? tiles : ctx->sm_count / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = ctx->stream;
+  GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi));
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+}  // namespace tc
+
+// Reports (and clears) a timed-out pipeline wait of an earlier tcgen05 GEMM.
+char* tc_check_errors() {
+  int e = 0;
+  GT_CUDA(cudaMemcpyFromSymbol(&e, g_tc_error, sizeof e));
+  if (e) {
+    int zero = 0;
+    cudaMemcpyToSymbol(g_tc_error, &zero, sizeof zero);
+    return errorf("tcgen05 GEMM: a pipeline wait timed out (site %d); results are invalid", e);
+  }
+  return nullptr;
+}
+
+char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
+                  bool* done) {
+  *done = false;
+  // TMA needs 16-byte aligned bases and row pitches; tiny problems stay on SIMT.
+  if (((uintptr_t)A & 15) || ((uintptr_t)B & 15) || (s.lda & 3) || (s.ldb & 3)) return nullptr;
+  if (s.M < 1 || s.N < 1 || s.K < 1 || s.M > INT32_MAX / 2 || s.N > INT32_MAX / 2 || s.K > INT32_MAX / 2)
+    return nullptr;
+  if (ctx->sm_count < 2) return nullptr;
+  if (gemm_path() != 2 && s.M * s.N * s.K < (int64_t)1 << 21) return nullptr;
+  const bool a_mn = s.trans_a, b_mn = !s.trans_b;
+  char* err;
+  if (!a_mn && !b_mn)
+    err = tc::launch<false, false>(ctx, s, A, B, epi);
+  else if (!a_mn && b_mn)
+    err = tc::launch<false, true>(ctx, s, A, B, epi);
+  else if (a_mn && !b_mn)
+    err = tc::launch<true, false>(ctx, s, A, B, epi);
+  else
+    err = tc::launch<true, true>(ctx, s, A, B, epi);
+  if (!err) *done = true;
+  return err;
+}
+
+}  // namespace gt

@@ -1,0 +1,112 @@
+// Fused softmax cross-entropy, forward and backward in one pass over the
+// logits. Replaces CrossEntropyLoss = -mean(Pick(LogSoftmax(x), y))
+// (nn/loss.go:12-14, tensor/ops.go:335-359) and the ~12 primitive passes of
+// its backward, following the reference's rounding of each intermediate:
+//
+//   m_i   = max_j x_ij                     (Reduce Max)
+//   s_ij  = x_ij - m_i                     (Sub)
+//   e_ij  = T(exp(double(s_ij)))           (Exp)
+//   S_i   = sum_j e_ij                     (SumDim; tree order here)
+//   L_i   = T(log(double(S_i)))            (Log)
+//   p_i   = s_iy - L_i                     (Sub, then Pick)
+//   loss  = -(sum_i p_i * T(1/B))          (Sum, MulScalar, Neg)
+//   dx_ij = (-c * onehot_ij) + (c / S_i) * e_ij,  c = T(1/B)
+//
+// (The backward expression is what the reference's tape evaluates: the Neg /
+// MulScalar / Sum / SumDim closures seed -c at the label, the Sub closure for
+// L sums it back to c, Log divides by S and Exp multiplies by e.)
+//
+// A warp owns a row; the row's loss term goes to scratch and a second,
+// single-block kernel sums the B terms in a fixed order, so the loss is
+// deterministic. HBM traffic: read B*C logits, write B*C gradients.
+#include "gt_common.cuh"
+
+namespace gt {
+
+template <typename T>
+__global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restrict__ labels, int64_t B, int64_t C,
+                                 T c, T* __restrict__ row_terms, T* __restrict__ dx, int32_t* bad_label) {
+  const int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t i = warp; i < B; i += nwarps) {
+    const T* xr = x + i * C;
+    int32_t y = labels[i];
+    bool bad = y < 0 || y >= C;
+    if (bad && lane == 0 && bad_label) *bad_label = 1;
+    T m = (T)(-INFINITY);
+    for (int64_t j = lane; j < C; j += 32) m = go_max(m, xr[j]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = go_max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    T S = (T)0;
+    for (int64_t j = lane; j < C; j += 32) S = add_rn(S, (T)exp((double)sub_rn(xr[j], m)));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) S = add_rn(S, __shfl_xor_sync(0xffffffffu, S, off));
+    T Lse = (T)log((double)S);
+    // Pick multiplies every log-probability by the one-hot row and sums: a
+    // non-finite log-probability off the label turns into NaN (inf * 0).
+    bool nonfinite = false;
+    T picked = (T)0;
+    T q = div_rn(c, S);
+    for (int64_t j = lane; j < C; j += 32) {
+      T s = sub_rn(xr[j], m);
+      T lp = sub_rn(s, Lse);
+      if (j == y) {
+        picked = lp;
+      } else if (!isfinite(lp)) {
+        nonfinite = true;
+      }
+      if (dx) {
+        T e = (T)exp((double)s);
+        T g = mul_rn(q, e);
+        dx[i * C + j] = j == y ? add_rn(-c, g) : g;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      picked = add_rn(picked, __shfl_xor_sync(0xffffffffu, picked, off));
+      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, off) != 0;
+    }
+    if (lane == 0) row_terms[i] = (nonfinite || bad) ? (T)NAN : picked;
+  }
+}
+
+// loss = -(sum_i row_terms[i] * c), one block, fixed reduction order.
+template <typename T>
+__global__ void xent_sum_kernel(const T* __restrict__ row_terms, int64_t B, T c, T* __restrict__ loss) {
+  __shared__ T part[1024];
+  T acc = (T)0;
+  for (int64_t i = threadIdx.x; i < B; i += blockDim.x) acc = add_rn(acc, row_terms[i]);
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) part[threadIdx.x] = add_rn(part[threadIdx.x], part[threadIdx.x + s]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *loss = -mul_rn(part[0], c);
+}
+
+}  // namespace gt
+
+using namespace gt;
+
+extern "C" char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
+                                 int64_t C, void* loss, void* dlogits, int32_t* bad_label) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (B <= 0 || C <= 0) return errorf("gt_xent_fwd_bwd: B and C must be positive");
+  size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  void* terms = nullptr;
+  GT_TRY(scratch(ctx, B * es, &terms));
+  GT_DISPATCH(dtype, {
+    T c = (T)(1.0 / (double)B);  // MulScalar(1/float64(N)) rounds the scalar to T
+    xent_rows_kernel<T><<<grid_for(ctx, B * 32, 256), 256, 0, ctx->stream>>>(
+        (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
+    xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
+  });
+  count_launch(2);
+  cudaError_t e = cudaGetLastError();
+  release(ctx, terms);
+  if (e != cudaSuccess) return cuda_error(e, "xent launch", __FILE__, __LINE__);
+  return nullptr;
+}

@@ -1,0 +1,471 @@
+// Plan construction and execution of the fused training step.
+//
+// Forward, for the layer patterns of go-tensor's Sequential models:
+//   Linear [+ ReLU|Tanh|Sigmoid]        -> gt_linear_fwd (bias + act in the epilogue)
+//   Conv2d [+ ReLU]                     -> gt_conv_fwd (bias + act fused)
+//   MaxPool2d                           -> gt_maxpool_fwd_idx (value + first-max index)
+//   standalone activation               -> gt_unary
+//   Flatten, Dropout(p = 0)             -> no kernel (a view of the same buffer)
+// then gt_xent_fwd_bwd for CrossEntropyLoss.
+//
+// Backward walks the plan in reverse. A Linear's input-gradient GEMM applies
+// the derivative of the activation that produced its input in its epilogue
+// (tensor/ops.go:110-123 folded into the GEMM), and a pool whose input came
+// from a ReLU routes the gradient and applies the ReLU mask in one pass.
+// Weight gradients land in one flat buffer laid out in Parameters() order; with
+// data parallelism each bucket of it is averaged across ranks as soon as the
+// backward pass has written it, overlapping the remaining backward GEMMs.
+#include "model.hpp"
+
+#include <algorithm>
+#include <cstring>
+
+namespace gotensor {
+
+namespace {
+
+int64_t numel(const std::vector<int64_t>& s) {
+  int64_t n = 1;
+  for (auto d : s) n *= d;
+  return n;
+}
+
+int act_of(int32_t kind) {
+  switch (kind) {
+    case GTH_RELU: return GT_ACT_RELU;
+    case GTH_TANH: return GT_ACT_TANH;
+    case GTH_SIGMOID: return GT_ACT_SIGMOID;
+    default: return GT_ACT_NONE;
+  }
+}
+
+int unary_of(int act) {
+  switch (act) {
+    case GT_ACT_RELU: return GT_RELU;
+    case GT_ACT_TANH: return GT_TANH;
+    default: return GT_SIGMOID;
+  }
+}
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::string out = "[";
+  for (size_t i = 0; i < s.size(); i++) out += (i ? " " : "") + std::to_string(s[i]);
+  return out + "]";
+}
+
+constexpr int64_t kAlignElems = 64;  // every parameter tensor starts on a 256-byte boundary
+
+}  // namespace
+
+Model::Model(gt_ctx* ctx, int dtype, const std::vector<gth_layer>& layers, const std::vector<int64_t>& input_shape)
+    : ctx_(ctx), dtype_(dtype), es_(dtype == GT_FLOAT64 ? 8 : 4) {
+  if (dtype != GT_FLOAT32 && dtype != GT_FLOAT64) throw Error("gth_model_new: unknown dtype");
+  if (input_shape.empty() || input_shape[0] <= 0) throw Error("gth_model_new: input shape needs a batch dimension");
+  plan(layers, input_shape);
+}
+
+Model::~Model() { drop_graph(); }
+
+void Model::drop_graph() {
+  if (graph_) gt_graph_free(graph_);
+  graph_ = nullptr;
+}
+
+void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t>& input_shape) {
+  batch_ = input_shape[0];
+  input_ = DevBuf(ctx_, numel(input_shape) * es_);
+  labels_ = DevBuf(ctx_, batch_ * sizeof(int32_t));
+  loss_ = DevBuf(ctx_, 64);
+
+  std::vector<int64_t> shape = input_shape;
+  const void* cur = input_.get();
+  bool cur_is_act = false;  // cur holds an activation output
+  int cur_act = GT_ACT_NONE;
+  bool seen_params = false;
+  int cur_src = -1;  // op that produced `cur` (identities skipped); -1 = the batch
+  int64_t dev_off = 0, dense_off = 0, max_elems = numel(input_shape);
+
+  auto add_param = [&](int layer, const char* what, std::vector<int64_t> pshape) {
+    ParamInfo p;
+    p.name = std::to_string(layer) + "." + what;
+    p.shape = pshape;
+    p.numel = numel(pshape);
+    p.dense_offset = dense_off;
+    p.dev_offset = dev_off;
+    dense_off += p.numel;
+    dev_off += (p.numel + kAlignElems - 1) / kAlignElems * kAlignElems;
+    params_.push_back(p);
+    return p.dev_offset;
+  };
+
+  for (size_t i = 0; i < layers.size(); i++) {
+    const gth_layer& L = layers[i];
+    Op op;
+    op.layer = (int)i;
+    op.in_shape = shape;
+    op.in = cur;
+    switch (L.kind) {
+      case GTH_LINEAR: {
+        if (shape.size() != 2 || shape[1] != L.in)
+          throw Error("Linear(" + std::to_string(L.in) + ", " + std::to_string(L.out) + ") got input " +
+                      shape_str(shape) + "; flatten first");
+        op.kind = Op::LINEAR;
+        op.M = shape[0], op.K = L.in, op.N = L.out;
+        op.w_off = add_param((int)i, "weight", {L.out, L.in});
+        op.b_off = add_param((int)i, "bias", {L.out});
+        if (i + 1 < layers.size() && act_of(layers[i + 1].kind) != GT_ACT_NONE) op.act = act_of(layers[++i].kind);
+        op.out_shape = {shape[0], L.out};
+        break;
+      }
+      case GTH_CONV2D: {
+        if (shape.size() != 4 || shape[1] != L.in)
+          throw Error("Conv2d expects (N, " + std::to_string(L.in) + ", H, W), got " + shape_str(shape));
+        if (L.stride < 1 || L.padding < 0 || L.kernel < 1) throw Error("Conv2d: bad kernel/stride/padding");
+        op.kind = Op::CONV;
+        gt_geom& g = op.g;
+        g.N = shape[0], g.C = shape[1], g.H = shape[2], g.W = shape[3];
+        g.KH = g.KW = L.kernel, g.stride = L.stride, g.pad = L.padding;
+        g.OH = (g.H + 2 * g.pad - g.KH) / g.stride + 1;
+        g.OW = (g.W + 2 * g.pad - g.KW) / g.stride + 1;
+        if (g.OH <= 0 || g.OW <= 0) throw Error("Conv2d: kernel larger than padded input");
+        op.O = L.out;
+        op.w_off = add_param((int)i, "weight", {L.out, L.in, L.kernel, L.kernel});
+        op.b_off = add_param((int)i, "bias", {L.out});
+        if (i + 1 < layers.size() && layers[i + 1].kind == GTH_RELU) {
+          op.act = GT_ACT_RELU;
+          i++;
+        }
+        op.out_shape = {g.N, L.out, g.OH, g.OW};
+        break;
+      }
+      case GTH_MAXPOOL2D: {
+        if (shape.size() != 4) throw Error("MaxPool2d expects (N, C, H, W), got " + shape_str(shape));
+        op.kind = Op::POOL;
+        int64_t k = L.kernel, s = L.stride ? L.stride : L.kernel;
+        gt_geom& g = op.g;
+        g.N = shape[0], g.C = shape[1], g.H = shape[2], g.W = shape[3];
+        g.KH = g.KW = k, g.stride = s, g.pad = 0;
+        g.OH = (g.H - k) / s + 1;
+        g.OW = (g.W - k) / s + 1;
+        if (g.OH <= 0 || g.OW <= 0 || k > 16) throw Error("MaxPool2d: window larger than input (or than 16)");
+        op.relu_in = cur_is_act && cur_act == GT_ACT_RELU;
+        op.out_shape = {g.N, g.C, g.OH, g.OW};
+        break;
+      }
+      case GTH_RELU:
+      case GTH_TANH:
+      case GTH_SIGMOID:
+        op.kind = Op::ACT;
+        op.act = act_of(L.kind);
+        op.out_shape = shape;
+        break;
+      case GTH_FLATTEN:
+        op.kind = Op::IDENTITY;
+        op.out_shape = {shape[0], numel(shape) / shape[0]};
+        break;
+      case GTH_DROPOUT:
+        if (L.p != 0) throw Error("Dropout with p > 0 is not on the fused training path");
+        op.kind = Op::IDENTITY;
+        op.out_shape = shape;
+        break;
+      default:
+        throw Error("unknown layer kind " + std::to_string(L.kind));
+    }
+    if (op.kind == Op::LINEAR || op.kind == Op::CONV) {
+      op.needs_dx = seen_params;
+      seen_params = true;
+    }
+    if (op.kind == Op::IDENTITY) {
+      op.out = const_cast<void*>(cur);  // same buffer, new shape
+      op.produces_act = cur_is_act;
+      op.act = cur_act;
+    } else {
+      int64_t n = numel(op.out_shape);
+      acts_.emplace_back(ctx_, std::max<int64_t>(n, 1) * es_);
+      op.out = acts_.back().get();
+      if (op.kind == Op::POOL) {
+        acts_.emplace_back(ctx_, std::max<int64_t>(n, 1));
+        op.idx = (uint8_t*)acts_.back().get();
+        // A pool of ReLU outputs outputs ReLU outputs (max of non-negatives).
+        op.produces_act = op.relu_in;
+        if (op.relu_in) op.act = GT_ACT_RELU;
+      } else {
+        op.produces_act = op.act != GT_ACT_NONE;
+      }
+      max_elems = std::max(max_elems, n);
+    }
+    max_elems = std::max(max_elems, numel(op.in_shape));
+    op.src = cur_src;
+    if (op.kind != Op::IDENTITY) cur_src = (int)ops_.size();
+    if ((op.kind == Op::LINEAR || op.kind == Op::CONV) && first_param_op_ < 0) first_param_op_ = (int)ops_.size();
+    cur = op.out;
+    cur_is_act = op.produces_act;
+    cur_act = op.produces_act ? op.act : GT_ACT_NONE;
+    shape = op.out_shape;
+    ops_.push_back(op);
+  }
+  if (shape.size() != 2) throw Error("the model must end in (batch, classes) logits, got " + shape_str(shape));
+  if (!seen_params) throw Error("the model has no parameters");
+  classes_ = shape[1];
+  dense_params_ = dense_off;
+  dev_params_ = dev_off;
+  pbuf_ = DevBuf(ctx_, dev_params_ * es_);
+  gbuf_ = DevBuf(ctx_, dev_params_ * es_);
+  check(gt_zero(ctx_, pbuf_.get(), dev_params_ * es_));
+  check(gt_zero(ctx_, gbuf_.get(), dev_params_ * es_));
+  grad_elems_ = max_elems;
+  grad_a_ = DevBuf(ctx_, max_elems * es_);
+  grad_b_ = DevBuf(ctx_, max_elems * es_);
+  step_dev_ = DevBuf(ctx_, 64);
+  check(gt_zero(ctx_, step_dev_.get(), 64));
+}
+
+// ---- parameters -------------------------------------------------------------
+
+void Model::set_params(const void* host) {
+  drop_graph();
+  const char* h = (const char*)host;
+  for (auto& p : params_)
+    check(gt_upload(ctx_, (char*)pbuf_.get() + p.dev_offset * es_, h + p.dense_offset * es_, p.numel * es_));
+}
+
+void Model::get_params(void* host) {
+  std::vector<char> tmp(dev_params_ * es_);
+  check(gt_download(ctx_, tmp.data(), pbuf_.get(), tmp.size()));
+  for (auto& p : params_)
+    memcpy((char*)host + p.dense_offset * es_, tmp.data() + p.dev_offset * es_, p.numel * es_);
+}
+
+void Model::get_grads(void* host) {
+  std::vector<char> tmp(dev_params_ * es_);
+  check(gt_download(ctx_, tmp.data(), gbuf_.get(), tmp.size()));
+  for (auto& p : params_)
+    memcpy((char*)host + p.dense_offset * es_, tmp.data() + p.dev_offset * es_, p.numel * es_);
+}
+
+void Model::set_sgd(const gt_sgd_cfg& cfg) {
+  drop_graph();
+  opt_ = OPT_SGD;
+  sgd_ = cfg;
+  opt_steps_ = 0;
+  opt_b_.reset();
+  opt_a_ = DevBuf(ctx_, dev_params_ * es_);  // velocity
+  check(gt_zero(ctx_, opt_a_.get(), dev_params_ * es_));
+}
+
+void Model::set_adam(const gt_adam_cfg& cfg) {
+  drop_graph();
+  opt_ = OPT_ADAM;
+  adam_ = cfg;
+  opt_steps_ = 0;
+  opt_a_ = DevBuf(ctx_, dev_params_ * es_);  // m
+  opt_b_ = DevBuf(ctx_, dev_params_ * es_);  // v
+  check(gt_zero(ctx_, opt_a_.get(), dev_params_ * es_));
+  check(gt_zero(ctx_, opt_b_.get(), dev_params_ * es_));
+  check(gt_zero(ctx_, step_dev_.get(), 64));
+}
+
+// ---- step -------------------------------------------------------------------
+
+void Model::forward() {
+  char* p = (char*)pbuf_.get();
+  for (auto& op : ops_) {
+    switch (op.kind) {
+      case Op::LINEAR:
+        check(gt_linear_fwd(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, op.M, op.K, op.N,
+                            op.act));
+        break;
+      case Op::CONV:
+        check(gt_conv_fwd(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, &op.g, op.O, op.act));
+        break;
+      case Op::POOL:
+        check(gt_maxpool_fwd_idx(ctx_, dtype_, op.in, op.out, op.idx, &op.g));
+        break;
+      case Op::ACT:
+        check(gt_unary(ctx_, dtype_, unary_of(op.act), 0.0, op.in, op.out, numel(op.out_shape)));
+        break;
+      case Op::IDENTITY:
+        break;
+    }
+  }
+}
+
+void Model::issue_ready_buckets(int64_t boundary) {
+  while (next_bucket_ < buckets_.size() && buckets_[next_bucket_].first >= boundary) {
+    auto b = buckets_[next_bucket_++];
+    check(gt_allreduce_avg_async(ctx_, dtype_, (char*)gbuf_.get() + b.first * es_, b.second - b.first));
+  }
+}
+
+void Model::backward() {
+  char* p = (char*)pbuf_.get();
+  char* gr = (char*)gbuf_.get();
+  // Invariant: g is the gradient w.r.t. the output of op i; g_pre says the
+  // derivative of the activation that produced that output is already in it.
+  void* g = grad_a_.get();
+  void* spare = grad_b_.get();
+  check(gt_xent_fwd_bwd(ctx_, dtype_, ops_.back().out, labels_device(), batch_, classes_, loss_.get(), g, nullptr));
+  bool g_pre = false;
+  next_bucket_ = 0;
+  for (int i = (int)ops_.size() - 1; i >= first_param_op_; i--) {
+    Op& op = ops_[i];
+    const bool has_act = (op.kind == Op::LINEAR || op.kind == Op::CONV || op.kind == Op::ACT) && op.act != GT_ACT_NONE;
+    if (has_act && !g_pre) check(gt_act_bwd(ctx_, dtype_, op.act, g, op.out, g, numel(op.out_shape)));
+    if (op.kind != Op::IDENTITY) g_pre = false;  // g is now w.r.t. the op's pre-activation / input
+    switch (op.kind) {
+      case Op::LINEAR: {
+        check(gt_linear_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, op.M, op.K,
+                                   op.N));
+        if (world_ > 1) issue_ready_buckets(op.w_off);
+        if (op.needs_dx) {
+          // Fold the derivative of the activation that produced this input
+          // into the GEMM epilogue when the producer is a Linear/Conv/act.
+          const Op* src = op.src >= 0 ? &ops_[op.src] : nullptr;
+          bool fuse = src && src->kind != Op::POOL && src->act != GT_ACT_NONE;
+          check(gt_linear_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, fuse ? op.in : nullptr,
+                                   fuse ? src->act : GT_ACT_NONE, spare, op.M, op.K, op.N));
+          std::swap(g, spare);
+          g_pre = fuse;
+        }
+        break;
+      }
+      case Op::CONV:
+        check(gt_conv_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, &op.g, op.O));
+        if (world_ > 1) issue_ready_buckets(op.w_off);
+        if (op.needs_dx) {
+          check(gt_conv_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, spare, &op.g, op.O));
+          std::swap(g, spare);
+        }
+        break;
+      case Op::POOL:
+        if (op.g.stride >= op.g.KH && op.g.stride >= op.g.KW) {
+          // Routes g to each window's first maximum; with relu_in the ReLU
+          // mask of the producer is applied in the same pass.
+          check(gt_maxpool_bwd_idx(ctx_, dtype_, g, op.idx, op.out, op.relu_in ? 1 : 0, spare, &op.g));
+          g_pre = op.relu_in;
+        } else {
+          check(gt_maxpool_bwd(ctx_, dtype_, op.in, g, spare, &op.g));
+        }
+        std::swap(g, spare);
+        break;
+      case Op::ACT:      // derivative applied above
+      case Op::IDENTITY:  // same buffer, g_pre carried through
+        break;
+    }
+  }
+  if (world_ > 1) {
+    issue_ready_buckets(0);
+    check(gt_allreduce_avg_async(ctx_, dtype_, loss_.get(), 1));
+    check(gt_comm_wait(ctx_));
+  }
+}
+
+void Model::forward_backward() {
+  forward();
+  backward();
+}
+
+void Model::optimizer_step() {
+  if (opt_ == OPT_NONE) throw Error("no optimizer: call gth_set_sgd or gth_set_adam");
+  if (opt_ == OPT_SGD) {
+    check(gt_sgd_step(ctx_, dtype_, pbuf_.get(), gbuf_.get(), opt_a_.get(), dev_params_, &sgd_, opt_steps_ == 0));
+  } else {
+    check(gt_adam_step_dev(ctx_, dtype_, pbuf_.get(), gbuf_.get(), opt_a_.get(), opt_b_.get(), dev_params_, &adam_,
+                           (int64_t*)step_dev_.get()));
+  }
+  opt_steps_++;
+}
+
+void Model::train_step() {
+  if (opt_ == OPT_NONE) throw Error("no optimizer: call gth_set_sgd or gth_set_adam");
+  if (use_graph_ && graph_) {
+    check(gt_graph_launch(ctx_, graph_));
+    opt_steps_++;
+    return;
+  }
+  // The first SGD step initialises the velocity, so capture from the second.
+  bool capture = use_graph_ && opt_steps_ >= 1;
+  int64_t before = gt_launch_count();
+  if (capture) check(gt_capture_begin(ctx_));
+  try {
+    forward_backward();
+    optimizer_step();
+  } catch (...) {
+    if (capture) {
+      gt_graph* g = nullptr;
+      gt_free_error(gt_capture_end(ctx_, &g));
+      gt_graph_free(g);
+    }
+    throw;
+  }
+  launches_ = (int)(gt_launch_count() - before);
+  if (capture) {
+    check(gt_capture_end(ctx_, &graph_));
+    opt_steps_--;  // the captured step has not run yet
+    check(gt_graph_launch(ctx_, graph_));
+    opt_steps_++;
+  }
+}
+
+void Model::enable_graph(bool on) {
+  use_graph_ = on;
+  if (!on) drop_graph();
+}
+
+double Model::loss() {
+  double out = 0;
+  if (dtype_ == GT_FLOAT64) {
+    check(gt_download(ctx_, &out, loss_.get(), 8));
+  } else {
+    float f = 0;
+    check(gt_download(ctx_, &f, loss_.get(), 4));
+    out = f;
+  }
+  return out;
+}
+
+void Model::forward_eval(void* logits_host) {
+  forward();
+  check(gt_download(ctx_, logits_host, ops_.back().out, batch_ * classes_ * es_));
+}
+
+// ---- data parallelism -------------------------------------------------------
+
+void Model::dp_init(int rank, int world, const unsigned char id[128], int timeout_ms, int64_t bucket_bytes) {
+  drop_graph();
+  if (world > 1) check(gt_comm_init(ctx_, rank, world, id, timeout_ms));
+  rank_ = rank;
+  world_ = world;
+  std::vector<int64_t> sizes;
+  for (size_t i = 0; i < params_.size(); i++) {
+    int64_t end = i + 1 < params_.size() ? params_[i + 1].dev_offset : dev_params_;
+    sizes.push_back(end - params_[i].dev_offset);
+  }
+  std::vector<int64_t> bounds(2 * sizes.size() + 2);
+  int nb = gth_bucket_plan(sizes.data(), (int)sizes.size(), std::max<int64_t>(1, bucket_bytes / (int64_t)es_),
+                           bounds.data(), (int)sizes.size());
+  buckets_.clear();
+  for (int b = 0; b < nb; b++) buckets_.emplace_back(bounds[2 * b], bounds[2 * b + 1]);
+}
+
+}  // namespace gotensor
+
+extern "C" int gth_bucket_plan(const int64_t* sizes, int n, int64_t bucket_elems, int64_t* bounds, int cap) {
+  int count = 0;
+  int64_t total = 0;
+  for (int i = 0; i < n; i++) total += sizes[i];
+  int64_t hi = total, acc = 0, pos = total;
+  for (int i = n - 1; i >= 0; i--) {
+    pos -= sizes[i];
+    acc += sizes[i];
+    if (acc >= bucket_elems || i == 0) {
+      if (count >= cap) return -1;
+      bounds[2 * count] = pos;
+      bounds[2 * count + 1] = hi;
+      count++;
+      hi = pos;
+      acc = 0;
+    }
+  }
+  return count;
+}

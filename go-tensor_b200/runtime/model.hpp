@@ -1,0 +1,152 @@
+// Native training-step runtime for go-tensor Sequential models on B200.
+//
+// A Model turns the layer list of an nn.Sequential into a fixed plan of
+// fused kernel calls on libgotensor_cuda's C interface and owns every device
+// buffer the step touches, so a step allocates nothing and can be captured
+// into one CUDA graph.
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "gt_cuda.h"
+#include "gt_host.h"
+
+namespace gotensor {
+
+class Error : public std::runtime_error {
+ public:
+  using std::runtime_error::runtime_error;
+};
+
+// Throws the message of a failed gt_* call (and frees it).
+inline void check(char* err) {
+  if (err) {
+    std::string msg(err);
+    gt_free_error(err);
+    throw Error(msg);
+  }
+}
+
+// A device allocation from the context's pool, released on destruction.
+class DevBuf {
+ public:
+  DevBuf() = default;
+  DevBuf(gt_ctx* ctx, size_t bytes) : ctx_(ctx), bytes_(bytes) { check(gt_alloc(ctx, bytes, &ptr_)); }
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept { *this = std::move(o); }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    reset();
+    ctx_ = o.ctx_, ptr_ = o.ptr_, bytes_ = o.bytes_;
+    o.ptr_ = nullptr;
+    return *this;
+  }
+  ~DevBuf() { reset(); }
+  void reset() {
+    if (ptr_) gt_free_error(gt_release(ctx_, ptr_));
+    ptr_ = nullptr;
+  }
+  void* get() const { return ptr_; }
+  size_t bytes() const { return bytes_; }
+
+ private:
+  gt_ctx* ctx_ = nullptr;
+  void* ptr_ = nullptr;
+  size_t bytes_ = 0;
+};
+
+struct ParamInfo {
+  std::string name;
+  std::vector<int64_t> shape;
+  int64_t numel = 0;
+  int64_t dense_offset = 0;  // in the host (Parameters()-order, packed) layout
+  int64_t dev_offset = 0;    // in the device layout (each tensor 256-byte aligned)
+};
+
+struct Op {
+  enum Kind { LINEAR, CONV, POOL, ACT, IDENTITY } kind = IDENTITY;
+  int layer = -1;               // index in the Sequential of the layer owning the params
+  int act = GT_ACT_NONE;        // LINEAR/CONV: fused activation; ACT: the activation
+  bool relu_in = false;         // POOL: the input is a ReLU output (mask fused into backward)
+  std::vector<int64_t> in_shape, out_shape;
+  int64_t M = 0, K = 0, N = 0;  // LINEAR: x (M, K) @ W (N, K)^T
+  gt_geom g{};                  // CONV / POOL geometry
+  int64_t O = 0;                // CONV output channels
+  int64_t w_off = -1, b_off = -1;  // device offsets (elements) of weight and bias
+  const void* in = nullptr;     // input activation
+  void* out = nullptr;          // output activation
+  uint8_t* idx = nullptr;       // POOL: first-max window offsets
+  bool needs_dx = true;         // false for the first op with parameters
+  bool produces_act = false;    // output is an activation's output (derivative can be fused upstream)
+  int src = -1;                 // op that produced this op's input, identities skipped (-1: the batch)
+};
+
+class Model {
+ public:
+  Model(gt_ctx* ctx, int dtype, const std::vector<gth_layer>& layers, const std::vector<int64_t>& input_shape);
+  ~Model();
+
+  const std::vector<ParamInfo>& params() const { return params_; }
+  int64_t num_params() const { return dense_params_; }
+  void set_params(const void* host);
+  void get_params(void* host);
+  void get_grads(void* host);
+  void* params_device() const { return params_.empty() ? nullptr : pbuf_.get(); }
+  void* grads_device() const { return params_.empty() ? nullptr : gbuf_.get(); }
+
+  void set_sgd(const gt_sgd_cfg& cfg);
+  void set_adam(const gt_adam_cfg& cfg);
+
+  void* input_device() const { return input_.get(); }
+  int32_t* labels_device() const { return (int32_t*)labels_.get(); }
+  void* loss_device() const { return loss_.get(); }
+
+  void forward_backward();
+  void optimizer_step();
+  void train_step();
+  void enable_graph(bool on);
+  double loss();
+  void forward_eval(void* logits_host);
+  int step_launches() const { return launches_; }
+
+  void dp_init(int rank, int world, const unsigned char id[128], int timeout_ms, int64_t bucket_bytes);
+
+ private:
+  void plan(const std::vector<gth_layer>& layers, const std::vector<int64_t>& input_shape);
+  void forward();
+  void backward();
+  void issue_ready_buckets(int64_t boundary);
+  void drop_graph();
+
+  gt_ctx* ctx_;
+  int dtype_;
+  size_t es_;
+  int64_t batch_ = 0, classes_ = 0;
+  std::vector<Op> ops_;
+  int first_param_op_ = -1;  // backward stops here: nothing before it needs gradients
+  std::vector<ParamInfo> params_;
+  int64_t dense_params_ = 0, dev_params_ = 0;
+  std::vector<DevBuf> acts_;  // activation buffers owned by ops
+  DevBuf pbuf_, gbuf_, opt_a_, opt_b_, step_dev_;
+  DevBuf input_, labels_, loss_, grad_a_, grad_b_;
+  int64_t grad_elems_ = 0;
+
+  enum { OPT_NONE, OPT_SGD, OPT_ADAM } opt_ = OPT_NONE;
+  gt_sgd_cfg sgd_{};
+  gt_adam_cfg adam_{};
+  int64_t opt_steps_ = 0;
+
+  int rank_ = 0, world_ = 1;
+  std::vector<std::pair<int64_t, int64_t>> buckets_;  // device element ranges, last first
+  size_t next_bucket_ = 0;
+
+  bool use_graph_ = false;
+  gt_graph* graph_ = nullptr;
+  int launches_ = 0;
+};
+
+}  // namespace gotensor

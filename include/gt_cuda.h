@@ -1,0 +1,283 @@
+/*
+ * gt_cuda.h — C interface of libgotensor_cuda.so, the B200 (sm_100a) backend
+ * for go-tensor.
+ *
+ * This is the boundary a Go `internal/cuda` package binds over cgo to
+ * implement `backend.Backend` (internal/backend/backend.go:130-157) for
+ * `tensor.CUDA(i)`. It has the shape of the Metal backend's C interface
+ * (internal/mps/mps.h): plain pointers and sizes, op codes that equal the Go
+ * enums, and `char*` error messages (NULL on success) that the caller frees
+ * with gt_free_error. Every entry point is non-blocking unless it says
+ * otherwise: work is queued on the context's stream, and asynchronous kernel
+ * faults surface at the next gt_sync, like mps_sync.
+ *
+ * Device buffers are raw device pointers from gt_alloc. Element counts and
+ * offsets are in elements of the call's dtype unless a name ends in _bytes.
+ */
+#ifndef GT_CUDA_H
+#define GT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define GT_API __attribute__((visibility("default")))
+#else
+#define GT_API
+#endif
+
+#define GT_MAX_DIMS 8 /* backend.MaxDims, internal/backend/backend.go:109 */
+
+/* Per-device context: stream, communicator and the device's stream-ordered
+ * memory pool. One per (process, device). */
+typedef struct gt_ctx gt_ctx;
+
+/* backend.DType (internal/backend/backend.go:10-15). */
+enum { GT_FLOAT32 = 0, GT_FLOAT64 = 1 };
+
+/* backend.UnaryOp (internal/backend/backend.go:71-88). */
+enum {
+  GT_NEG = 0, GT_EXP, GT_LOG, GT_SQRT, GT_ABS, GT_RELU, GT_SIGMOID, GT_TANH,
+  GT_SIGN, GT_STEP, GT_ADD_SCALAR, GT_MUL_SCALAR, GT_POW
+};
+/* backend.BinaryOp (internal/backend/backend.go:90-98). */
+enum { GT_ADD = 0, GT_SUB, GT_MUL, GT_DIV };
+/* backend.ReduceOp (internal/backend/backend.go:100-106). */
+enum { GT_SUM = 0, GT_MAX };
+/* Activation fused into an epilogue or prologue (nn.NewReLU/NewTanh/NewSigmoid,
+ * nn/module.go:86-93). */
+enum { GT_ACT_NONE = 0, GT_ACT_RELU = 1, GT_ACT_TANH = 2, GT_ACT_SIGMOID = 3 };
+
+/* backend.View (internal/backend/backend.go:111-117): element idx (row-major
+ * over shape) is at offset + sum(idx[d]*strides[d]); stride 0 broadcasts.
+ * Same layout as mps_view (internal/mps/mps.h:8-13) widened to 64 bits. */
+typedef struct {
+  int32_t ndim;
+  int32_t _pad;
+  int64_t offset;
+  int64_t shape[GT_MAX_DIMS];
+  int64_t strides[GT_MAX_DIMS];
+} gt_view;
+
+/* backend.ConvGeom (internal/backend/backend.go:119-125); mps_geom
+ * (internal/mps/mps.h:15-18) widened to 64 bits. */
+typedef struct {
+  int64_t N, C, H, W, KH, KW, OH, OW, stride, pad;
+} gt_geom;
+
+/* ---- context and errors -------------------------------------------------- */
+
+/* Opens device `device`: stream, memory pool, kernel attributes. Replaces
+ * mps_init (internal/mps/mps.h:20-21) and the per-device factory registered
+ * through tensor/device.go:166-195. */
+GT_API char* gt_init(int device, gt_ctx** out);
+/* Frees every resource of the context (communicator, stream). */
+GT_API char* gt_destroy(gt_ctx* ctx);
+/* Frees an error message returned by any gt_* call. */
+GT_API void gt_free_error(char* msg);
+/* Device name, e.g. "NVIDIA B200"; mps_device_name (internal/mps/mps.h:22). */
+GT_API const char* gt_device_name(const gt_ctx* ctx);
+/* Device ordinal and SM count. */
+GT_API int gt_device_index(const gt_ctx* ctx);
+GT_API int gt_sm_count(const gt_ctx* ctx);
+/* The context's CUDA stream (a cudaStream_t), for interoperation. */
+GT_API void* gt_stream(gt_ctx* ctx);
+/* Waits for all queued work; returns any asynchronous fault. Backend.Sync
+ * (internal/backend/backend.go:140), mps_sync (internal/mps/mps.h:31). */
+GT_API char* gt_sync(gt_ctx* ctx);
+
+/* ---- memory: Backend.Zeros/FromHost/ToHost/Cast/Write (backend.go:134-139) */
+
+/* Stream-ordered allocation from the device's caching pool; mps_alloc
+ * (internal/mps/mps.h:25). */
+GT_API char* gt_alloc(gt_ctx* ctx, size_t bytes, void** out);
+/* Returns a buffer to the pool, ordered after the work already queued;
+ * mps_release (internal/mps/mps.h:28). */
+GT_API char* gt_release(gt_ctx* ctx, void* ptr);
+/* mps_zero (internal/mps/mps.h:27); Backend.Zeros = gt_alloc + gt_zero. */
+GT_API char* gt_zero(gt_ctx* ctx, void* dst, size_t bytes);
+/* Host -> device copy; Backend.FromHost (mps_alloc_copy, mps.h:26). The host
+ * buffer may be reused as soon as the call returns. */
+GT_API char* gt_upload(gt_ctx* ctx, void* dst, const void* src, size_t bytes);
+/* Device -> host copy after all queued work; Backend.ToHost. Blocking. */
+GT_API char* gt_download(gt_ctx* ctx, void* dst, const void* src, size_t bytes);
+/* Host <-> device copies that stay ordered on the stream without blocking,
+ * for pinned host memory (cudaHostAlloc'd by the caller). */
+GT_API char* gt_upload_async(gt_ctx* ctx, void* dst, const void* src, size_t bytes);
+GT_API char* gt_download_async(gt_ctx* ctx, void* dst, const void* src, size_t bytes);
+/* dst[dst_offset_bytes : +bytes] = src[0 : bytes]; Backend.Write
+ * (internal/backend/backend.go:139), mps_write (internal/mps/mps.h:50). */
+GT_API char* gt_write(gt_ctx* ctx, void* dst, size_t dst_offset_bytes, const void* src, size_t bytes);
+/* y = dtype-converted x, n elements; Backend.Cast (internal/cpu/cpu.go:75-90). */
+GT_API char* gt_cast(gt_ctx* ctx, const void* x, int from_dtype, void* y, int to_dtype, int64_t n);
+
+/* ---- element-wise, reductions, linear algebra, convolution helpers -------- */
+
+/* y[i] = op(x[i], s), n elements. Backend.Unary (backend.go:142); internal/cpu/
+ * cpu.go:103-167 (transcendentals evaluated in float64, then rounded to the
+ * dtype; the scalar is rounded to the dtype for AddScalar/MulScalar). */
+GT_API char* gt_unary(gt_ctx* ctx, int dtype, int op, double s, const void* x, void* y, int64_t n);
+/* out (contiguous, over va->shape) = a[va] op b[vb]. Backend.Binary
+ * (backend.go:143); internal/cpu/cpu.go:169-231. */
+GT_API char* gt_binary(gt_ctx* ctx, int dtype, int op, const void* a, const gt_view* va, const void* b,
+                const gt_view* vb, void* out);
+/* out (contiguous) = src[v]. Backend.Copy (backend.go:144); cpu.go:246-268. */
+GT_API char* gt_copy(gt_ctx* ctx, int dtype, const void* src, const gt_view* v, void* out);
+/* Reduces the middle axis of x viewed as (outer, n, inner) into (outer, inner).
+ * Backend.Reduce (backend.go:147); cpu.go:270-296. */
+GT_API char* gt_reduce(gt_ctx* ctx, int dtype, int op, const void* x, void* out, int64_t outer, int64_t n,
+                int64_t inner);
+/* c (m, n) = op(a) (m, k) @ op(b) (k, n); a is stored (k, m) when trans_a and b
+ * is stored (n, k) when trans_b. Backend.MatMul (backend.go:150);
+ * internal/cpu/linalg.go:15-62. float32 runs on tcgen05 tensor cores with
+ * 3xTF32 split emulation (fp32 accumulation), float64 on the FP64 pipe. */
+GT_API char* gt_matmul(gt_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t m, int64_t k,
+                int64_t n, int trans_a, int trans_b);
+/* Backend.Im2col/Col2im/MaxPool2d/MaxPool2dBackward (backend.go:153-156);
+ * internal/cpu/linalg.go:94-191. Col2im and the pool backward gather, in the
+ * order the reference scatters, so they are bit-exact. */
+GT_API char* gt_im2col(gt_ctx* ctx, int dtype, const void* x, void* cols, const gt_geom* g);
+GT_API char* gt_col2im(gt_ctx* ctx, int dtype, const void* cols, void* x, const gt_geom* g);
+GT_API char* gt_maxpool_fwd(gt_ctx* ctx, int dtype, const void* x, void* out, const gt_geom* g);
+GT_API char* gt_maxpool_bwd(gt_ctx* ctx, int dtype, const void* x, const void* grad, void* dx, const gt_geom* g);
+
+/* ---- fused capability entry points ---------------------------------------
+ * Each replaces a chain of Backend primitives that the Go tensor/nn/optim code
+ * issues today; the Go side reaches them through optional capability
+ * interfaces, so the public Go API does not change. */
+
+/* y (M, N) = act(x (M, K) @ w (N, K)^T + bias (N)); bias may be NULL.
+ * Replaces Linear.Forward (nn/module.go:51-53: W.T() copy, MatMul, broadcast
+ * Add) and the activation module after it (tensor/ops.go:109-125). */
+GT_API char* gt_linear_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y,
+                    int64_t M, int64_t K, int64_t N, int act);
+/* dx (M, K) = (dy (M, N) @ w (N, K)) * act'(y_prev), where y_prev (M, K) is the
+ * output of activation act_prev applied to this layer's input (NULL/NONE: no
+ * factor). Replaces the MatMul backward for the input (tensor/ops.go:321-323),
+ * the Permute backward and the previous activation's backward closure
+ * (tensor/ops.go:110, 116, 123). */
+GT_API char* gt_linear_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, const void* y_prev,
+                         int act_prev, void* dx, int64_t M, int64_t K, int64_t N);
+/* dw (N, K) = dy (M, N)^T @ x (M, K); db (N) = sum over rows of dy (NULL: skip).
+ * Replaces the MatMul backward for the weight (tensor/ops.go:324-326), the
+ * Permute backward of W.T() and sumTo for the bias (tensor/ops.go:418-433). */
+GT_API char* gt_linear_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db,
+                           int64_t M, int64_t K, int64_t N);
+/* Activation backward on its own: dx = dy * act'(y), n elements
+ * (tensor/ops.go:110, 116, 123). */
+GT_API char* gt_act_bwd(gt_ctx* ctx, int dtype, int act, const void* dy, const void* y, void* dx, int64_t n);
+/* Adds bias (C) over an (N, C, L) tensor and applies act in place. */
+GT_API char* gt_bias_act(gt_ctx* ctx, int dtype, void* y, const void* bias, int64_t N, int64_t C, int64_t L,
+                  int act);
+
+/* y (N, O, OH, OW) = act(conv2d(x (N, C, H, W), w (O, C, KH, KW)) + bias (O)).
+ * Replaces tensor.Conv2d (tensor/conv.go:40-59: Im2col, MatMul with the
+ * reshaped transposed weight, Permute, broadcast Add) plus the activation. */
+GT_API char* gt_conv_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y,
+                  const gt_geom* g, int64_t out_channels, int act);
+/* dx (N, C, H, W) = conv2d backward for the input (the Col2im of dy-patches @ W,
+ * tensor/conv.go:29-30 and the MatMul backward before it). */
+GT_API char* gt_conv_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, void* dx, const gt_geom* g,
+                       int64_t out_channels);
+/* dw (O, C, KH, KW) and db (O) (NULL: skip) of a Conv2d given x and dy. */
+GT_API char* gt_conv_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db,
+                         const gt_geom* g, int64_t out_channels);
+/* MaxPool2d forward that also records, per output, the window offset of the
+ * first maximum (uint8, kh*KW+kw) — the index the backward pass routes to
+ * (internal/cpu/linalg.go:169-183). Non-overlapping windows (stride >= KH, KW)
+ * only; KH*KW <= 256. */
+GT_API char* gt_maxpool_fwd_idx(gt_ctx* ctx, int dtype, const void* x, void* out, uint8_t* idx, const gt_geom* g);
+/* dx = scatter of grad to the recorded maxima, times relu'(pooled output) when
+ * relu_mask is set (ReLU before the pool). Writes every element of dx. */
+GT_API char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t* idx, const void* pooled,
+                         int relu_mask, void* dx, const gt_geom* g);
+
+/* Softmax cross-entropy over logits (B, C) with int32 labels on the device:
+ * loss (1 element, device) = -mean_i log softmax(x_i)[y_i] and, if dlogits is
+ * not NULL, dlogits = (softmax(x) - onehot(y)) / B. Replaces CrossEntropyLoss
+ * (nn/loss.go:12-14: LogSoftmax, host one-hot Pick, Mean, Neg) and its
+ * backward, following the reference's rounding of each intermediate.
+ * Labels outside [0, C) set *bad_label (device int32, may be NULL) to 1. */
+GT_API char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
+                      int64_t C, void* loss, void* dlogits, int32_t* bad_label);
+
+/* Optimizer hyperparameters (optim.SGDConfig / optim.AdamConfig,
+ * optim/optim.go:22-27, 74-80). */
+typedef struct {
+  double lr, momentum, weight_decay;
+} gt_sgd_cfg;
+typedef struct {
+  double lr, beta1, beta2, eps, weight_decay;
+} gt_adam_cfg;
+
+/* One SGD update over n parameters, in one pass: p, vel updated in place.
+ * first != 0 initialises the velocity (the reference's Clone on the first
+ * step). Same arithmetic and rounding as SGD.Step (optim/optim.go:48-70). */
+GT_API char* gt_sgd_step(gt_ctx* ctx, int dtype, void* p, const void* g, void* vel, int64_t n,
+                  const gt_sgd_cfg* cfg, int first);
+/* One Adam update (step >= 1) over n parameters in one pass; m and v start at
+ * zero. Same arithmetic and rounding as Adam.Step (optim/optim.go:110-132),
+ * bias corrections computed in float64 like the reference. */
+GT_API char* gt_adam_step(gt_ctx* ctx, int dtype, void* p, const void* g, void* m, void* v, int64_t n,
+                   const gt_adam_cfg* cfg, int64_t step);
+/* As gt_adam_step but the step number lives on the device (int64, read and
+ * incremented by the call's first kernel), so a captured CUDA graph can replay
+ * the update. No counterpart in the reference (graph capture). */
+GT_API char* gt_adam_step_dev(gt_ctx* ctx, int dtype, void* p, const void* g, void* m, void* v, int64_t n,
+                       const gt_adam_cfg* cfg, int64_t* step_dev);
+
+/* ---- data parallelism (no counterpart in the reference) ------------------ */
+
+/* 128-byte unique id for gt_comm_init, made on one rank and shared. */
+GT_API char* gt_comm_unique_id(unsigned char id[128]);
+/* Joins a communicator of `world` ranks, one per GPU. Fails instead of
+ * blocking forever: gives up after timeout_ms. */
+GT_API char* gt_comm_init(gt_ctx* ctx, int rank, int world, const unsigned char id[128], int timeout_ms);
+/* In-place average over ranks of n elements on the context's stream. */
+GT_API char* gt_allreduce_avg(gt_ctx* ctx, int dtype, void* buf, int64_t n);
+/* Leaves the communicator (abort when a rank failed, else destroy). */
+GT_API char* gt_comm_destroy(gt_ctx* ctx, int abort);
+/* Overlapped variant: the average runs on the context's communication stream,
+ * after the work queued so far on the compute stream, so later compute
+ * (the rest of the backward pass) overlaps it. */
+GT_API char* gt_allreduce_avg_async(gt_ctx* ctx, int dtype, void* buf, int64_t n);
+/* Makes later compute-stream work wait for every average queued so far. */
+GT_API char* gt_comm_wait(gt_ctx* ctx);
+
+/* ---- CUDA graphs (no counterpart in the reference) ------------------------
+ * Records the work queued on the context's stream between begin and end into
+ * a graph that replays it with one launch (the training step's ~40 kernels).
+ * Nothing may synchronize the stream while it records. */
+typedef struct gt_graph gt_graph;
+GT_API char* gt_capture_begin(gt_ctx* ctx);
+GT_API char* gt_capture_end(gt_ctx* ctx, gt_graph** out);
+GT_API char* gt_graph_launch(gt_ctx* ctx, gt_graph* graph);
+GT_API void gt_graph_free(gt_graph* graph);
+
+/* ---- timing --------------------------------------------------------------- */
+/* Device time in milliseconds between two points of the context's stream:
+ * gt_mark records a point (slot 0..7), gt_elapsed_ms synchronizes on `to` and
+ * returns the interval. */
+GT_API char* gt_mark(gt_ctx* ctx, int slot);
+GT_API char* gt_elapsed_ms(gt_ctx* ctx, int from, int to, float* ms);
+
+/* Number of kernels this library has launched (or recorded into a graph) in
+ * the process so far. */
+GT_API int64_t gt_launch_count(void);
+
+/* ---- testing -------------------------------------------------------------- */
+/* Pins the float32 GEMM path: 0 automatic, 1 SIMT only, 2 tcgen05 only (shapes
+ * that do not qualify then fail). Process-wide; for tests and benchmarks. */
+GT_API void gt_debug_set_gemm_path(int path);
+/* The path the most recent float32 GEMM took: 1 SIMT, 2 tcgen05 (0: none yet). */
+GT_API int gt_gemm_path_taken(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GT_CUDA_H */

@@ -1,0 +1,116 @@
+/*
+ * gt_host.h — C interface of libgotensor_host.so, the native training-step
+ * runtime above libgotensor_cuda.so.
+ *
+ * It runs go-tensor's training loop for a Sequential model,
+ *
+ *   loss := nn.CrossEntropyLoss(model.Forward(x), y)
+ *   opt.ZeroGrad(); loss.Backward(); opt.Step()
+ *
+ * (examples/mnist/main.go:68-73, nn/nn_mps_test.go:31-36), as a fixed plan of
+ * fused kernels instead of a tape of primitives: Linear (+activation) and
+ * Conv2d (+ReLU) + MaxPool2d forward in GEMM epilogues, one fused softmax
+ * cross-entropy, backward GEMMs with the activation derivative in their
+ * epilogue, one optimizer pass over the flat parameter buffer, and (with more
+ * than one rank) a bucketed gradient average overlapped with the backward
+ * pass. Parameters are laid out flat in Module.Parameters() order
+ * (nn/module.go:72-78) and named like nn.NamedParameters ("0.weight",
+ * nn/state.go:28-55).
+ */
+#ifndef GT_HOST_H
+#define GT_HOST_H
+
+#include "gt_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct gth_model gth_model;
+
+/* Layer kinds: nn.NewLinear, nn.NewConv2d, nn.NewMaxPool2d, nn.NewReLU,
+ * nn.NewTanh, nn.NewSigmoid, nn.NewFlatten, nn.NewDropout. */
+enum {
+  GTH_LINEAR = 0, GTH_CONV2D, GTH_MAXPOOL2D, GTH_RELU, GTH_TANH, GTH_SIGMOID, GTH_FLATTEN, GTH_DROPOUT
+};
+
+/* One layer. Linear: in, out. Conv2d: in, out, kernel, stride, padding
+ * (nn/conv.go:19-28). MaxPool2d: kernel, stride (0 = kernel, nn/conv.go:41-48).
+ * Dropout: p (only p = 0, the identity, is supported on this path). */
+typedef struct {
+  int32_t kind;
+  int32_t _pad;
+  int64_t in, out, kernel, stride, padding;
+  double p;
+} gth_layer;
+
+/* Builds the plan for a fixed input shape (batch first) and allocates
+ * parameters, gradients and activations on ctx's device. Parameters start
+ * at zero: load them with gth_set_params. */
+GT_API char* gth_model_new(gt_ctx* ctx, int dtype, const gth_layer* layers, int nlayers, const int64_t* input_shape,
+                           int ndim, gth_model** out);
+GT_API void gth_model_free(gth_model* m);
+
+/* Parameter tensors in Parameters() order. */
+GT_API int gth_num_tensors(const gth_model* m);
+GT_API int64_t gth_num_params(const gth_model* m);
+/* name (NUL-terminated, truncated to name_cap), shape (up to 4 dims), ndim,
+ * offset in elements within the flat buffer. */
+GT_API char* gth_param_info(const gth_model* m, int i, char* name, int name_cap, int64_t* shape, int* ndim,
+                            int64_t* offset);
+/* Flat copies of all parameters / gradients, host side, in the model dtype. */
+GT_API char* gth_set_params(gth_model* m, const void* host);
+GT_API char* gth_get_params(gth_model* m, void* host);
+GT_API char* gth_get_grads(gth_model* m, void* host);
+/* Device pointers of the flat buffers (for bulk device-side access). */
+GT_API void* gth_params_device(gth_model* m);
+GT_API void* gth_grads_device(gth_model* m);
+
+/* Optimizer: optim.NewSGD / optim.NewAdam (optim/optim.go:22-106). Resets the
+ * optimizer state. */
+GT_API char* gth_set_sgd(gth_model* m, const gt_sgd_cfg* cfg);
+GT_API char* gth_set_adam(gth_model* m, const gt_adam_cfg* cfg);
+
+/* Device buffers the step reads: the input batch (input_shape, model dtype)
+ * and the labels (batch int32). */
+GT_API void* gth_input_device(gth_model* m);
+GT_API int32_t* gth_labels_device(gth_model* m);
+/* Device scalar (model dtype) holding the last loss. */
+GT_API void* gth_loss_device(gth_model* m);
+
+/* Loss and gradients for the batch in the input buffers (gradients are
+ * overwritten, i.e. ZeroGrad + Backward), averaged over ranks when data
+ * parallel. Asynchronous. */
+GT_API char* gth_forward_backward(gth_model* m);
+/* One optimizer update from the current gradients. Asynchronous. */
+GT_API char* gth_optimizer_step(gth_model* m);
+/* forward_backward + optimizer_step. With graphs enabled, the step is
+ * captured once (after its first eager run) and replayed. Asynchronous. */
+GT_API char* gth_train_step(gth_model* m);
+GT_API char* gth_enable_graph(gth_model* m, int on);
+/* Reads the last loss (synchronizes). */
+GT_API char* gth_loss(gth_model* m, double* out);
+/* Evaluation forward pass (no gradients): logits (batch, classes) to host. */
+GT_API char* gth_forward(gth_model* m, void* logits_host);
+/* Number of GPU kernel launches one training step issues (the plan's size). */
+GT_API int gth_step_launches(const gth_model* m);
+
+/* Data parallelism: joins a communicator of `world` ranks (one GPU each) and
+ * splits the gradient buffer into buckets of about bucket_bytes, averaged as
+ * soon as the backward pass has finished them. */
+GT_API char* gth_dp_init(gth_model* m, int rank, int world, const unsigned char id[128], int timeout_ms,
+                         int64_t bucket_bytes);
+
+/* The bucket plan for parameter tensors of the given sizes (elements, in
+ * Parameters() order): buckets are contiguous element ranges of the flat
+ * buffer filled from its end (the order in which backward produces
+ * gradients), closing once they hold at least bucket_elems elements and only
+ * at tensor boundaries. Writes (lo, hi) pairs, last bucket of the buffer
+ * first; returns the bucket count, or -1 if cap is too small. Host only. */
+GT_API int gth_bucket_plan(const int64_t* sizes, int n, int64_t bucket_elems, int64_t* bounds, int cap);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GT_HOST_H */

@@ -55,7 +55,7 @@ class Device:
         self.type, self.index = type_, index
 
     def __eq__(self, o):
-        return isinstance(o, Device) and (self.type, self.index) == (o.type, o.index)
+        return (getattr(o, "type", None), getattr(o, "index", None)) == (self.type, self.index)
 
     def __hash__(self):
         return hash((self.type, self.index))

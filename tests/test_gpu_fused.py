@@ -1,0 +1,251 @@
+"""The fused entry points of gt_cuda.h against the chains of reference ops
+they replace, computed by the oracle on identical inputs."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from gotensor import _lib
+from gotensor._lib import AdamCfg, SgdCfg, check
+from gpu_common import assert_bits, assert_close, cuda_backend
+from oracle import gotensor_ref as T
+
+pytestmark = pytest.mark.gpu
+
+ACTS = {0: None, 1: "ReLU", 2: "Tanh", 3: "Sigmoid"}
+DT = [(T.Float32, np.float32, 1e-4), (T.Float64, np.float64, 1e-10)]
+
+
+def lib():
+    return cuda_backend().lib
+
+
+def ctx():
+    return cuda_backend().ctx.ptr
+
+
+_keep = []  # device storages must outlive the asynchronous calls that use them
+
+
+@pytest.fixture(autouse=True)
+def _keep_alive():
+    yield
+    cuda_backend().Sync()
+    _keep.clear()
+
+
+def dev(a):
+    s = cuda_backend().FromHost(np.ascontiguousarray(a))
+    _keep.append(s)
+    return s
+
+
+def host(s):
+    return cuda_backend().ToHost(s)
+
+
+def new(n, dt):
+    s = cuda_backend().Zeros(dt, n)
+    _keep.append(s)
+    return s
+
+
+def ref(a, *shape):
+    return T.FromFloat64(np.asarray(a, dtype=np.float64).reshape(-1), *shape).ToDType(
+        T.Float32 if np.asarray(a).dtype == np.float32 else T.Float64)
+
+
+def apply_act(t, act):
+    return t if act == 0 else getattr(t, ACTS[act])()
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+@pytest.mark.parametrize("mkn", [(64, 784, 128), (257, 129, 65), (1024, 512, 1000), (5, 3, 7)])
+def test_linear_fwd(dt, npdt, tol, act, mkn):
+    M, K, N = mkn
+    rng = np.random.default_rng(M + K + N)
+    x = rng.standard_normal((M, K)).astype(npdt)
+    w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(npdt)
+    b = rng.standard_normal(N).astype(npdt)
+    y = new(M * N, dt)
+    check(lib().gt_linear_fwd(ctx(), dt, dev(x).ptr, dev(w).ptr, dev(b).ptr, y.ptr, M, K, N, act))
+    with T.no_grad():
+        want = apply_act(ref(x, M, K).MatMul(ref(w, N, K).T()).Add(ref(b, N)), act).Float64s()
+    assert_close(host(y), want, tol, f"linear fwd act={act}")
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("act_prev", [0, 1, 2, 3])
+@pytest.mark.parametrize("mkn", [(64, 784, 128), (257, 129, 65), (512, 1024, 1000)])
+def test_linear_bwd(dt, npdt, tol, act_prev, mkn):
+    M, K, N = mkn
+    rng = np.random.default_rng(M * 3 + K + N)
+    x = rng.standard_normal((M, K)).astype(npdt)
+    yprev = apply_act(ref(x, M, K), act_prev).Float64s().astype(npdt).reshape(M, K)  # an activation output
+    w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(npdt)
+    # gradients of a mean loss scale like 1/batch
+    dy = (rng.standard_normal((M, N)) / np.sqrt(M)).astype(npdt)
+    dx, dw, db = new(M * K, dt), new(N * K, dt), new(N, dt)
+    check(lib().gt_linear_bwd_data(ctx(), dt, dev(dy).ptr, dev(w).ptr, dev(yprev).ptr, act_prev, dx.ptr, M, K, N))
+    check(lib().gt_linear_bwd_weight(ctx(), dt, dev(yprev).ptr, dev(dy).ptr, dw.ptr, db.ptr, M, K, N))
+    with T.no_grad():
+        g = ref(dy, M, N).MatMul(ref(w, N, K))  # dX = dY @ W (tensor/ops.go:321-323)
+        y = ref(yprev, M, K)
+        if act_prev == 1:
+            g = g.Mul(y._raw(T.STEP, 0.0))
+        elif act_prev == 2:
+            g = g.Mul(y.Mul(y).Neg().AddScalar(1))
+        elif act_prev == 3:
+            g = g.Mul(y.Mul(y.Neg().AddScalar(1)))
+        want_dx = g.Float64s()
+        want_dw = ref(yprev, M, K).T().MatMul(ref(dy, M, N)).T().Float64s()  # Permute backward of W.T()
+        want_db = ref(dy, M, N).SumDim(0, False).Float64s()
+    assert_close(host(dx), want_dx, tol, "dx")
+    assert_close(host(dw), want_dw, tol, "dw")
+    assert_close(host(db), want_db, tol, "db")
+
+
+CONVS = [(2, 3, 5, 5, 4, 3, 1, 0), (2, 2, 5, 4, 3, 3, 2, 1), (8, 1, 28, 28, 32, 3, 1, 1), (4, 32, 14, 14, 64, 3, 1, 1),
+         (2, 3, 32, 32, 64, 3, 1, 1)]
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("cs", CONVS)
+def test_conv_fwd_bwd(dt, npdt, tol, cs):
+    N, C, H, W, O, k, s, p = cs
+    rng = np.random.default_rng(sum(cs))
+    x = rng.standard_normal((N, C, H, W)).astype(npdt)
+    w = (rng.standard_normal((O, C, k, k)) / np.sqrt(C * k * k)).astype(npdt)
+    b = rng.standard_normal(O).astype(npdt)
+    g = T.conv_geom("Conv2d", [N, C, H, W], k, k, s, p)
+    gg = _lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_])
+    L = g.OH * g.OW
+    for act in (0, 1):
+        y = new(N * O * L, dt)
+        check(lib().gt_conv_fwd(ctx(), dt, dev(x).ptr, dev(w).ptr, dev(b).ptr, y.ptr, ctypes.byref(gg), O, act))
+        with T.no_grad():
+            want = apply_act(T.Conv2d(ref(x, N, C, H, W), ref(w, O, C, k, k), ref(b, O), s, p), act).Float64s()
+        assert_close(host(y), want, tol, f"conv fwd act={act}")
+    dy = rng.standard_normal((N, O, g.OH, g.OW)).astype(npdt)
+    dx, dw, db = new(N * C * H * W, dt), new(O * C * k * k, dt), new(O, dt)
+    check(lib().gt_conv_bwd_data(ctx(), dt, dev(dy).ptr, dev(w).ptr, dx.ptr, ctypes.byref(gg), O))
+    check(lib().gt_conv_bwd_weight(ctx(), dt, dev(x).ptr, dev(dy).ptr, dw.ptr, db.ptr, ctypes.byref(gg), O))
+    xs, ws, bs = ref(x, N, C, H, W).SetRequiresGrad(True), ref(w, O, C, k, k).SetRequiresGrad(True), \
+        ref(b, O).SetRequiresGrad(True)
+    T.Conv2d(xs, ws, bs, s, p).Backward(ref(dy, N, O, g.OH, g.OW))
+    assert_close(host(dx), xs.Grad().Float64s(), tol, "conv dx")
+    assert_close(host(dw), ws.Grad().Float64s(), tol, "conv dw")
+    assert_close(host(db), bs.Grad().Float64s(), tol, "conv db")
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("ps", [(2, 3, 4, 6, 2), (8, 32, 28, 28, 2), (4, 64, 7, 7, 2), (2, 2, 9, 9, 3)])
+def test_pool_idx_with_relu_mask_bit_exact(dt, npdt, tol, ps):
+    N, C, H, W, k = ps
+    g = T.conv_geom("MaxPool2d", [N, C, H, W], k, k, k, 0)
+    gg = _lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_])
+    rng = np.random.default_rng(H + C)
+    z = rng.integers(-3, 4, (N, C, H, W)).astype(npdt)  # ties and non-positive windows
+    relu = np.maximum(z, 0).astype(npdt)
+    out, idx = new(N * C * g.OH * g.OW, dt), new(N * C * g.OH * g.OW, T.Float32)
+    check(lib().gt_maxpool_fwd_idx(ctx(), dt, dev(relu).ptr, out.ptr, idx.ptr, ctypes.byref(gg)))
+    grad = rng.standard_normal(N * C * g.OH * g.OW).astype(npdt)
+    dz = new(N * C * H * W, dt)
+    check(lib().gt_maxpool_bwd_idx(ctx(), dt, dev(grad).ptr, idx.ptr, out.ptr, 1, dz.ptr, ctypes.byref(gg)))
+    # reference: ReLU -> MaxPool2d, backward through both
+    zt = ref(z, N, C, H, W).SetRequiresGrad(True)
+    y = T.MaxPool2d(zt.ReLU(), k, k)
+    assert_bits(host(out), y.Float64s().astype(npdt), "pool fwd")
+    y.Backward(ref(grad, N, C, g.OH, g.OW))
+    assert_bits(host(dz), zt.Grad().Float64s().astype(npdt), "pool+relu bwd")
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("bc", [(64, 10), (8192, 1000), (3, 4), (256, 10), (1, 1)])
+def test_xent_fwd_bwd(dt, npdt, tol, bc):
+    B, C = bc
+    rng = np.random.default_rng(B + C)
+    x = (rng.standard_normal((B, C)) * 3).astype(npdt)
+    y = rng.integers(0, C, B).astype(np.int32)
+    loss, dl = new(1, dt), new(B * C, dt)
+    bad = new(1, T.Float32)
+    check(lib().gt_zero(ctx(), bad.ptr, 4))
+    labels = cuda_backend().ctx.alloc(4 * B)
+    check(lib().gt_upload(ctx(), labels, y.ctypes.data, 4 * B))
+    check(lib().gt_xent_fwd_bwd(ctx(), dt, dev(x).ptr, labels, B, C, loss.ptr, dl.ptr, bad.ptr))
+    xt = ref(x, B, C).SetRequiresGrad(True)
+    lt = xt.LogSoftmax().Pick(list(y)).Mean().Neg()  # CrossEntropyLoss, nn/loss.go:12-14
+    lt.Backward()
+    assert_close(host(loss), lt.Float64s(), tol, "loss")
+    assert_close(host(dl), xt.Grad().Float64s(), tol, "dlogits")
+    assert host(bad).view(np.int32)[0] == 0
+    cuda_backend().ctx.release(labels)
+
+
+def _opt_params(npdt, n, rng):
+    p = rng.standard_normal(n).astype(npdt)
+    gs = [rng.standard_normal(n).astype(npdt) * s for s in (1.0, 1e-3, 10.0)]
+    gs[0][:5] = [0.0, -0.0, 1e-30, -1e-30, 1e30]
+    return p, gs
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("wd", [0.0, 1e-4])
+def test_adam_bit_exact(dt, npdt, tol, wd):
+    """Adam.Step (optim/optim.go:110-132) given identical gradients: bit-identical."""
+    from oracle import optim_ref as optim
+    n = 1001
+    rng = np.random.default_rng(11)
+    p, gs = _opt_params(npdt, n, rng)
+    pt = ref(p, n).SetRequiresGrad(True)
+    opt = optim.NewAdam([pt], optim.AdamConfig(LR=1e-3, WeightDecay=wd))
+    pd, m, v = dev(p), new(n, dt), new(n, dt)
+    cfg = AdamCfg(1e-3, 0, 0, 0, wd)
+    for step, g in enumerate(gs, 1):
+        pt.grad = ref(g, n)
+        opt.Step()
+        check(lib().gt_adam_step(ctx(), dt, pd.ptr, dev(g).ptr, m.ptr, v.ptr, n, ctypes.byref(cfg), step))
+        assert_bits(host(pd), pt.Float64s().astype(npdt), f"adam step {step}")
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("mom,wd", [(0.9, 1e-4), (0.0, 0.0), (0.9, 0.0), (0.0, 1e-4)])
+def test_sgd_bit_exact(dt, npdt, tol, mom, wd):
+    """SGD.Step (optim/optim.go:48-70) given identical gradients: bit-identical."""
+    from oracle import optim_ref as optim
+    n = 1003
+    rng = np.random.default_rng(12)
+    p, gs = _opt_params(npdt, n, rng)
+    pt = ref(p, n).SetRequiresGrad(True)
+    opt = optim.NewSGD([pt], optim.SGDConfig(LR=0.01, Momentum=mom, WeightDecay=wd))
+    pd, vel = dev(p), new(n, dt)
+    cfg = SgdCfg(0.01, mom, wd)
+    for step, g in enumerate(gs):
+        pt.grad = ref(g, n)
+        opt.Step()
+        check(lib().gt_sgd_step(ctx(), dt, pd.ptr, dev(g).ptr, vel.ptr, n, ctypes.byref(cfg), int(step == 0)))
+        assert_bits(host(pd), pt.Float64s().astype(npdt), f"sgd step {step}")
+
+
+def test_adam_device_step_counter():
+    """gt_adam_step_dev reads and advances the device step: same as host steps."""
+    n = 4097
+    rng = np.random.default_rng(13)
+    p, gs = _opt_params(np.float32, n, rng)
+    a, b = dev(p), dev(p)
+    ma, va, mb, vb = (new(n, T.Float32) for _ in range(4))
+    step = cuda_backend().ctx.alloc(8)
+    check(lib().gt_zero(ctx(), step, 8))
+    cfg = AdamCfg(1e-3, 0.9, 0.999, 1e-8, 0)
+    for s, g in enumerate(gs, 1):
+        gd = dev(g)
+        check(lib().gt_adam_step(ctx(), T.Float32, a.ptr, gd.ptr, ma.ptr, va.ptr, n, ctypes.byref(cfg), s))
+        check(lib().gt_adam_step_dev(ctx(), T.Float32, b.ptr, gd.ptr, mb.ptr, vb.ptr, n, ctypes.byref(cfg), step))
+    # bias corrections from the device's pow may differ from the host's in the
+    # last float64 bit; after rounding to float32 that is at most one ulp
+    assert_close(host(b), host(a), 1e-6, "device-step adam")
+    cnt = np.zeros(1, dtype=np.int64)
+    check(lib().gt_download(ctx(), cnt.ctypes.data, step, 8))
+    assert cnt[0] == 3
+    cuda_backend().ctx.release(step)

@@ -1,0 +1,80 @@
+"""The tcgen05 3xTF32 GEMM (forced path) against the oracle's fp32 matmul and,
+at sizes the CPU oracle cannot finish quickly, against float64 host products
+with an fp32-class error bound."""
+import numpy as np
+import pytest
+
+from gotensor import _lib
+from gpu_common import assert_close, cpu_backend, cuda_backend
+from oracle import gotensor_ref as T
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _force_tc():
+    lib = _lib.cuda_lib()
+    lib.gt_debug_set_gemm_path(2)
+    yield
+    lib.gt_debug_set_gemm_path(0)
+
+
+def run(m, k, n, ta, tb, rng, weight_like=True):
+    # activations ~N(0,1); the other operand scaled like a Linear weight,
+    # U(+-1/sqrt(k)) (nn/module.go:43-49), so outputs are O(1) as in training
+    a = rng.standard_normal(m * k).astype(np.float32)
+    if weight_like:
+        b = rng.uniform(-1, 1, k * n).astype(np.float32) / np.float32(np.sqrt(k))
+    else:
+        b = rng.standard_normal(k * n).astype(np.float32)
+    be = cuda_backend()
+    ga, gb = be.FromHost(a), be.FromHost(b)
+    got = be.ToHost(be.MatMul(ga, gb, m, k, n, ta, tb))
+    assert _lib.cuda_lib().gt_gemm_path_taken() == 2
+    return a, b, got
+
+
+@pytest.mark.parametrize("mkn", [(128, 32, 128), (128, 8, 128), (1, 4, 1), (130, 36, 132), (256, 1000, 384),
+                                 (64, 784, 128), (300, 1028, 10), (517, 96, 260)])
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+def test_tc_matches_oracle(mkn, ta, tb):
+    m, k, n = mkn
+    # TMA needs every row pitch to be a multiple of 16 bytes
+    if (ta and m % 4) or (not ta and k % 4) or (tb and k % 4) or (not tb and n % 4):
+        pytest.skip("row pitch not a multiple of 16 bytes (the dispatcher uses SIMT there)")
+    rng = np.random.default_rng(m * 7 + k * 3 + n)
+    a, b, got = run(m, k, n, ta, tb, rng)
+    want = cpu_backend().MatMul(T.CPUStorage(a), T.CPUStorage(b), m, k, n, ta, tb).data
+    assert_close(got, want, 1e-4, f"tc {mkn} ta={ta} tb={tb}")
+
+
+@pytest.mark.parametrize("mkn", [(4096, 4096, 1024), (1024, 8192, 4096), (8192, 1000, 512), (256, 1000, 384)])
+@pytest.mark.parametrize("ta,tb", [(False, True), (False, False), (True, False)])
+def test_tc_large_against_float64(mkn, ta, tb):
+    """The three operand layouts of a Linear layer's forward, dX and dW GEMMs at
+    wide-MLP sizes, on unscaled N(0,1) operands (outputs ~sqrt(k) with heavy
+    cancellation): the error vs the exact (float64) product, relative to
+    sum |a||b|, stays at fp32 level, no worse than a plain fp32 dot product."""
+    m, k, n = mkn
+    rng = np.random.default_rng(m + k + n)
+    a, b, got = run(m, k, n, ta, tb, rng, weight_like=False)
+    A = a.reshape(k, m).T if ta else a.reshape(m, k)
+    B = b.reshape(n, k).T if tb else b.reshape(k, n)
+    exact = A.astype(np.float64) @ B.astype(np.float64)
+    scale = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64)
+    err = np.abs(got.reshape(m, n) - exact) / scale
+    # fp32 reference: the same product with fp32 accumulation (numpy/BLAS sgemm)
+    err32 = np.abs((A @ B).astype(np.float64) - exact) / scale
+    assert err.max() <= max(4 * err32.max(), 2.0 ** -20), (err.max(), err32.max())
+
+
+def test_tc_special_values_and_accuracy_beyond_tf32():
+    """Values that tf32 alone cannot represent: 3xTF32 must recover them."""
+    m = k = n = 128
+    a = np.full(m * k, 1.0 + 2.0 ** -20, dtype=np.float32)
+    b = np.full(k * n, 1.0 - 2.0 ** -21, dtype=np.float32)
+    be = cuda_backend()
+    got = be.ToHost(be.MatMul(be.FromHost(a), be.FromHost(b), m, k, n, False, False))
+    exact = k * (1.0 + 2.0 ** -20) * (1.0 - 2.0 ** -21)
+    assert np.abs(got - exact).max() <= 2 * np.spacing(np.float32(exact)), (got[0], exact)
