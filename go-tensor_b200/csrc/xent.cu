@@ -88,7 +88,58 @@ __global__ void xent_sum_kernel(const T* __restrict__ row_terms, int64_t B, T c,
 
 }  // namespace gt
 
+// Row terms of gt_xent_fwd_bwd_noalloc: a buffer compiled into the library
+// (one per device), so that variant never asks the pool for memory. Each call
+// writes every row term it later reads, so leftovers from an earlier call,
+// larger or smaller, never leak into a result and nothing needs clearing.
+static __device__ __align__(256) unsigned char g_xent_rows[GT_XENT_NOALLOC_MAX_ROWS * sizeof(double)];
+
+namespace gt {
+
+// Device address of g_xent_rows per device. Host code cannot pass the
+// symbol itself to a kernel (on the host it names a host-side stand-in), so
+// the address is looked up once per device, with that device current.
+static void* g_xent_rows_addr[64];
+static std::mutex g_xent_rows_mu;
+
+static char* xent_rows_buffer(gt_ctx* ctx, void** out) {
+  if (ctx->device < 0 || ctx->device >= 64) return errorf("gt_xent_fwd_bwd_noalloc: device %d out of range", ctx->device);
+  std::lock_guard<std::mutex> lock(g_xent_rows_mu);
+  if (!g_xent_rows_addr[ctx->device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_xent_rows);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(g_xent_rows)", __FILE__, __LINE__);
+    g_xent_rows_addr[ctx->device] = p;
+  }
+  *out = g_xent_rows_addr[ctx->device];
+  return nullptr;
+}
+
+}  // namespace gt
+
 using namespace gt;
+
+extern "C" char* gt_xent_fwd_bwd_noalloc(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
+                                         int64_t C, void* loss, void* dlogits, int32_t* bad_label) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (B <= 0 || C <= 0) return errorf("gt_xent_fwd_bwd_noalloc: B and C must be positive");
+  if (B > GT_XENT_NOALLOC_MAX_ROWS)
+    return errorf("gt_xent_fwd_bwd_noalloc: batch of %lld rows exceeds the %d-row buffer; use gt_xent_fwd_bwd",
+                  (long long)B, GT_XENT_NOALLOC_MAX_ROWS);
+  void* terms = nullptr;
+  GT_TRY(xent_rows_buffer(ctx, &terms));
+  GT_DISPATCH(dtype, {
+    T c = (T)(1.0 / (double)B);
+    xent_rows_kernel<T><<<grid_for(ctx, B * 32, 256), 256, 0, ctx->stream>>>(
+        (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
+    xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
+  });
+  count_launch(2);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "xent launch", __FILE__, __LINE__);
+  return nullptr;
+}
 
 extern "C" char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
                                  int64_t C, void* loss, void* dlogits, int32_t* bad_label) {

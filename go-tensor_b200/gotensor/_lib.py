@@ -92,6 +92,7 @@ CUDA_API = {
     "gt_maxpool_fwd_idx": ("err", [_P, _INT, _P, _P, _P, ctypes.POINTER(GtGeom)]),
     "gt_maxpool_bwd_idx": ("err", [_P, _INT, _P, _P, _P, _INT, _P, ctypes.POINTER(GtGeom)]),
     "gt_xent_fwd_bwd": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P]),
+    "gt_xent_fwd_bwd_noalloc": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P]),
     "gt_sgd_step": ("err", [_P, _INT, _P, _P, _P, _I64, ctypes.POINTER(SgdCfg), _INT]),
     "gt_adam_step": ("err", [_P, _INT, _P, _P, _P, _P, _I64, ctypes.POINTER(AdamCfg), _I64]),
     "gt_adam_step_dev": ("err", [_P, _INT, _P, _P, _P, _P, _I64, ctypes.POINTER(AdamCfg), _P]),

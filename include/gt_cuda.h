@@ -205,6 +205,24 @@ GT_API char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const 
 GT_API char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
                       int64_t C, void* loss, void* dlogits, int32_t* bad_label);
 
+/* Largest batch gt_xent_fwd_bwd_noalloc accepts: its per-row loss terms live
+ * in a fixed 2 MiB device buffer inside the library (8 bytes per row). */
+#define GT_XENT_NOALLOC_MAX_ROWS 262144
+/* gt_xent_fwd_bwd for callers that must not allocate device memory during a
+ * step, e.g. a host that has already reserved the GPU's memory for its own
+ * allocator and cannot let a second pool grow, or one that forbids
+ * allocation inside its training loop. Same arguments, same results; no
+ * counterpart in the reference (whose backends allocate every result).
+ * Instead of pool memory it uses a 2 MiB buffer compiled into this library,
+ * which every GPU that loads the library keeps until the process exits.
+ * Batches larger than GT_XENT_NOALLOC_MAX_ROWS are rejected with an error.
+ * The first call on each device looks up that buffer's device address, so
+ * make it before capturing the stream into a graph. All calls share the one
+ * buffer: two calls that run on the GPU at the same time (different streams
+ * or contexts on one device) race and corrupt each other's loss. */
+GT_API char* gt_xent_fwd_bwd_noalloc(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
+                                     int64_t C, void* loss, void* dlogits, int32_t* bad_label);
+
 /* Optimizer hyperparameters (optim.SGDConfig / optim.AdamConfig,
  * optim/optim.go:22-27, 74-80). */
 typedef struct {
