@@ -40,6 +40,7 @@ LR, MOM, WD = 0.01, 0.9, 1e-4
 GEMM_FLOPS_PER_SAMPLE = 2 * (3 * IN * HID + 3 * HID * HID + 3 * HID * OUT - IN * HID)
 BWD_GEMM_FLOPS_PER_SAMPLE = 2 * (2 * IN * HID + 2 * HID * HID + 2 * HID * OUT - IN * HID)
 CPU_SAMPLE_ROWS = 256
+GEMM_REPS = [10]  # launches of each backward GEMM timed by gemm_roofline
 
 
 def peaks():
@@ -315,7 +316,7 @@ def gemm_roofline(lib, model, B):
         # realistic operands: tensor-core power (and so clocks) depend on the data
         h = rng.standard_normal(n, dtype=np.float32)
         check(lib.gt_upload(ctx.ptr, p, h.ctypes.data, n * 4))
-    reps = 10
+    reps = GEMM_REPS[0]
     for _ in range(2):
         check(lib.gt_linear_bwd_weight(ctx.ptr, 0, x, dy, dw, None, B, HID, HID))
         check(lib.gt_linear_bwd_data(ctx.ptr, 0, dy, w, x, 1, dx, B, HID, HID))
@@ -331,7 +332,7 @@ def gemm_roofline(lib, model, B):
     achieved = flops / (per_launch_ms / 1e3) / 1e12
     for p in (x, dy, w, dw, dx):
         ctx.release(p)
-    return {"path": "tc" if os.environ.get("GT_GEMM_PATH", "") != "simt" else "simt",
+    return {"path": "tc" if lib.gt_gemm_path_taken() == 2 else "simt",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None,
                          "kernel": f"backward GEMMs of a 4096x4096 layer (dW and dX, M=K=4096, batch {B})",
@@ -348,12 +349,34 @@ def main():
     ap.add_argument("--bucket-mb", type=int, default=32)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="time only the dominant kernel (the backward GEMMs at the workload's shapes), for profiling")
+    ap.add_argument("--reps", type=int, default=10)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.gemm_only:
+        return run_gemm_only(args)
     return run_ours(args)
+
+
+def run_gemm_only(args):
+    """The backward GEMMs of one 4096x4096 layer at batch 8192 (dW, then dX),
+    `reps` times each after two warm-up launches; prints one JSON line."""
+    from gotensor import model as gm
+    from gotensor._lib import cuda_lib
+    lib = cuda_lib()
+    model = gm.Model([gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, OUT)], [GLOBAL_BATCH, IN])
+    saved = GEMM_REPS[0]
+    GEMM_REPS[0] = args.reps
+    roof = gemm_roofline(lib, model, GLOBAL_BATCH)
+    GEMM_REPS[0] = saved
+    print(json.dumps({"kernel": roof["roofline"]["kernel"], "per_launch_ms": roof["roofline"]["per_launch_ms"],
+                      "achieved_tflops": roof["roofline"]["achieved"], "frac": roof["roofline"]["frac"],
+                      "gemm_path": lib.gt_gemm_path_taken()}), flush=True)
+    return 0
 
 
 if __name__ == "__main__":

@@ -252,14 +252,19 @@ __device__ __forceinline__ float tf32_round(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
-// One warp splits n16 float4s of a staged slice.
-__device__ __forceinline__ void split_tf32(float4* hi, float4* lo, int n16, int lane) {
+// One warp splits n16 float4s of a staged slice in place: x -> hi = tf32(x)
+// over x, lo = tf32(x - hi) into the lo plane. The tensor core reads an fp32
+// operand of kind::tf32 by dropping its low 13 bits (truncation), so both
+// halves are stored already rounded: lo = x - hi is exact in fp32, and
+// rounding it too keeps the pair within half a tf32 ulp of lo.
+__device__ __forceinline__ void split_tf32(float4* x, float4* lo, int n16, int lane) {
 #pragma unroll 8
   for (int i = lane; i < n16; i += 32) {
-    float4 v = hi[i], h, l;
+    float4 v = x[i], h, l;
     h.x = tf32_round(v.x), h.y = tf32_round(v.y), h.z = tf32_round(v.z), h.w = tf32_round(v.w);
-    l.x = __fsub_rn(v.x, h.x), l.y = __fsub_rn(v.y, h.y), l.z = __fsub_rn(v.z, h.z), l.w = __fsub_rn(v.w, h.w);
-    hi[i] = h;
+    l.x = tf32_round(__fsub_rn(v.x, h.x)), l.y = tf32_round(__fsub_rn(v.y, h.y));
+    l.z = tf32_round(__fsub_rn(v.z, h.z)), l.w = tf32_round(__fsub_rn(v.w, h.w));
+    x[i] = h;
     lo[i] = l;
   }
 }
