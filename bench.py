@@ -40,7 +40,6 @@ LR, MOM, WD = 0.01, 0.9, 1e-4
 GEMM_FLOPS_PER_SAMPLE = 2 * (3 * IN * HID + 3 * HID * HID + 3 * HID * OUT - IN * HID)
 BWD_GEMM_FLOPS_PER_SAMPLE = 2 * (2 * IN * HID + 2 * HID * HID + 2 * HID * OUT - IN * HID)
 CPU_SAMPLE_ROWS = 256
-GEMM_REPS = [10]  # launches of each backward GEMM timed by gemm_roofline
 
 
 def peaks():
@@ -262,10 +261,12 @@ def run_ours(args):
     ms_e2e = timed(step_e2e, args.steps)
     e2e = GLOBAL_BATCH * args.steps / (ms_e2e / 1e3)
 
-    # Roofline of the dominant kernel: the backward GEMMs (3xTF32 tcgen05) of
-    # the two 4096x4096 layers, launched alone on the model's stream with the
-    # same shapes, timed with CUDA events.
-    roof = gemm_roofline(lib, model, B)
+    # Roofline of the dominant kernel, the float32 GEMM (tcgen05 3xTF32):
+    # K more steps of the same workload with every GEMM launch bracketed by
+    # CUDA events on the model's stream (graph replay off: events inside a
+    # replayed graph keep only the last replay's times).
+    roof = step_roofline(lib, model, args.steps)
+    roof["roofline"]["step_ms_graph"] = ms_total / args.steps
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -286,10 +287,12 @@ def run_ours(args):
                        "graph": not args.no_graph,
                        "l2": "per-step working set (weights, grads, momentum 452 MB + activations) exceeds L2",
                        "gemm": "tcgen05 3xTF32" if roof.get("path") == "tc" else "SIMT fp32"},
+            "gemm_launches": roof["launches"],
             "loss_after": loss,
             "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
             "gpu_launches": int(launches),
             "roofline": roof["roofline"],
+            "optimizer_roofline": roof["optimizer"],
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
@@ -299,12 +302,99 @@ def run_ours(args):
     return 0
 
 
-def gemm_roofline(lib, model, B):
-    from gotensor._lib import check
-    ctx = model.ctx
+# dram__bytes_read.sum + dram__bytes_write.sum of the GEMM launches of one
+# training step of this workload, from one ncu capture (the command and the
+# per-launch figures are in profiles/wide_mlp_b8192_step_launches.md).
+GEMM_TRAFFIC_BYTES_PER_STEP = 4_526_827_008
+GEMM_LAUNCHES_PER_STEP = 8
+# The SGD update: read p, g, v and write p, v (float32), and the DRAM traffic
+# of its launch in the same capture.
+SGD_BYTES_PER_PARAM = 20
+SGD_TRAFFIC_BYTES = 697_041_152
+
+
+def _peak_3xtf32():
     hbm, bf16, kind = peaks()
     # 3xTF32: three TF32 products per fp32 MAC; TF32 runs at half the bf16 rate.
-    peak = bf16 / 2 / 3
+    return bf16 / 2 / 3, f"3xTF32 peak = {kind} bf16 burst {bf16:.0f} TF/s / 2 (TF32 rate) / 3 (products)"
+
+
+def step_roofline(lib, model, steps):
+    """Runs `steps` training steps with the GEMM launch timer on; returns the
+    flop rate of all GEMM launches (total algorithmic flops / total kernel
+    time) against the 3xTF32 peak, plus the per-shape breakdown."""
+    from gotensor._lib import check
+    ctx = model.ctx.ptr
+    peak, note = _peak_3xtf32()
+    model.enable_graph(False)
+    check(lib.gt_gemm_timer_start(ctx, steps * 32 + 64))
+    pass_ms, opt_ms, t = ctypes.c_float(), 0.0, ctypes.c_float()
+    check(lib.gt_mark(ctx, 4))
+    for _ in range(steps):
+        # train_step without a graph: forward_backward, then optimizer_step;
+        # marks 6/7 bracket the optimizer kernel (read back every step)
+        model.forward_backward()
+        check(lib.gt_mark(ctx, 6))
+        model.optimizer_step()
+        check(lib.gt_mark(ctx, 7))
+        check(lib.gt_elapsed_ms(ctx, 6, 7, ctypes.byref(t)))
+        opt_ms += t.value
+    check(lib.gt_mark(ctx, 5))
+    check(lib.gt_elapsed_ms(ctx, 4, 5, ctypes.byref(pass_ms)))
+    hbm, _, hbm_kind = peaks()
+    nparams = model.num_params
+    opt_gbs = SGD_BYTES_PER_PARAM * nparams / (opt_ms / steps / 1e3) / 1e9
+    optimizer = {"bound": "hbm", "kernel": "sgd_kernel (momentum + weight decay, one pass)",
+                 "achieved": opt_gbs, "peak": hbm, "unit": "GB/s", "frac": opt_gbs / hbm,
+                 "bytes_per_launch": SGD_BYTES_PER_PARAM * nparams, "ms_per_launch": opt_ms / steps,
+                 "traffic": SGD_TRAFFIC_BYTES,
+                 "note": f"{SGD_BYTES_PER_PARAM} B/param (read p, g, v; write p, v) x {nparams} params; "
+                         f"peak = {hbm_kind} copy bandwidth"}
+    n, dropped = ctypes.c_int64(), ctypes.c_int64()
+    check(lib.gt_gemm_timer_count(ctx, ctypes.byref(n), ctypes.byref(dropped)))
+    if dropped.value:
+        raise SystemExit(f"GEMM timer dropped {dropped.value} launches")
+    shapes = {}
+    total_ms = total_flops = 0.0
+    tc = True
+    mnk = (ctypes.c_int64 * 3)()
+    path = ctypes.c_int()
+    ms = ctypes.c_float()
+    for i in range(n.value):
+        check(lib.gt_gemm_timer_read(ctx, i, mnk, ctypes.byref(path), ctypes.byref(ms)))
+        key = f"{mnk[0]}x{mnk[1]}x{mnk[2]}"
+        flops = 2.0 * mnk[0] * mnk[1] * mnk[2]
+        e = shapes.setdefault(key, {"launches": 0, "ms": 0.0, "flops": flops})
+        e["launches"] += 1
+        e["ms"] += ms.value
+        total_ms += ms.value
+        total_flops += flops
+        tc = tc and path.value == 2
+    check(lib.gt_gemm_timer_stop(ctx))
+    per_step = n.value // steps
+    achieved = total_flops / (total_ms / 1e3) / 1e12
+    traffic = None
+    if GEMM_TRAFFIC_BYTES_PER_STEP and per_step == GEMM_LAUNCHES_PER_STEP:
+        traffic = GEMM_TRAFFIC_BYTES_PER_STEP / GEMM_LAUNCHES_PER_STEP
+    breakdown = {k: {"launches_per_step": v["launches"] // steps, "ms_per_launch": v["ms"] / v["launches"],
+                     "tflops": v["flops"] * v["launches"] / (v["ms"] / 1e3) / 1e12} for k, v in shapes.items()}
+    return {"path": "tc" if tc else "simt", "launches": per_step,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "gemm_tf32x3_pair (float32 GEMM, 3xTF32 on tcgen05): every GEMM launch of the "
+                                   "step (forward, dW, dX), M x N x K below",
+                         "flops_per_launch": total_flops / n.value, "ms_per_launch": total_ms / n.value,
+                         "gemm_share_of_step": total_ms / pass_ms.value, "step_ms_timed_pass": pass_ms.value / steps,
+                         "by_shape": breakdown, "peak_note": note + " (of measured)"},
+            "optimizer": optimizer}
+
+
+def gemm_isolated(lib, model, B, reps):
+    """The backward GEMMs of one 4096x4096 layer at batch B (dW, then dX),
+    `reps` times each after two warm-up launches, alone on the model's stream."""
+    from gotensor._lib import check
+    ctx = model.ctx
+    peak, note = _peak_3xtf32()
     fp = model.ctx.alloc
     x = fp(B * HID * 4)
     dy = fp(B * HID * 4)
@@ -316,7 +406,6 @@ def gemm_roofline(lib, model, B):
         # realistic operands: tensor-core power (and so clocks) depend on the data
         h = rng.standard_normal(n, dtype=np.float32)
         check(lib.gt_upload(ctx.ptr, p, h.ctypes.data, n * 4))
-    reps = GEMM_REPS[0]
     for _ in range(2):
         check(lib.gt_linear_bwd_weight(ctx.ptr, 0, x, dy, dw, None, B, HID, HID))
         check(lib.gt_linear_bwd_data(ctx.ptr, 0, dy, w, x, 1, dx, B, HID, HID))
@@ -332,12 +421,9 @@ def gemm_roofline(lib, model, B):
     achieved = flops / (per_launch_ms / 1e3) / 1e12
     for p in (x, dy, w, dw, dx):
         ctx.release(p)
-    return {"path": "tc" if lib.gt_gemm_path_taken() == 2 else "simt",
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "kernel": f"backward GEMMs of a 4096x4096 layer (dW and dX, M=K=4096, batch {B})",
-                         "per_launch_ms": per_launch_ms, "flops_per_launch": flops,
-                         "peak_note": f"3xTF32 peak = {kind} bf16 burst {bf16:.0f} TF/s / 2 (TF32) / 3 (products)"}}
+    return {"kernel": f"backward GEMMs of a 4096x4096 layer (dW and dX, M=K=4096, batch {B}), alone",
+            "per_launch_ms": per_launch_ms, "achieved_tflops": achieved, "peak_tflops": peak,
+            "frac": achieved / peak, "gemm_path": lib.gt_gemm_path_taken(), "peak_note": note}
 
 
 def main():
@@ -363,19 +449,13 @@ def main():
 
 
 def run_gemm_only(args):
-    """The backward GEMMs of one 4096x4096 layer at batch 8192 (dW, then dX),
-    `reps` times each after two warm-up launches; prints one JSON line."""
+    """Times only the dominant kernel (the backward GEMMs at the workload's
+    shapes) and prints one JSON line; the case the ncu --set full capture runs."""
     from gotensor import model as gm
     from gotensor._lib import cuda_lib
     lib = cuda_lib()
     model = gm.Model([gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, OUT)], [GLOBAL_BATCH, IN])
-    saved = GEMM_REPS[0]
-    GEMM_REPS[0] = args.reps
-    roof = gemm_roofline(lib, model, GLOBAL_BATCH)
-    GEMM_REPS[0] = saved
-    print(json.dumps({"kernel": roof["roofline"]["kernel"], "per_launch_ms": roof["roofline"]["per_launch_ms"],
-                      "achieved_tflops": roof["roofline"]["achieved"], "frac": roof["roofline"]["frac"],
-                      "gemm_path": lib.gt_gemm_path_taken()}), flush=True)
+    print(json.dumps(gemm_isolated(lib, model, GLOBAL_BATCH, args.reps)), flush=True)
     return 0
 
 

@@ -89,6 +89,7 @@ char* gt_destroy(gt_ctx* ctx) {
   if (!ctx) return nullptr;
   GT_TRY(gt::enter(ctx));
   if (ctx->nccl) GT_TRY(gt_comm_destroy(ctx, 0));
+  GT_TRY(gt_gemm_timer_stop(ctx));
   cudaStreamSynchronize(ctx->stream);
   cudaStreamSynchronize(ctx->comm_stream);
   cudaEventDestroy(ctx->fork);

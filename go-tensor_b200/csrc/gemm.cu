@@ -1,5 +1,7 @@
 // GEMM dispatch and the entry points built on it: Backend.MatMul
 // (internal/backend/backend.go:150) and the fused Linear forward/backward.
+#include <vector>
+
 #include "gemm.cuh"
 
 namespace gt {
@@ -9,14 +11,61 @@ static int g_gemm_taken = 0;
 void set_gemm_path(int path) { g_gemm_path = path; }
 int gemm_path() { return g_gemm_path; }
 
+}  // namespace gt
+
+// Per-launch device times of the GEMMs issued on a context: a CUDA event on
+// the context's stream before and after each GEMM kernel, so the figures are
+// the kernels' own durations inside whatever step issues them.
+struct gt_gemm_timer {
+  struct Launch {
+    int64_t m, n, k;
+    int path;
+    cudaEvent_t start, end;
+  };
+  std::vector<Launch> launches;
+  int64_t used = 0, dropped = 0;
+};
+
+namespace gt {
+
+// Brackets one GEMM with the context's timer events (when a timer is on and
+// the stream is not being captured into a graph).
+template <typename F>
+static char* timed_gemm(gt_ctx* ctx, const GemmShape& s, F&& run) {
+  gt_gemm_timer* t = ctx->gemm_timer;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (t) GT_CUDA(cudaStreamIsCapturing(ctx->stream, &cap));
+  if (!t || cap != cudaStreamCaptureStatusNone) return run();
+  if (t->used >= (int64_t)t->launches.size()) {
+    t->dropped++;
+    return run();
+  }
+  auto& l = t->launches[t->used++];
+  l.m = s.M, l.n = s.N, l.k = s.K;
+  GT_CUDA(cudaEventRecord(l.start, ctx->stream));
+  char* err = run();
+  l.path = g_gemm_taken;
+  GT_CUDA(cudaEventRecord(l.end, ctx->stream));
+  return err;
+}
+
+static char* gemm_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi);
+
 template <>
 char* gemm<double>(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
   if (g_gemm_path == 2) return errorf("gemm: the tcgen05 path has no float64 kind");
-  return gemm_simt<double>(ctx, s, A, B, epi);
+  return timed_gemm(ctx, s, [&] {
+    g_gemm_taken = 1;
+    return gemm_simt<double>(ctx, s, A, B, epi);
+  });
 }
 
 template <>
 char* gemm<float>(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {
+  return timed_gemm(ctx, s, [&] { return gemm_f32(ctx, s, A, B, epi); });
+}
+
+static char* gemm_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {
   if (g_gemm_path != 1) {
     bool done = false;
     GT_TRY(gemm_tc_f32(ctx, s, A, B, epi, &done));
@@ -40,6 +89,62 @@ extern "C" {
 
 void gt_debug_set_gemm_path(int path) { set_gemm_path(path); }
 int gt_gemm_path_taken(void) { return g_gemm_taken; }
+
+char* gt_gemm_timer_start(gt_ctx* ctx, int64_t capacity) {
+  GT_ENTER(ctx);
+  if (capacity <= 0 || capacity > (1 << 20)) return errorf("gt_gemm_timer_start: capacity %lld out of range",
+                                                           (long long)capacity);
+  GT_TRY(gt_gemm_timer_stop(ctx));
+  auto* t = new gt_gemm_timer();
+  t->launches.resize(capacity);
+  for (auto& l : t->launches) {
+    cudaError_t e1 = cudaEventCreate(&l.start), e2 = cudaEventCreate(&l.end);
+    if (e1 != cudaSuccess || e2 != cudaSuccess) {
+      ctx->gemm_timer = t;
+      gt_free_error(gt_gemm_timer_stop(ctx));
+      return cuda_error(e1 != cudaSuccess ? e1 : e2, "cudaEventCreate", __FILE__, __LINE__);
+    }
+  }
+  ctx->gemm_timer = t;
+  return nullptr;
+}
+
+char* gt_gemm_timer_stop(gt_ctx* ctx) {
+  GT_ENTER(ctx);
+  gt_gemm_timer* t = ctx->gemm_timer;
+  if (!t) return nullptr;
+  ctx->gemm_timer = nullptr;
+  GT_CUDA(cudaStreamSynchronize(ctx->stream));
+  for (auto& l : t->launches) {
+    if (l.start) cudaEventDestroy(l.start);
+    if (l.end) cudaEventDestroy(l.end);
+  }
+  delete t;
+  return nullptr;
+}
+
+char* gt_gemm_timer_count(gt_ctx* ctx, int64_t* launches, int64_t* dropped) {
+  GT_ENTER(ctx);
+  gt_gemm_timer* t = ctx->gemm_timer;
+  if (!t) return errorf("gt_gemm_timer_count: no timer on this context");
+  if (launches) *launches = t->used;
+  if (dropped) *dropped = t->dropped;
+  return nullptr;
+}
+
+char* gt_gemm_timer_read(gt_ctx* ctx, int64_t i, int64_t mnk[3], int* path, float* ms) {
+  GT_ENTER(ctx);
+  gt_gemm_timer* t = ctx->gemm_timer;
+  if (!t) return errorf("gt_gemm_timer_read: no timer on this context");
+  if (i < 0 || i >= t->used) return errorf("gt_gemm_timer_read: launch %lld of %lld", (long long)i,
+                                           (long long)t->used);
+  const auto& l = t->launches[i];
+  GT_CUDA(cudaEventSynchronize(l.end));
+  if (ms) GT_CUDA(cudaEventElapsedTime(ms, l.start, l.end));
+  if (mnk) mnk[0] = l.m, mnk[1] = l.n, mnk[2] = l.k;
+  if (path) *path = l.path;
+  return nullptr;
+}
 
 char* gt_matmul(gt_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t m, int64_t k, int64_t n,
                 int trans_a, int trans_b) {

@@ -25,6 +25,7 @@ struct gt_ctx {
   void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled entry point
   cudaEvent_t fork = nullptr, join = nullptr;  // compute <-> comm ordering
   cudaEvent_t marks[8] = {};                   // gt_mark timing points
+  struct gt_gemm_timer* gemm_timer = nullptr;  // gt_gemm_timer_start .. _stop
 };
 
 namespace gt {

@@ -109,6 +109,10 @@ CUDA_API = {
     "gt_mark": ("err", [_P, _INT]),
     "gt_elapsed_ms": ("err", [_P, _INT, _INT, ctypes.POINTER(ctypes.c_float)]),
     "gt_launch_count": (_I64, []),
+    "gt_gemm_timer_start": ("err", [_P, _I64]),
+    "gt_gemm_timer_stop": ("err", [_P]),
+    "gt_gemm_timer_count": ("err", [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
+    "gt_gemm_timer_read": ("err", [_P, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_INT), ctypes.POINTER(ctypes.c_float)]),
     "gt_debug_set_gemm_path": (None, [_INT]),
     "gt_gemm_path_taken": (_INT, []),
 }

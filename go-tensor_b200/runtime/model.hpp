@@ -2,8 +2,9 @@
 //
 // A Model turns the layer list of an nn.Sequential into a fixed plan of
 // fused kernel calls on libgotensor_cuda's C interface and owns every device
-// buffer the step touches, so a step allocates nothing and can be captured
-// into one CUDA graph.
+// buffer the step touches. The only allocations inside a step are kernel
+// scratch from the stream-ordered pool, which stream capture records as
+// graph memory nodes, so a step can be captured into one CUDA graph.
 #pragma once
 
 #include <cstdint>

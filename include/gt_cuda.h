@@ -287,6 +287,20 @@ GT_API char* gt_elapsed_ms(gt_ctx* ctx, int from, int to, float* ms);
  * the process so far. */
 GT_API int64_t gt_launch_count(void);
 
+/* Per-launch device times of the GEMM kernels issued on ctx (no counterpart
+ * in the reference; instrumentation for measuring the hot kernel inside a
+ * real step). While a timer is on, every GEMM launched on ctx's stream
+ * outside graph capture is bracketed by two CUDA events on that stream, up to
+ * `capacity` launches (later ones are counted as dropped, not timed).
+ * gt_gemm_timer_start replaces any earlier timer; gt_gemm_timer_read
+ * synchronizes on launch i's end event and returns its shape (M, N, K of
+ * C[M,N] += A[M,K] B[K,N]), its path (1 SIMT, 2 tcgen05) and its duration.
+ * gt_destroy stops the timer. */
+GT_API char* gt_gemm_timer_start(gt_ctx* ctx, int64_t capacity);
+GT_API char* gt_gemm_timer_stop(gt_ctx* ctx);
+GT_API char* gt_gemm_timer_count(gt_ctx* ctx, int64_t* launches, int64_t* dropped);
+GT_API char* gt_gemm_timer_read(gt_ctx* ctx, int64_t i, int64_t mnk[3], int* path, float* ms);
+
 /* ---- testing -------------------------------------------------------------- */
 /* Pins the float32 GEMM path: 0 automatic, 1 SIMT only, 2 tcgen05 only (shapes
  * that do not qualify then fail). Process-wide; for tests and benchmarks. */

@@ -78,3 +78,45 @@ def test_tc_special_values_and_accuracy_beyond_tf32():
     got = be.ToHost(be.MatMul(be.FromHost(a), be.FromHost(b), m, k, n, False, False))
     exact = k * (1.0 + 2.0 ** -20) * (1.0 - 2.0 ** -21)
     assert np.abs(got - exact).max() <= 2 * np.spacing(np.float32(exact)), (got[0], exact)
+
+
+def test_gemm_timer_records_each_launch_outside_capture():
+    import ctypes
+    from gotensor._lib import GTError, check
+    lib = _lib.cuda_lib()
+    be = cuda_backend()
+    ctx = be.ctx.ptr
+    rng = np.random.default_rng(9)
+    a = be.FromHost(rng.standard_normal(256 * 512).astype(np.float32))
+    b = be.FromHost(rng.standard_normal(512 * 384).astype(np.float32))
+    check(lib.gt_gemm_timer_start(ctx, 2))
+    try:
+        for _ in range(3):  # the third is beyond the capacity: counted as dropped
+            be.MatMul(a, b, 256, 512, 384, False, False)
+        n, dropped = ctypes.c_int64(), ctypes.c_int64()
+        check(lib.gt_gemm_timer_count(ctx, ctypes.byref(n), ctypes.byref(dropped)))
+        assert (n.value, dropped.value) == (2, 1)
+        mnk, path, ms = (ctypes.c_int64 * 3)(), ctypes.c_int(), ctypes.c_float()
+        for i in range(2):
+            check(lib.gt_gemm_timer_read(ctx, i, mnk, ctypes.byref(path), ctypes.byref(ms)))
+            assert tuple(mnk) == (256, 384, 512) and path.value == 2 and ms.value > 0
+        with pytest.raises(GTError, match="launch 2 of 2"):
+            check(lib.gt_gemm_timer_read(ctx, 2, mnk, ctypes.byref(path), ctypes.byref(ms)))
+        # a GEMM recorded into a graph is not timed (its events would only
+        # hold the last replay)
+        check(lib.gt_gemm_timer_start(ctx, 4))
+        out = be.Zeros(_lib.FLOAT32, 256 * 384)
+        check(lib.gt_capture_begin(ctx))
+        err = lib.gt_matmul(ctx, _lib.FLOAT32, a.ptr, b.ptr, out.ptr, 256, 512, 384, 0, 0)
+        g = ctypes.c_void_p()
+        check(lib.gt_capture_end(ctx, ctypes.byref(g)))
+        check(err)
+        check(lib.gt_graph_launch(ctx, g))
+        be.Sync()
+        lib.gt_graph_free(g)
+        check(lib.gt_gemm_timer_count(ctx, ctypes.byref(n), ctypes.byref(dropped)))
+        assert (n.value, dropped.value) == (0, 0)
+    finally:
+        check(lib.gt_gemm_timer_stop(ctx))
+    with pytest.raises(GTError, match="no timer"):
+        check(lib.gt_gemm_timer_count(ctx, None, None))
