@@ -152,9 +152,8 @@ def run_reference(args):
 # GPU leg
 
 def init_dist(n_gpus):
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from gotensor.dist import env_ranks
+    rank, world, local = env_ranks()
     if world != n_gpus:
         raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     if world > 1:
@@ -166,19 +165,13 @@ def init_dist(n_gpus):
 
 
 def allgather_max(x, world):
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from gotensor.dist import max_over_ranks
+    return max_over_ranks(x)
 
 
 def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
+    from gotensor.dist import barrier as _barrier
+    _barrier()
 
 
 def run_ours(args):
@@ -188,9 +181,9 @@ def run_ours(args):
     from gotensor._lib import check, cuda_lib
     rank, world, local = init_dist(args.gpus)
     torch.cuda.set_device(local)
-    if GLOBAL_BATCH % world:
-        raise SystemExit("the global batch must divide evenly over the GPUs")
-    B = GLOBAL_BATCH // world
+    from gotensor.dist import exchange_unique_id, shard
+    lo, hi = shard(GLOBAL_BATCH, rank, world)
+    B = hi - lo
     layers = [gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, HID), gm.ReLU(), gm.Linear(HID, OUT)]
     model = gm.Model(layers, [B, IN], device=local)
     lib, ctx = cuda_lib(), model.ctx.ptr
@@ -202,10 +195,7 @@ def run_ours(args):
     model.load_state_dict(sd)
     model.sgd(LR, MOM, WD)
     if world > 1:
-        import torch.distributed as dist
-        obj = [gm.unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        model.dp_init(rank, world, obj[0], timeout_ms=120000, bucket_bytes=args.bucket_mb << 20)
+        model.dp_init(rank, world, exchange_unique_id(rank), timeout_ms=120000, bucket_bytes=args.bucket_mb << 20)
     model.enable_graph(not args.no_graph)
 
     # This rank's shard of the batch, in pinned host memory for the e2e leg.
@@ -298,7 +288,10 @@ def run_ours(args):
         }
         print(json.dumps(line), flush=True)
     barrier(world)
-    del model
+    model.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
     return 0
 
 

@@ -60,6 +60,24 @@ static char* nccl_error(ncclResult_t r, const char* what) {
   return errorf("%s: %s", what, g_nccl.GetErrorString ? g_nccl.GetErrorString(r) : "nccl error");
 }
 
+// A non-blocking communicator may return ncclInProgress from a call that is
+// still being enqueued; it must not be used again until its state leaves
+// ncclInProgress. Waits for that (bounded), reporting any error.
+static char* nccl_settle(ncclComm_t comm, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return nullptr;
+  if (r != ncclInProgress) return nccl_error(r, what);
+  auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(60);
+  ncclResult_t state = ncclInProgress;
+  while (true) {
+    ncclResult_t q = g_nccl.CommGetAsyncError(comm, &state);
+    if (q != ncclSuccess) return nccl_error(q, "ncclCommGetAsyncError");
+    if (state != ncclInProgress) break;
+    if (std::chrono::steady_clock::now() > deadline) return errorf("%s: still in progress after 60 s", what);
+    std::this_thread::yield();
+  }
+  return state == ncclSuccess ? nullptr : nccl_error(state, what);
+}
+
 }  // namespace gt
 
 using namespace gt;
@@ -121,8 +139,7 @@ char* gt_allreduce_avg(gt_ctx* ctx, int dtype, void* buf, int64_t n) {
   if (n <= 0 || ctx->world == 1) return nullptr;
   ncclResult_t r = g_nccl.AllReduce(buf, buf, (size_t)n, dtype == GT_FLOAT64 ? ncclFloat64 : ncclFloat32, ncclAvg,
                                     (ncclComm_t)ctx->nccl, ctx->stream);
-  if (r != ncclSuccess && r != ncclInProgress) return nccl_error(r, "ncclAllReduce");
-  return nullptr;
+  return nccl_settle((ncclComm_t)ctx->nccl, r, "ncclAllReduce");
 }
 
 char* gt_allreduce_avg_async(gt_ctx* ctx, int dtype, void* buf, int64_t n) {
@@ -134,8 +151,7 @@ char* gt_allreduce_avg_async(gt_ctx* ctx, int dtype, void* buf, int64_t n) {
   GT_CUDA(cudaStreamWaitEvent(ctx->comm_stream, ctx->fork, 0));
   ncclResult_t r = g_nccl.AllReduce(buf, buf, (size_t)n, dtype == GT_FLOAT64 ? ncclFloat64 : ncclFloat32, ncclAvg,
                                     (ncclComm_t)ctx->nccl, ctx->comm_stream);
-  if (r != ncclSuccess && r != ncclInProgress) return nccl_error(r, "ncclAllReduce");
-  return nullptr;
+  return nccl_settle((ncclComm_t)ctx->nccl, r, "ncclAllReduce");
 }
 
 char* gt_comm_wait(gt_ctx* ctx) {
@@ -151,9 +167,20 @@ char* gt_comm_destroy(gt_ctx* ctx, int abort) {
   GT_TRY(gt::enter(ctx));
   ncclComm_t comm = (ncclComm_t)ctx->nccl;
   ctx->nccl = nullptr;
-  ncclResult_t r = abort ? g_nccl.CommAbort(comm) : g_nccl.CommDestroy(comm);
-  if (r != ncclSuccess && r != ncclInProgress) return nccl_error(r, abort ? "ncclCommAbort" : "ncclCommDestroy");
-  return nullptr;
+  if (abort) {
+    ncclResult_t r = g_nccl.CommAbort(comm);
+    return r == ncclSuccess ? nullptr : nccl_error(r, "ncclCommAbort");
+  }
+  // Destroying waits for the communicator's queued work on the streams.
+  cudaStreamSynchronize(ctx->comm_stream);
+  cudaStreamSynchronize(ctx->stream);
+  ncclResult_t r = g_nccl.CommDestroy(comm);
+  if (r == ncclInProgress) {
+    // A non-blocking destroy finishes in the background; the handle is freed
+    // by NCCL and must not be queried after this call.
+    return nullptr;
+  }
+  return r == ncclSuccess ? nullptr : nccl_error(r, "ncclCommDestroy");
 }
 
 }  // extern "C"

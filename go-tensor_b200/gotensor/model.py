@@ -76,6 +76,18 @@ class Model:
             self.params.append((name.value.decode(), [shape[d] for d in range(nd.value)], off.value))
         self.num_params = self.lib.gth_num_params(self.ptr)
 
+    def close(self):
+        """Frees the model (its captured step graph included) and leaves the
+        data-parallel communicator if dp_init joined one. Every rank calls it
+        after its last step."""
+        p = getattr(self, "ptr", None)
+        if p:
+            self.ptr = None
+            self.lib.gth_model_free(p)
+        if getattr(self, "_dp", False):
+            self._dp = False
+            check(_lib.cuda_lib().gt_comm_destroy(self.ctx.ptr, 0))
+
     def __del__(self):
         p = getattr(self, "ptr", None)
         if p:
@@ -190,6 +202,7 @@ class Model:
 
     def dp_init(self, rank, world, unique_id: bytes, timeout_ms=60000, bucket_bytes=25 << 20):
         check(self.lib.gth_dp_init(self.ptr, rank, world, unique_id, timeout_ms, bucket_bytes))
+        self._dp = world > 1
 
 
 def bucket_plan(sizes, bucket_elems):
