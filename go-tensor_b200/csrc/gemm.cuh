@@ -31,6 +31,11 @@ struct Epi {
     if (bias) v = add_rn(v, bias[bias_by_row ? m : n]);
     if (act != GT_ACT_NONE) v = act_fwd(act, v);
     if (dmask) v = act_bwd(dact, v, dmask[m * ldm + n]);
+    put(m, n, v);
+  }
+
+  // Writes the finished value of C(m, n) (row-major or the NCHW order).
+  __device__ __forceinline__ void put(int64_t m, int64_t n, T v) const {
     if (nchw_L > 0) {
       int64_t img = n / nchw_L;
       out[(img * nchw_M + m) * nchw_L + (n - img * nchw_L)] = v;

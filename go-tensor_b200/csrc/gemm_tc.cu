@@ -17,16 +17,23 @@
 // order. Roles per CTA (16 warps):
 //   warp 0      TMA producer: fp32 slices of A and B (16 elements of K) into
 //               a 6-stage shared-memory ring, K-major or M/N-major;
-//   warp 1      (leader CTA) MMA issuer: 3 x 2 tcgen05.mma per slice into the
+//   warp 1      (leader CTA) MMA issuer: 3 x 2 tcgen05.mma per slice into a
 //               partial accumulator, commits that free the slot in both CTAs;
 //   warps 2-7   splitters, one per ring slot: warp 2+j rewrites every slice
 //               landing in slot j as tf32 hi (in place) and lo (beside it),
 //               then signals the leader's MMA, so six slices are split
 //               concurrently and each warp's fence/arrive latency is hidden;
-//   warps 8-15  promoters: total += partial after every group, and at the end
-//               of a tile the epilogue (bias, activation or activation
-//               derivative, store) straight from registers.
-// Tensor memory: columns [0,256) hold the total, [256,512) the partial.
+//   warps 8-15  promoters: read each finished partial into registers and add
+//               it to the tile's running total, which lives in their
+//               registers (128 values per thread); at the end of a tile the
+//               epilogue (bias, activation or activation derivative, store)
+//               goes from those registers through a per-warp shared-memory
+//               transpose, so global loads and stores are coalesced rows.
+// Tensor memory holds two partial accumulators (columns [0,256) and
+// [256,512)): the MMAs of one group of K-slices run while the promoters read
+// the other, so neither waits for the other, and a tile's epilogue overlaps
+// the next tile's first two groups. The register split (setmaxnreg) gives
+// warps 0-7 64 registers each and the promoters 192.
 //
 // Every barrier wait is bounded in time; on expiry the kernel records the
 // waiting site in an error word (reported by gt_sync), stops its loops,
@@ -56,9 +63,18 @@ constexpr uint32_t A_BYTES = BM * BK * 4;
 constexpr uint32_t B_BYTES = BNH * BK * 4;
 constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // A hi, A lo, B hi, B lo
 constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
-constexpr uint32_t SMEM_BYTES = BAR_OFFSET + 512 + 1024;
+constexpr int PROMOTER_WARPS = PROMOTERS / 32;
+constexpr int EPI_LD = 33;  // padded row of the per-warp 32 x 32 transpose (conflict-free both ways)
+constexpr uint32_t EPI_OFFSET = BAR_OFFSET + 512;
+constexpr uint32_t EPI_BYTES = PROMOTER_WARPS * 32 * EPI_LD * 4;
+constexpr uint32_t SMEM_BYTES = EPI_OFFSET + EPI_BYTES + 1024;  // + slack for 1024-byte alignment
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t PARTIAL_COL = 256;
+constexpr uint32_t BUF_COLS = 256;  // one partial accumulator: 128 lanes x 256 fp32 columns
+// Registers per thread after the split: warps 0-7 (TMA, MMA, splitters) and
+// warps 8-15 (promoters). The launch gives every thread 65536 / 512 = 128;
+// the split keeps the block's total: 256 * 64 + 256 * 192 = 256 * 128 * 2.
+constexpr int REGS_LOW = 64, REGS_HIGH = 192;
+static_assert(256 * REGS_LOW + 256 * REGS_HIGH <= THREADS * 128, "register split exceeds the launch's registers");
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s; a healthy wait takes microseconds
 
 static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
@@ -269,18 +285,77 @@ __device__ __forceinline__ void split_tf32(float4* x, float4* lo, int n16, int l
   }
 }
 
+// Epilogue kinds: each kernel instantiation carries only the code of its
+// kind. The promoters' code shares the SM's instruction cache with the MMA
+// issuer and the splitters, and large unrolled epilogues measurably slowed
+// the whole pipeline, so every kind keeps its unrolled part small.
+enum EpiKind : int {
+  EK_PLAIN = 0,      // C stored row-major
+  EK_BIAS_RELU = 1,  // + bias[n] (optional), then ReLU (optional): Linear forward
+  EK_MASK = 2,       // * act'(mask[m][n]): the dX of a Linear after an activation
+  EK_GENERIC = 3,    // anything else (tanh/sigmoid forward, bias by row, NCHW order)
+};
+
+inline int epi_kind(const Epi<float>& e) {
+  const bool rowmajor = e.nchw_L == 0;
+  if (!e.bias && e.act == GT_ACT_NONE && !e.dmask && rowmajor) return EK_PLAIN;
+  if (!e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask && rowmajor) return EK_BIAS_RELU;
+  if (!e.bias && e.act == GT_ACT_NONE && e.dmask && rowmajor) return EK_MASK;
+  return EK_GENERIC;
+}
+
+// Finishes one 32 x 32 block of C held in the warp's transpose buffer: lane l
+// owns column n of rows m0 .. m0+31, so each row's access is 128 contiguous
+// bytes. Same operations, in the same order, as Epi::store.
+template <int EK>
+__device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const GemmShape& s, const float* xpose, int lane,
+                                               int64_t m0, int64_t n) {
+  if (n >= s.N) return;
+  const int rows = (int)(s.M - m0 < 32 ? s.M - m0 : 32);
+  float* op = epi.out + m0 * epi.ldc + n;
+  if (EK == EK_PLAIN) {
+#pragma unroll 4
+    for (int r = 0; r < rows; r++) op[r * epi.ldc] = xpose[r * EPI_LD + lane];
+  } else if (EK == EK_BIAS_RELU) {
+    const float b = epi.bias ? __ldg(epi.bias + n) : 0.0f;
+    const bool relu = epi.act == GT_ACT_RELU;
+#pragma unroll 4
+    for (int r = 0; r < rows; r++) {
+      float v = xpose[r * EPI_LD + lane];
+      if (epi.bias) v = __fadd_rn(v, b);
+      if (relu) v = go_max(v, 0.0f);
+      op[r * epi.ldc] = v;
+    }
+  } else if (EK == EK_MASK) {
+    // The mask values of 8 rows are requested before any is used.
+    const float* mp = epi.dmask + m0 * epi.ldm + n;
+#pragma unroll 1
+    for (int r0 = 0; r0 < 32; r0 += 8) {
+      float mask[8];
+#pragma unroll
+      for (int r = 0; r < 8; r++) mask[r] = r0 + r < rows ? __ldg(mp + (r0 + r) * epi.ldm) : 0.0f;
+#pragma unroll
+      for (int r = 0; r < 8; r++)
+        if (r0 + r < rows) op[(r0 + r) * epi.ldc] = act_bwd(epi.dact, xpose[(r0 + r) * EPI_LD + lane], mask[r]);
+    }
+  } else {
+#pragma unroll 1
+    for (int r = 0; r < rows; r++) epi.store(m0 + r, n, xpose[r * EPI_LD + lane]);
+  }
+}
+
 struct Shared {
   uint64_t full[STAGES];   // TMA -> splitters (local)
   uint64_t split[STAGES];  // splitters of both CTAs -> leader's MMA
   uint64_t empty[STAGES];  // MMA -> producers of both CTAs
-  uint64_t pfull;          // MMA -> promoters of both CTAs: a partial is complete
-  uint64_t pempty;         // promoters of both CTAs -> leader's MMA: the partial was read
+  uint64_t pfull[2];       // MMA -> promoters of both CTAs: partial buffer b is complete
+  uint64_t pempty[2];      // promoter warps of both CTAs -> leader's MMA: buffer b was read
   uint64_t mma_done;       // leader: every MMA issued has completed
   uint32_t tmem_base;
   int failed;
 };
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int EK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             GemmShape s, Epi<float> epi) {
@@ -304,8 +379,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_init(&sh->split[i], 2 * 32);  // one splitter warp per CTA per slice
       mbar_init(&sh->empty[i], 1);
     }
-    mbar_init(&sh->pfull, 1);
-    mbar_init(&sh->pempty, 2 * PROMOTERS);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&sh->pfull[b], 1);
+      mbar_init(&sh->pempty[b], 2 * PROMOTER_WARPS);  // one arrival per promoter warp per CTA
+    }
     mbar_init(&sh->mma_done, 1);
     sh->failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -321,147 +398,171 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  if (warp == 0) {
-    if (lane == 0) {  // ---- TMA producer (both CTAs)
-      int it = 0, issued_to = 0;
-      for (int t = pair; t < tiles && !*failed; t += pairs) {
-        const int mt = t / n_tiles, nt = t % n_tiles;
-        const int a_row = mt * 2 * BM + (int)rank * BM;
-        const int b_row = nt * BN + (int)rank * BNH;
-        for (int kt = 0; kt < num_k; kt++, it++) {
-          const int st = it % STAGES;
-          if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1)) {
-            *failed = 1;
-            break;
+  // Whole warpgroups change their register allocation together, each in
+  // its own branch: code that both paths reach is held to the lower limit.
+  if (warp < 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_LOW));
+    if (warp == 0) {
+      if (lane == 0) {  // ---- TMA producer (both CTAs)
+        int it = 0, issued_to = 0;
+        for (int t = pair; t < tiles && !*failed; t += pairs) {
+          const int mt = t / n_tiles, nt = t % n_tiles;
+          const int a_row = mt * 2 * BM + (int)rank * BM;
+          const int b_row = nt * BN + (int)rank * BNH;
+          for (int kt = 0; kt < num_k; kt++, it++) {
+            const int st = it % STAGES;
+            if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1)) {
+              *failed = 1;
+              break;
+            }
+            uint8_t* a_hi = smem + st * STAGE_BYTES;
+            uint8_t* b_hi = a_hi + 2 * A_BYTES;
+            mbar_expect_tx(&sh->full[st], A_BYTES + B_BYTES);
+            const int k0 = kt * BK;
+            if (A_MN) {
+  #pragma unroll
+              for (int j = 0; j < BM / 32; j++) tma_load_2d(a_hi + j * kLboMN, &tmA, &sh->full[st], a_row + 32 * j, k0);
+            } else {
+              tma_load_2d(a_hi, &tmA, &sh->full[st], k0, a_row);
+            }
+            if (B_MN) {
+  #pragma unroll
+              for (int j = 0; j < BNH / 32; j++)
+                tma_load_2d(b_hi + j * kLboMN, &tmB, &sh->full[st], b_row + 32 * j, k0);
+            } else {
+              tma_load_2d(b_hi, &tmB, &sh->full[st], k0, b_row);
+            }
+            issued_to = it + 1;
           }
-          uint8_t* a_hi = smem + st * STAGE_BYTES;
-          uint8_t* b_hi = a_hi + 2 * A_BYTES;
-          mbar_expect_tx(&sh->full[st], A_BYTES + B_BYTES);
-          const int k0 = kt * BK;
-          if (A_MN) {
-#pragma unroll
-            for (int j = 0; j < BM / 32; j++) tma_load_2d(a_hi + j * kLboMN, &tmA, &sh->full[st], a_row + 32 * j, k0);
-          } else {
-            tma_load_2d(a_hi, &tmA, &sh->full[st], k0, a_row);
-          }
-          if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < BNH / 32; j++)
-              tma_load_2d(b_hi + j * kLboMN, &tmB, &sh->full[st], b_row + 32 * j, k0);
-          } else {
-            tma_load_2d(b_hi, &tmB, &sh->full[st], k0, b_row);
-          }
-          issued_to = it + 1;
+        }
+        if (*failed) {  // let copies in flight land before the CTA tears down
+          for (int i = issued_to > STAGES ? issued_to - STAGES : 0; i < issued_to; i++)
+            mbar_wait(&sh->full[i % STAGES], (i / STAGES) & 1, 5);
         }
       }
-      if (*failed) {  // let copies in flight land before the CTA tears down
-        for (int i = issued_to > STAGES ? issued_to - STAGES : 0; i < issued_to; i++)
-          mbar_wait(&sh->full[i % STAGES], (i / STAGES) & 1, 5);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
-      const uint32_t idesc = instr_desc<A_MN, B_MN>();
-      int it = 0, group = 0;
-      bool stop = false;
-      for (int t = pair; t < tiles && !stop; t += pairs) {
-        for (int kt = 0; kt < num_k; kt++, it++) {
-          const bool group_start = kt % GROUP == 0;
-          if (group_start) {  // the promoters must have read the previous partial
-            if (!mbar_wait(&sh->pempty, (group & 1) ^ 1, 2)) {
+    } else if (warp == 1) {
+      if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
+        const uint32_t idesc = instr_desc<A_MN, B_MN>();
+        int it = 0, group = 0;
+        bool stop = false;
+        for (int t = pair; t < tiles && !stop; t += pairs) {
+          for (int kt = 0; kt < num_k; kt++, it++) {
+            const bool group_start = kt % GROUP == 0;
+            const uint32_t buf = (uint32_t)(group & 1);
+            if (group_start) {  // the promoters must have read this buffer's previous partial
+              if (!mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2)) {
+                stop = true;
+                break;
+              }
+              tc_fence_after();
+            }
+            const int st = it % STAGES;
+            if (!mbar_wait(&sh->split[st], (it / STAGES) & 1, 3)) {
               stop = true;
               break;
             }
             tc_fence_after();
-          }
-          const int st = it % STAGES;
-          if (!mbar_wait(&sh->split[st], (it / STAGES) & 1, 3)) {
-            stop = true;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_hi = smem_u32(smem + st * STAGE_BYTES), a_lo = a_hi + A_BYTES;
-          const uint32_t b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < BK / 8; kk++) {
-            const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
-            const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
-            mma_tf32_pair(tmem + PARTIAL_COL, dal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
-            mma_tf32_pair(tmem + PARTIAL_COL, dah, dbl, idesc, 1u);
-            mma_tf32_pair(tmem + PARTIAL_COL, dah, dbh, idesc, 1u);
-          }
-          mma_commit_pair(&sh->empty[st]);  // frees the slot in both CTAs
-          if (kt % GROUP == GROUP - 1 || kt == num_k - 1) {
-            mma_commit_pair(&sh->pfull);
-            group++;
+            const uint32_t a_hi = smem_u32(smem + st * STAGE_BYTES), a_lo = a_hi + A_BYTES;
+            const uint32_t b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
+  #pragma unroll
+            for (int kk = 0; kk < BK / 8; kk++) {
+              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
+              const uint32_t d = tmem + buf * BUF_COLS;
+              mma_tf32_pair(d, dal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
+              mma_tf32_pair(d, dah, dbl, idesc, 1u);
+              mma_tf32_pair(d, dah, dbh, idesc, 1u);
+            }
+            mma_commit_pair(&sh->empty[st]);  // frees the slot in both CTAs
+            if (kt % GROUP == GROUP - 1 || kt == num_k - 1) {
+              mma_commit_pair(&sh->pfull[buf]);
+              group++;
+            }
           }
         }
+        if (stop) *failed = 1;
+        // Every MMA must be complete before the pair frees its tensor memory.
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&sh->mma_done))
+                     : "memory");
+        mbar_wait(&sh->mma_done, 0, 6);
       }
-      if (stop) *failed = 1;
-      // Every MMA must be complete before the pair frees its tensor memory.
-      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       smem_u32(&sh->mma_done))
-                   : "memory");
-      mbar_wait(&sh->mma_done, 0, 6);
-    }
-  } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + STAGES) {
-    // ---- splitters (both CTAs): this warp owns ring slot st, i.e. every
-    // STAGES-th slice, starting with slice st.
-    const int st = warp - SPLIT_WARP0;
-    const int total = ((tiles - pair + pairs - 1) / pairs) * num_k;  // slices this pair streams
-    for (int it = st; it < total; it += STAGES) {
-      if (__shfl_sync(0xffffffffu, *failed, 0)) break;
-      if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4)) {
-        *failed = 1;
-        break;
-      }
-      uint8_t* stage = smem + st * STAGE_BYTES;
-      split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
-      split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + B_BYTES), B_BYTES / 16, lane);
-      fence_async_shared();  // generic-proxy writes -> visible to the tensor core
-      mbar_arrive_rank(&sh->split[st], 0);
-    }
-  } else if (warp >= 8) {
-    // ---- promoters and epilogue (both CTAs): TMEM lanes 32*(warp%4)..+31 are
-    // this warp's rows, columns [128*h, 128*h + 128) its half of the tile.
-    // Every decision below is warp-uniform: tcgen05.ld/st are .sync.aligned.
-    const int q = warp & 3, h = (warp - 8) >> 2;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    int group = 0;
-    for (int t = pair; t < tiles && !__shfl_sync(0xffffffffu, *failed, 0); t += pairs) {
-      const int mt = t / n_tiles, nt = t % n_tiles;
-      const int64_t row = (int64_t)mt * 2 * BM + rank * BM + 32 * q + lane;
-      const int groups = (num_k + GROUP - 1) / GROUP;
-      for (int g = 0; g < groups; g++, group++) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&sh->pfull, group & 1, 7))) {
+    } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + STAGES) {
+      // ---- splitters (both CTAs): this warp owns ring slot st, i.e. every
+      // STAGES-th slice, starting with slice st.
+      const int st = warp - SPLIT_WARP0;
+      const int total = ((tiles - pair + pairs - 1) / pairs) * num_k;  // slices this pair streams
+      for (int it = st; it < total; it += STAGES) {
+        if (__shfl_sync(0xffffffffu, *failed, 0)) break;
+        if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4)) {
           *failed = 1;
           break;
         }
-        tc_fence_after();
-        const bool last = g == groups - 1;
-#pragma unroll 1
-        for (int j = 0; j < 4; j++) {
-          const uint32_t col = 128 * h + 32 * j;
-          float p[32];
-          tmem_load32(lane_base + PARTIAL_COL + col, p);
-          if (g > 0) {
-            float tot[32];
-            tmem_load32(lane_base + col, tot);
+        uint8_t* stage = smem + st * STAGE_BYTES;
+        split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
+        split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + B_BYTES), B_BYTES / 16, lane);
+        fence_async_shared();  // generic-proxy writes -> visible to the tensor core
+        mbar_arrive_rank(&sh->split[st], 0);
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_HIGH));
+    // ---- promoters and epilogue (both CTAs): TMEM lanes 32*(warp%4)..+31 are
+    // this warp's rows, columns [128*h, 128*h + 128) its half of the tile.
+    // Every decision below is warp-uniform: tcgen05.ld is .sync.aligned.
+    const int q = warp & 3, h = (warp - 8) >> 2;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + 128 * h;
+    float* xpose = (float*)(smem + EPI_OFFSET) + (warp - 8) * 32 * EPI_LD;
+    const int groups = (num_k + GROUP - 1) / GROUP;
+    int group = 0;
+    for (int t = pair; t < tiles && !__shfl_sync(0xffffffffu, *failed, 0); t += pairs) {
+      const int mt = t / n_tiles, nt = t % n_tiles;
+      // The running total starts at +0 and every partial is added with
+      // round-to-nearest, like the reference's c = 0; c += a*b.
+      float tot[128];
 #pragma unroll
-            for (int i = 0; i < 32; i++) p[i] = __fadd_rn(tot[i], p[i]);
-          }
-          if (!last) {
-            tmem_store32(lane_base + col, p);
-          } else if (row < s.M) {
-            const int64_t n0 = (int64_t)nt * BN + col;
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-              if (n0 + i < s.N) epi.store(row, n0 + i, p[i]);
-          }
+      for (int i = 0; i < 128; i++) tot[i] = 0.0f;
+      bool ok = true;
+      for (int g = 0; g < groups; g++, group++) {
+        const uint32_t buf = (uint32_t)(group & 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&sh->pfull[buf], (group >> 1) & 1, 7))) {
+          *failed = 1;
+          ok = false;
+          break;
         }
-        if (!last) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          float p[32];
+          tmem_load32(lane_base + buf * BUF_COLS + 32 * j, p);
+#pragma unroll
+          for (int i = 0; i < 32; i++) tot[32 * j + i] = __fadd_rn(tot[32 * j + i], p[i]);
+        }
         tc_fence_before();
-        mbar_arrive_rank(&sh->pempty, 0);  // the partial may be overwritten
+        __syncwarp();
+        if (lane == 0) mbar_arrive_rank(&sh->pempty[buf], 0);  // the buffer may be overwritten
+      }
+      if (!ok) break;
+      // Epilogue: four 32 x 32 blocks through the transpose buffer (the
+      // switch keeps the register indices static in a loop that is not
+      // unrolled, so the block's code exists once).
+      const int64_t m0 = (int64_t)mt * 2 * BM + rank * BM + 32 * q;
+#pragma unroll 1
+      for (int j = 0; j < 4; j++) {
+        switch (j) {
+#define GT_XPOSE_CASE(J)                                                          \
+  case J:                                                                         \
+    _Pragma("unroll") for (int i = 0; i < 32; i++) xpose[lane * EPI_LD + i] = tot[32 * J + i]; \
+    break;
+          GT_XPOSE_CASE(0)
+          GT_XPOSE_CASE(1)
+          GT_XPOSE_CASE(2)
+          GT_XPOSE_CASE(3)
+#undef GT_XPOSE_CASE
+        }
+        __syncwarp();
+        epilogue_block<EK>(epi, s, xpose, lane, m0, (int64_t)nt * BN + 128 * h + 32 * j + lane);
+        __syncwarp();
       }
     }
   }
@@ -498,7 +599,7 @@ static char* make_map(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t 
   return nullptr;
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int EK>
 static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {
   CUtensorMap ta, tb;
   if (A_MN)
@@ -509,7 +610,7 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
     GT_TRY(make_map(ctx, &tb, B, s.N, s.K, s.ldb, true));
   else
     GT_TRY(make_map(ctx, &tb, B, s.K, s.N, s.ldb, false));
-  auto kern = gemm_tf32x3_pair_kernel<A_MN, B_MN>;
+  auto kern = gemm_tf32x3_pair_kernel<A_MN, B_MN, EK>;
   static bool configured[64] = {};
   if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
     GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
@@ -525,6 +626,15 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
   GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi));
   GT_LAUNCH_CHECK();
   return nullptr;
+}
+
+template <int EK>
+static char* launch_layout(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
+                           bool a_mn, bool b_mn) {
+  if (!a_mn && !b_mn) return launch<false, false, EK>(ctx, s, A, B, epi);
+  if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi);
+  if (a_mn && !b_mn) return launch<true, false, EK>(ctx, s, A, B, epi);
+  return launch<true, true, EK>(ctx, s, A, B, epi);
 }
 
 }  // namespace tc
@@ -552,14 +662,12 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
   if (gemm_path() != 2 && s.M * s.N * s.K < (int64_t)1 << 21) return nullptr;
   const bool a_mn = s.trans_a, b_mn = !s.trans_b;
   char* err;
-  if (!a_mn && !b_mn)
-    err = tc::launch<false, false>(ctx, s, A, B, epi);
-  else if (!a_mn && b_mn)
-    err = tc::launch<false, true>(ctx, s, A, B, epi);
-  else if (a_mn && !b_mn)
-    err = tc::launch<true, false>(ctx, s, A, B, epi);
-  else
-    err = tc::launch<true, true>(ctx, s, A, B, epi);
+  switch (tc::epi_kind(epi)) {
+    case tc::EK_PLAIN: err = tc::launch_layout<tc::EK_PLAIN>(ctx, s, A, B, epi, a_mn, b_mn); break;
+    case tc::EK_BIAS_RELU: err = tc::launch_layout<tc::EK_BIAS_RELU>(ctx, s, A, B, epi, a_mn, b_mn); break;
+    case tc::EK_MASK: err = tc::launch_layout<tc::EK_MASK>(ctx, s, A, B, epi, a_mn, b_mn); break;
+    default: err = tc::launch_layout<tc::EK_GENERIC>(ctx, s, A, B, epi, a_mn, b_mn); break;
+  }
   if (!err) *done = true;
   return err;
 }
