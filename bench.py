@@ -51,20 +51,27 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+CLOCK_FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
 def clocks_sampler(index: int):
-    fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Starts nvidia-smi sampling GPU `index` every 50 ms (timestamped), well
+    before the timed regions so that its start-up delay costs no samples."""
     out = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
     try:
-        p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={fields}", "--format=csv,noheader,nounits",
-                              "-lms", "200"], stdout=out, stderr=subprocess.DEVNULL)
+        p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={CLOCK_FIELDS}",
+                              "--format=csv,noheader,nounits", "-lms", "50"], stdout=out, stderr=subprocess.DEVNULL)
     except OSError:
         p = None
     return p, out.name
 
 
-def clocks_summary(proc, path):
+def clocks_summary(proc, path, windows):
+    """Median SM clock, max clock and active throttle reasons over the samples
+    taken inside `windows` (host-time intervals of the timed regions)."""
+    import datetime as _dt
     if proc is None:
         return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
     proc.terminate()
@@ -72,27 +79,34 @@ def clocks_summary(proc, path):
         proc.wait(timeout=5)
     except subprocess.TimeoutExpired:
         proc.kill()
-    sm, smax, reasons = [], [], set()
+    sm, smax, power, reasons = [], [], [], set()
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
     with open(path) as f:
         for line in f:
             c = [x.strip() for x in line.split(",")]
-            if len(c) < 9:
+            if len(c) < 10:
                 continue
             try:
-                sm.append(float(c[1]))
-                smax.append(float(c[2]))
+                t = _dt.datetime.strptime(c[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                mhz, mx = float(c[2]), float(c[3])
             except ValueError:
                 continue
-            for n, v in zip(names, c[5:9]):
+            if not any(lo <= t <= hi for lo, hi in windows):
+                continue
+            sm.append(mhz)
+            smax.append(mx)
+            try:
+                power.append(float(c[4]))
+            except ValueError:
+                pass
+            for n, v in zip(names, c[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
     os.unlink(path)
     if not sm:
-        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-    loaded = [s for s in sm if s >= 0.5 * max(sm)] or sm
-    return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-            "samples": len(sm)}
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples inside the timed regions"]}
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+            "samples": len(sm), "sm_mhz_min": min(sm), "power_w_max": max(power) if power else None}
 
 
 # ---------------------------------------------------------------------------
@@ -208,22 +222,28 @@ def run_ours(args):
     h2d = xh.numel() * 4 + yh.numel() * 4
     model.set_batch(x_np, y_np)
 
-    def step_resident():
-        model.train_step()
+    def steps_resident(k):
+        for _ in range(k):
+            model.train_step()
 
-    def step_e2e():
-        check(lib.gt_upload_async(ctx, model.input_device, xh.data_ptr(), xh.numel() * 4))
-        check(lib.gt_upload_async(ctx, model.labels_device, yh.data_ptr(), yh.numel() * 4))
-        model.train_step()
-        check(lib.gt_download_async(ctx, loss_h.data_ptr(), model.lib.gth_loss_device(model.ptr), 4))
+    def steps_e2e(k):
+        # Every step's batch goes host -> device (pinned memory, copy stream)
+        # and its loss comes back. The upload of batch i+1 overlaps step i;
+        # the first upload has nothing to overlap.
+        model.stage_batch(xh.data_ptr(), yh.data_ptr())
+        for i in range(k):
+            if i + 1 < k:
+                model.stage_batch(xh.data_ptr(), yh.data_ptr())
+            model.train_step()
+            check(lib.gt_download_async(ctx, loss_h.data_ptr(), model.lib.gth_loss_device(model.ptr), 4))
 
     def timed(fn, k):
+        """Device time of fn(k) (k steps) on the model's stream, max over ranks."""
         barrier(world)
         model.ctx.sync()
         torch.cuda.synchronize()
         check(lib.gt_mark(ctx, 0))
-        for _ in range(k):
-            fn()
+        fn(k)
         check(lib.gt_mark(ctx, 1))
         ms = ctypes.c_float()
         check(lib.gt_elapsed_ms(ctx, 0, 1, ctypes.byref(ms)))
@@ -232,23 +252,26 @@ def run_ours(args):
         barrier(world)
         return allgather_max(ms.value, world)
 
-    for _ in range(max(args.warmup, 3)):
-        step_resident()
+    proc, cpath = clocks_sampler(local)
+    steps_resident(max(args.warmup, 3))
     model.ctx.sync()
     launches_per_step = model.step_launches
     before = lib.gt_launch_count()
-    proc, cpath = clocks_sampler(local)
-    ms_total = timed(step_resident, args.steps)
-    clocks = clocks_summary(proc, cpath)
+    windows = []
+    t0 = time.time()
+    ms_total = timed(steps_resident, args.steps)
+    windows.append((t0, time.time()))
     launches = lib.gt_launch_count() - before
     if launches == 0:  # graph replays launch without passing through the library's counter
         launches = launches_per_step * args.steps
     value = GLOBAL_BATCH * args.steps / (ms_total / 1e3)
     loss = model.loss()
 
-    for _ in range(2):
-        step_e2e()
-    ms_e2e = timed(step_e2e, args.steps)
+    steps_e2e(2)
+    t0 = time.time()
+    ms_e2e = timed(steps_e2e, args.steps)
+    windows.append((t0, time.time()))
+    clocks = clocks_summary(proc, cpath, windows)
     e2e = GLOBAL_BATCH * args.steps / (ms_e2e / 1e3)
 
     # Roofline of the dominant kernel, the float32 GEMM (tcgen05 3xTF32):
@@ -310,6 +333,15 @@ def _peak_3xtf32():
     hbm, bf16, kind = peaks()
     # 3xTF32: three TF32 products per fp32 MAC; TF32 runs at half the bf16 rate.
     return bf16 / 2 / 3, f"3xTF32 peak = {kind} bf16 burst {bf16:.0f} TF/s / 2 (TF32 rate) / 3 (products)"
+
+
+def _peak_3xtf32_sustained():
+    """The same from the sustained (power-capped) bf16 figure, or None."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]) / 2 / 3
+    except Exception:
+        return None
 
 
 def step_roofline(lib, model, steps):
@@ -378,7 +410,9 @@ def step_roofline(lib, model, steps):
                                    "step (forward, dW, dX), M x N x K below",
                          "flops_per_launch": total_flops / n.value, "ms_per_launch": total_ms / n.value,
                          "gemm_share_of_step": total_ms / pass_ms.value, "step_ms_timed_pass": pass_ms.value / steps,
-                         "by_shape": breakdown, "peak_note": note + " (of measured)"},
+                         "by_shape": breakdown, "peak_note": note + " (of measured)",
+                         "peak_sustained": _peak_3xtf32_sustained(),
+                         "frac_of_sustained": (achieved / _peak_3xtf32_sustained()) if _peak_3xtf32_sustained() else None},
             "optimizer": optimizer}
 
 
@@ -422,7 +456,7 @@ def gemm_isolated(lib, model, B, reps):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--bucket-mb", type=int, default=32)

@@ -72,6 +72,7 @@ char* gt_init(int device, gt_ctx** out) {
   snprintf(ctx->name, sizeof ctx->name, "%s", prop.name);
   GT_CUDA(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
   GT_CUDA(cudaStreamCreateWithFlags(&ctx->comm_stream, cudaStreamNonBlocking));
+  GT_CUDA(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
   GT_CUDA(cudaDeviceGetDefaultMemPool(&ctx->pool, device));
   uint64_t keep = UINT64_MAX;  // keep freed blocks cached, like a caching allocator
   GT_CUDA(cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &keep));
@@ -92,11 +93,13 @@ char* gt_destroy(gt_ctx* ctx) {
   GT_TRY(gt_gemm_timer_stop(ctx));
   cudaStreamSynchronize(ctx->stream);
   cudaStreamSynchronize(ctx->comm_stream);
+  cudaStreamSynchronize(ctx->copy_stream);
   cudaEventDestroy(ctx->fork);
   cudaEventDestroy(ctx->join);
   for (auto& e : ctx->marks) cudaEventDestroy(e);
   cudaStreamDestroy(ctx->stream);
   cudaStreamDestroy(ctx->comm_stream);
+  cudaStreamDestroy(ctx->copy_stream);
   delete ctx;
   return nullptr;
 }

@@ -1,4 +1,6 @@
-// CUDA graph capture of the context's stream, and stream timing points.
+// CUDA graph capture of the context's stream, stream timing points, and the
+// events and copy stream that let a host overlap the next batch's upload with
+// the step in flight.
 #include "gt_common.cuh"
 
 struct gt_graph {
@@ -59,6 +61,77 @@ char* gt_elapsed_ms(gt_ctx* ctx, int from, int to, float* ms) {
   GT_CUDA(cudaEventSynchronize(ctx->marks[to]));
   GT_CUDA(cudaEventElapsedTime(ms, ctx->marks[from], ctx->marks[to]));
   return nullptr;
+}
+
+// ---- events and the copy stream ---------------------------------------------
+
+struct gt_event {
+  cudaEvent_t ev = nullptr;
+};
+
+static cudaStream_t stream_of(gt_ctx* ctx, int which) {
+  switch (which) {
+    case GT_STREAM_COMPUTE: return ctx->stream;
+    case GT_STREAM_COPY: return ctx->copy_stream;
+    case GT_STREAM_COMM: return ctx->comm_stream;
+    default: return nullptr;
+  }
+}
+
+char* gt_event_new(gt_ctx* ctx, gt_event** out) {
+  GT_ENTER(ctx);
+  if (!out) return gt::errorf("gt_event_new: null output");
+  auto* e = new gt_event();
+  cudaError_t r = cudaEventCreateWithFlags(&e->ev, cudaEventDisableTiming);
+  if (r != cudaSuccess) {
+    delete e;
+    return gt::cuda_error(r, "cudaEventCreateWithFlags", __FILE__, __LINE__);
+  }
+  *out = e;
+  return nullptr;
+}
+
+void gt_event_free(gt_event* e) {
+  if (!e) return;
+  if (e->ev) cudaEventDestroy(e->ev);
+  delete e;
+}
+
+char* gt_event_record(gt_ctx* ctx, gt_event* e, int stream) {
+  GT_ENTER(ctx);
+  cudaStream_t st = stream_of(ctx, stream);
+  if (!e || !st) return gt::errorf("gt_event_record: bad event or stream %d", stream);
+  GT_CUDA(cudaEventRecord(e->ev, st));
+  return nullptr;
+}
+
+char* gt_stream_wait_event(gt_ctx* ctx, int stream, gt_event* e) {
+  GT_ENTER(ctx);
+  cudaStream_t st = stream_of(ctx, stream);
+  if (!e || !st) return gt::errorf("gt_stream_wait_event: bad event or stream %d", stream);
+  GT_CUDA(cudaStreamWaitEvent(st, e->ev, 0));
+  return nullptr;
+}
+
+char* gt_upload_on(gt_ctx* ctx, int stream, void* dst, const void* src, size_t bytes) {
+  GT_ENTER(ctx);
+  cudaStream_t st = stream_of(ctx, stream);
+  if (!st) return gt::errorf("gt_upload_on: bad stream %d", stream);
+  if (bytes == 0) return nullptr;
+  if (!dst || !src) return gt::errorf("gt_upload_on: null pointer");
+  GT_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st));
+  return nullptr;
+}
+
+char* gt_host_alloc(size_t bytes, void** out) {
+  if (!out) return gt::errorf("gt_host_alloc: null output");
+  *out = nullptr;
+  GT_CUDA(cudaHostAlloc(out, bytes ? bytes : 1, cudaHostAllocPortable));
+  return nullptr;
+}
+
+void gt_host_free(void* p) {
+  if (p) cudaFreeHost(p);
 }
 
 }  // extern "C"

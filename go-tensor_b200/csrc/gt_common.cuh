@@ -18,6 +18,7 @@ struct gt_ctx {
   int sm_count = 0;
   cudaStream_t stream = nullptr;       // all compute work
   cudaStream_t comm_stream = nullptr;  // gradient all-reduce
+  cudaStream_t copy_stream = nullptr;  // host -> device copies that overlap compute
   cudaMemPool_t pool = nullptr;
   char name[256] = {0};
   void* nccl = nullptr;  // ncclComm_t

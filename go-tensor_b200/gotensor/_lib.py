@@ -108,6 +108,13 @@ CUDA_API = {
     "gt_graph_free": (None, [_P]),
     "gt_mark": ("err", [_P, _INT]),
     "gt_elapsed_ms": ("err", [_P, _INT, _INT, ctypes.POINTER(ctypes.c_float)]),
+    "gt_event_new": ("err", [_P, ctypes.POINTER(_P)]),
+    "gt_event_free": (None, [_P]),
+    "gt_event_record": ("err", [_P, _P, _INT]),
+    "gt_stream_wait_event": ("err", [_P, _INT, _P]),
+    "gt_upload_on": ("err", [_P, _INT, _P, _P, ctypes.c_size_t]),
+    "gt_host_alloc": ("err", [ctypes.c_size_t, ctypes.POINTER(_P)]),
+    "gt_host_free": (None, [_P]),
     "gt_launch_count": (_I64, []),
     "gt_gemm_timer_start": ("err", [_P, _I64]),
     "gt_gemm_timer_stop": ("err", [_P]),
@@ -135,6 +142,7 @@ HOST_API = {
     "gth_input_device": (_P, [_P]),
     "gth_labels_device": (_P, [_P]),
     "gth_loss_device": (_P, [_P]),
+    "gth_stage_batch": ("err", [_P, _P, _P]),
     "gth_forward_backward": ("err", [_P]),
     "gth_optimizer_step": ("err", [_P]),
     "gth_train_step": ("err", [_P]),

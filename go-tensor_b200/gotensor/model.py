@@ -168,6 +168,14 @@ class Model:
         check(lib.gt_upload(self.ctx.ptr, self.input_device, x.ctypes.data, x.nbytes))
         check(lib.gt_upload(self.ctx.ptr, self.labels_device, y.ctypes.data, y.nbytes))
 
+    def stage_batch(self, x_ptr: int, labels_ptr: int) -> None:
+        """Queues the upload of the batch at host addresses x_ptr (input
+        shape, model dtype) and labels_ptr (int32) on the copy stream; it
+        overlaps the step in flight and is read by the next unstaged step.
+        Pinned host memory (e.g. torch's pin_memory) makes it asynchronous; it
+        must stay unchanged until that step has run."""
+        check(self.lib.gth_stage_batch(self.ptr, x_ptr, labels_ptr))
+
     @property
     def classes(self) -> int:
         last = [s for _, s, _ in self.params][-1]

@@ -95,6 +95,9 @@ GT_API char* gth_set_adam(gth_model* m, const gt_adam_cfg* cfg) {
 GT_API void* gth_input_device(gth_model* m) { return m->m->input_device(); }
 GT_API int32_t* gth_labels_device(gth_model* m) { return m->m->labels_device(); }
 GT_API void* gth_loss_device(gth_model* m) { return m->m->loss_device(); }
+GT_API char* gth_stage_batch(gth_model* m, const void* x, const int32_t* labels) {
+  return guard([&] { m->m->stage_batch(x, labels); });
+}
 
 GT_API char* gth_forward_backward(gth_model* m) { return guard([&] { m->m->forward_backward(); }); }
 GT_API char* gth_optimizer_step(gth_model* m) { return guard([&] { m->m->optimizer_step(); }); }

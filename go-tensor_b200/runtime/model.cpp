@@ -62,23 +62,75 @@ Model::Model(gt_ctx* ctx, int dtype, const std::vector<gth_layer>& layers, const
   if (dtype != GT_FLOAT32 && dtype != GT_FLOAT64) throw Error("gth_model_new: unknown dtype");
   if (input_shape.empty() || input_shape[0] <= 0) throw Error("gth_model_new: input shape needs a batch dimension");
   plan(layers, input_shape);
+  for (int p = 0; p < 2; p++) {
+    check(gt_event_new(ctx_, &ready_[p]));
+    check(gt_event_new(ctx_, &free_[p]));
+  }
 }
 
-Model::~Model() { drop_graph(); }
+Model::~Model() {
+  drop_graph();
+  for (int p = 0; p < 2; p++) {
+    gt_event_free(ready_[p]);
+    gt_event_free(free_[p]);
+  }
+}
 
 void Model::drop_graph() {
-  if (graph_) gt_graph_free(graph_);
-  graph_ = nullptr;
+  for (auto& g : graph_) {
+    if (g) gt_graph_free(g);
+    g = nullptr;
+  }
+}
+
+void Model::bind_input(int p) {
+  void* x = input_[p].get();
+  for (auto& r : input_refs_) {
+    if (r.second == 0)
+      ops_[r.first].in = x;
+    else
+      ops_[r.first].out = x;
+  }
+}
+
+void Model::begin_read() {
+  if (staged_[cur_]) {
+    check(gt_stream_wait_event(ctx_, GT_STREAM_COMPUTE, ready_[cur_]));
+    staged_[cur_] = false;
+  }
+  bind_input(cur_);
+}
+
+// Records that the step reading pair cur_ has been queued and moves on to the
+// other pair if a batch has been staged there; otherwise the next step reads
+// the same buffers again (a batch written once serves any number of steps).
+void Model::end_read() {
+  check(gt_event_record(ctx_, free_[cur_], GT_STREAM_COMPUTE));
+  if (staged_[cur_ ^ 1]) cur_ ^= 1;
+}
+
+void Model::stage_batch(const void* x, const int32_t* labels) {
+  if (!x || !labels) throw Error("gth_stage_batch: null batch");
+  const int s = !staged_[cur_] ? cur_ : !staged_[cur_ ^ 1] ? (cur_ ^ 1) : -1;
+  if (s < 0) throw Error("gth_stage_batch: two batches are already staged; run a step first");
+  check(gt_stream_wait_event(ctx_, GT_STREAM_COPY, free_[s]));
+  check(gt_upload_on(ctx_, GT_STREAM_COPY, input_[s].get(), x, input_bytes_));
+  check(gt_upload_on(ctx_, GT_STREAM_COPY, labels_[s].get(), labels, batch_ * sizeof(int32_t)));
+  check(gt_event_record(ctx_, ready_[s], GT_STREAM_COPY));
+  staged_[s] = true;
 }
 
 void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t>& input_shape) {
   batch_ = input_shape[0];
-  input_ = DevBuf(ctx_, numel(input_shape) * es_);
-  labels_ = DevBuf(ctx_, batch_ * sizeof(int32_t));
+  input_bytes_ = numel(input_shape) * es_;
+  for (int p = 0; p < 2; p++) {
+    input_[p] = DevBuf(ctx_, input_bytes_);
+    labels_[p] = DevBuf(ctx_, batch_ * sizeof(int32_t));
+  }
   loss_ = DevBuf(ctx_, 64);
 
   std::vector<int64_t> shape = input_shape;
-  const void* cur = input_.get();
+  const void* cur = input_[0].get();
   bool cur_is_act = false;  // cur holds an activation output
   int cur_act = GT_ACT_NONE;
   bool seen_params = false;
@@ -203,6 +255,10 @@ void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t
     cur_act = op.produces_act ? op.act : GT_ACT_NONE;
     shape = op.out_shape;
     ops_.push_back(op);
+  }
+  for (size_t i = 0; i < ops_.size(); i++) {  // the ops that read (or alias) the batch
+    if (ops_[i].in == input_[0].get()) input_refs_.emplace_back((int)i, 0);
+    if (ops_[i].out == input_[0].get()) input_refs_.emplace_back((int)i, 1);
   }
   if (shape.size() != 2) throw Error("the model must end in (batch, classes) logits, got " + shape_str(shape));
   if (!seen_params) throw Error("the model has no parameters");
@@ -361,8 +417,10 @@ void Model::backward() {
 }
 
 void Model::forward_backward() {
+  begin_read();
   forward();
   backward();
+  end_read();
 }
 
 void Model::optimizer_step() {
@@ -378,33 +436,38 @@ void Model::optimizer_step() {
 
 void Model::train_step() {
   if (opt_ == OPT_NONE) throw Error("no optimizer: call gth_set_sgd or gth_set_adam");
-  if (use_graph_ && graph_) {
-    check(gt_graph_launch(ctx_, graph_));
+  const int p = cur_;
+  begin_read();  // outside any capture: the wait for a staged upload is per step
+  if (use_graph_ && graph_[p]) {
+    check(gt_graph_launch(ctx_, graph_[p]));
     opt_steps_++;
-    return;
-  }
-  // The first SGD step initialises the velocity, so capture from the second.
-  bool capture = use_graph_ && opt_steps_ >= 1;
-  int64_t before = gt_launch_count();
-  if (capture) check(gt_capture_begin(ctx_));
-  try {
-    forward_backward();
-    optimizer_step();
-  } catch (...) {
-    if (capture) {
-      gt_graph* g = nullptr;
-      gt_free_error(gt_capture_end(ctx_, &g));
-      gt_graph_free(g);
+  } else {
+    // The first SGD step initialises the velocity, so capture from the second
+    // (a graph per input pair, each reading its own buffers).
+    bool capture = use_graph_ && opt_steps_ >= 1;
+    int64_t before = gt_launch_count();
+    if (capture) check(gt_capture_begin(ctx_));
+    try {
+      forward();
+      backward();
+      optimizer_step();
+    } catch (...) {
+      if (capture) {
+        gt_graph* g = nullptr;
+        gt_free_error(gt_capture_end(ctx_, &g));
+        gt_graph_free(g);
+      }
+      throw;
     }
-    throw;
+    launches_ = (int)(gt_launch_count() - before);
+    if (capture) {
+      check(gt_capture_end(ctx_, &graph_[p]));
+      opt_steps_--;  // the captured step has not run yet
+      check(gt_graph_launch(ctx_, graph_[p]));
+      opt_steps_++;
+    }
   }
-  launches_ = (int)(gt_launch_count() - before);
-  if (capture) {
-    check(gt_capture_end(ctx_, &graph_));
-    opt_steps_--;  // the captured step has not run yet
-    check(gt_graph_launch(ctx_, graph_));
-    opt_steps_++;
-  }
+  end_read();
 }
 
 void Model::enable_graph(bool on) {
@@ -425,7 +488,9 @@ double Model::loss() {
 }
 
 void Model::forward_eval(void* logits_host) {
+  begin_read();
   forward();
+  end_read();
   check(gt_download(ctx_, logits_host, ops_.back().out, batch_ * classes_ * es_));
 }
 

@@ -102,9 +102,13 @@ class Model {
   void set_sgd(const gt_sgd_cfg& cfg);
   void set_adam(const gt_adam_cfg& cfg);
 
-  void* input_device() const { return input_.get(); }
-  int32_t* labels_device() const { return (int32_t*)labels_.get(); }
+  // The input and label buffers the next step reads.
+  void* input_device() const { return input_[cur_].get(); }
+  int32_t* labels_device() const { return (int32_t*)labels_[cur_].get(); }
   void* loss_device() const { return loss_.get(); }
+  // Queues the upload of a batch on the copy stream into the buffer pair
+  // that the first step without a staged batch will read.
+  void stage_batch(const void* x, const int32_t* labels);
 
   void forward_backward();
   void optimizer_step();
@@ -122,6 +126,9 @@ class Model {
   void backward();
   void issue_ready_buckets(int64_t boundary);
   void drop_graph();
+  void bind_input(int p);  // points the plan at input/label buffer pair p
+  void begin_read();       // before a step reads pair cur_: wait for its staged upload
+  void end_read();         // after it: the pair is free once the step is done; move to a staged pair
 
   gt_ctx* ctx_;
   int dtype_;
@@ -133,7 +140,16 @@ class Model {
   int64_t dense_params_ = 0, dev_params_ = 0;
   std::vector<DevBuf> acts_;  // activation buffers owned by ops
   DevBuf pbuf_, gbuf_, opt_a_, opt_b_, step_dev_;
-  DevBuf input_, labels_, loss_, grad_a_, grad_b_;
+  // Two input/label buffer pairs: while a step reads one, the next batch can
+  // be uploaded into the other on the copy stream.
+  DevBuf input_[2], labels_[2];
+  int cur_ = 0;                      // pair the next step reads
+  bool staged_[2] = {false, false};  // an upload into the pair is queued and not yet waited for
+  gt_event* ready_[2] = {};          // copy stream: the pair's upload is done
+  gt_event* free_[2] = {};           // compute stream: the last step reading the pair is done
+  std::vector<std::pair<int, int>> input_refs_;  // (op, 0 = in / 1 = out) that point at the input
+  int64_t input_bytes_ = 0;
+  DevBuf loss_, grad_a_, grad_b_;
   int64_t grad_elems_ = 0;
 
   enum { OPT_NONE, OPT_SGD, OPT_ADAM } opt_ = OPT_NONE;
@@ -146,7 +162,7 @@ class Model {
   size_t next_bucket_ = 0;
 
   bool use_graph_ = false;
-  gt_graph* graph_ = nullptr;
+  gt_graph* graph_[2] = {};  // the captured step for each input pair
   int launches_ = 0;
 };
 

@@ -283,6 +283,30 @@ GT_API void gt_graph_free(gt_graph* graph);
 GT_API char* gt_mark(gt_ctx* ctx, int slot);
 GT_API char* gt_elapsed_ms(gt_ctx* ctx, int from, int to, float* ms);
 
+/* ---- overlapping uploads ------------------------------------------------- */
+/* A context has three streams: compute (every kernel), copy (uploads that
+ * overlap compute) and comm (gradient all-reduce). Events order one stream
+ * after another, so a host can upload the next batch on the copy stream while
+ * the compute stream runs the current step (no counterpart in the reference,
+ * whose CPU path has no streams). */
+#define GT_STREAM_COMPUTE 0
+#define GT_STREAM_COPY 1
+#define GT_STREAM_COMM 2
+typedef struct gt_event gt_event;
+GT_API char* gt_event_new(gt_ctx* ctx, gt_event** out);
+GT_API void gt_event_free(gt_event* e);
+/* Marks the current end of `stream`'s queued work. */
+GT_API char* gt_event_record(gt_ctx* ctx, gt_event* e, int stream);
+/* Work queued on `stream` after this call waits for the event's point (an
+ * event never recorded is already complete). */
+GT_API char* gt_stream_wait_event(gt_ctx* ctx, int stream, gt_event* e);
+/* Host -> device copy queued on `stream`; asynchronous for pinned host
+ * memory (gt_host_alloc), which must stay unchanged until the copy is done. */
+GT_API char* gt_upload_on(gt_ctx* ctx, int stream, void* dst, const void* src, size_t bytes);
+/* Page-locked host memory for asynchronous uploads and downloads. */
+GT_API char* gt_host_alloc(size_t bytes, void** out);
+GT_API void gt_host_free(void* p);
+
 /* Number of kernels this library has launched (or recorded into a graph) in
  * the process so far. */
 GT_API int64_t gt_launch_count(void);

@@ -71,10 +71,21 @@ GT_API void* gth_grads_device(gth_model* m);
 GT_API char* gth_set_sgd(gth_model* m, const gt_sgd_cfg* cfg);
 GT_API char* gth_set_adam(gth_model* m, const gt_adam_cfg* cfg);
 
-/* Device buffers the step reads: the input batch (input_shape, model dtype)
- * and the labels (batch int32). */
+/* Device buffers the next step reads: the input batch (input_shape, model
+ * dtype) and the labels (batch int32). The model has two such pairs; a step
+ * moves on to the other pair only when a batch has been staged into it
+ * (gth_stage_batch), so without staging these pointers never change and a
+ * batch written once serves every following step. */
 GT_API void* gth_input_device(gth_model* m);
 GT_API int32_t* gth_labels_device(gth_model* m);
+/* Queues the upload of a host batch (x: input_shape in the model dtype,
+ * labels: batch int32) on the context's copy stream, into the pair that the
+ * first step without a staged batch will read (at most two batches staged).
+ * The copy waits for the last step that read that pair and overlaps the step
+ * in flight; the step that reads it waits for the copy. Asynchronous for
+ * pinned host memory (gt_host_alloc), which must stay unchanged until that
+ * step has run. The data loader's host-to-device hop (data/data.go:60-84). */
+GT_API char* gth_stage_batch(gth_model* m, const void* x, const int32_t* labels);
 /* Device scalar (model dtype) holding the last loss. */
 GT_API void* gth_loss_device(gth_model* m);
 

@@ -146,6 +146,61 @@ def test_graph_replay_is_bitwise_eager(name):
     assert graph.step_launches > 0
 
 
+@pytest.mark.parametrize("name", ["wide_mlp_small_sgd", "cnn28_b32_adam"])
+@pytest.mark.parametrize("graph", [False, True])
+def test_staged_batches_match_synchronous_uploads(name, graph):
+    """Batches uploaded on the copy stream one step ahead (gth_stage_batch,
+    pinned host memory, two device buffer pairs) train exactly like batches
+    written synchronously before each step: same losses and weights, bit for
+    bit, over six different batches."""
+    import ctypes
+
+    from gotensor._lib import check, cuda_lib
+    _, _, sync, _, _, _ = make_case(name, 3)
+    _, _, staged, _, _, _ = make_case(name, 3)
+    sync.enable_graph(graph)
+    staged.enable_graph(graph)
+    spec, shape, ncls, dt, _, _ = CASES[name]
+    npdt = np.float64 if dt == T.Float64 else np.float32
+    rng = np.random.default_rng(11)
+    batches = [(rng.standard_normal(shape).astype(npdt), rng.integers(0, ncls, shape[0]).astype(np.int32))
+               for _ in range(6)]
+    lib = cuda_lib()
+    pinned = []
+    for x, y in batches:  # one pinned buffer per batch: staged data must stay put until its step ran
+        px, py = ctypes.c_void_p(), ctypes.c_void_p()
+        check(lib.gt_host_alloc(x.nbytes, ctypes.byref(px)))
+        check(lib.gt_host_alloc(y.nbytes, ctypes.byref(py)))
+        ctypes.memmove(px, x.ctypes.data, x.nbytes)
+        ctypes.memmove(py, y.ctypes.data, y.nbytes)
+        pinned.append((px, py))
+    try:
+        want, got = [], []
+        for x, y in batches:
+            sync.set_batch(x, y)
+            sync.train_step()
+            want.append(sync.loss())
+        staged.stage_batch(pinned[0][0].value, pinned[0][1].value)
+        for i in range(len(batches)):
+            if i + 1 < len(batches):
+                staged.stage_batch(pinned[i + 1][0].value, pinned[i + 1][1].value)
+            staged.train_step()
+            got.append(staged.loss())
+        assert got == want
+        assert np.array_equal(sync.flat_params(), staged.flat_params())
+        # a third staged batch without a step in between is refused
+        staged.stage_batch(pinned[0][0].value, pinned[0][1].value)
+        staged.stage_batch(pinned[1][0].value, pinned[1][1].value)
+        with pytest.raises(Exception, match="already staged"):
+            staged.stage_batch(pinned[2][0].value, pinned[2][1].value)
+        staged.ctx.sync()
+    finally:
+        staged.ctx.sync()
+        for px, py in pinned:
+            lib.gt_host_free(px)
+            lib.gt_host_free(py)
+
+
 WIDE_C2 = [gm.Linear(4096, 4096), gm.ReLU(), gm.Linear(4096, 4096), gm.ReLU(), gm.Linear(4096, 1000)]
 
 
