@@ -64,7 +64,12 @@ def clocks_sampler(index: int):
         p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={CLOCK_FIELDS}",
                               "--format=csv,noheader,nounits", "-lms", "50"], stdout=out, stderr=subprocess.DEVNULL)
     except OSError:
-        p = None
+        return None, out.name
+    # NVML's start-up can hold the driver for a moment; let it finish (first
+    # sample written) before anything is timed.
+    deadline = time.time() + 10
+    while time.time() < deadline and p.poll() is None and os.path.getsize(out.name) == 0:
+        time.sleep(0.05)
     return p, out.name
 
 

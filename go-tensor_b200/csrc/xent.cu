@@ -23,11 +23,7 @@
 
 namespace gt {
 
-// One warp per row. R > 0: the row (C <= 32 * R) is read into registers
-// once, element j = lane + 32 k in slot k, so every pass after the first read
-// works from registers in the same per-lane order as the R == 0 form, which
-// streams the row from memory in each pass (any C).
-template <typename T, int R>
+template <typename T>
 __global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restrict__ labels, int64_t B, int64_t C,
                                  T c, T* __restrict__ row_terms, T* __restrict__ dx, int32_t* bad_label) {
   const int lane = threadIdx.x & 31;
@@ -38,32 +34,12 @@ __global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restr
     int32_t y = labels[i];
     bool bad = y < 0 || y >= C;
     if (bad && lane == 0 && bad_label) *bad_label = 1;
-    T v[R > 0 ? R : 1];
-    if (R > 0) {
-#pragma unroll
-      for (int k = 0; k < R; k++) {
-        const int64_t j = lane + 32 * k;
-        v[k] = j < C ? xr[j] : (T)0;
-      }
-    }
     T m = (T)(-INFINITY);
-    if (R > 0) {
-#pragma unroll
-      for (int k = 0; k < R; k++)
-        if (lane + 32 * k < C) m = go_max(m, v[k]);
-    } else {
-      for (int64_t j = lane; j < C; j += 32) m = go_max(m, xr[j]);
-    }
+    for (int64_t j = lane; j < C; j += 32) m = go_max(m, xr[j]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = go_max(m, __shfl_xor_sync(0xffffffffu, m, off));
     T S = (T)0;
-    if (R > 0) {
-#pragma unroll
-      for (int k = 0; k < R; k++)
-        if (lane + 32 * k < C) S = add_rn(S, (T)exp((double)sub_rn(v[k], m)));
-    } else {
-      for (int64_t j = lane; j < C; j += 32) S = add_rn(S, (T)exp((double)sub_rn(xr[j], m)));
-    }
+    for (int64_t j = lane; j < C; j += 32) S = add_rn(S, (T)exp((double)sub_rn(xr[j], m)));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) S = add_rn(S, __shfl_xor_sync(0xffffffffu, S, off));
     T Lse = (T)log((double)S);
@@ -72,26 +48,19 @@ __global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restr
     bool nonfinite = false;
     T picked = (T)0;
     T q = div_rn(c, S);
-    auto visit = [&](int64_t j, T xj) {
-      T sj = sub_rn(xj, m);
-      T lp = sub_rn(sj, Lse);
+    for (int64_t j = lane; j < C; j += 32) {
+      T s = sub_rn(xr[j], m);
+      T lp = sub_rn(s, Lse);
       if (j == y) {
         picked = lp;
       } else if (!isfinite(lp)) {
         nonfinite = true;
       }
       if (dx) {
-        T e = (T)exp((double)sj);
+        T e = (T)exp((double)s);
         T g = mul_rn(q, e);
         dx[i * C + j] = j == y ? add_rn(-c, g) : g;
       }
-    };
-    if (R > 0) {
-#pragma unroll
-      for (int k = 0; k < R; k++)
-        if (lane + 32 * k < C) visit(lane + 32 * k, v[k]);
-    } else {
-      for (int64_t j = lane; j < C; j += 32) visit(j, xr[j]);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -100,32 +69,6 @@ __global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restr
     }
     if (lane == 0) row_terms[i] = (nonfinite || bad) ? (T)NAN : picked;
   }
-}
-
-// Launches the row kernel with the smallest register row that holds C.
-template <typename T>
-static void launch_rows(gt_ctx* ctx, const T* x, const int32_t* labels, int64_t B, int64_t C, T c, T* terms, T* dx,
-                        int32_t* bad) {
-  const int grid = grid_for(ctx, B * 32, 256);
-  const int max_r = sizeof(T) == 8 ? 16 : 32;
-#define GT_XENT_ROWS(RR) \
-  xent_rows_kernel<T, RR><<<grid, 256, 0, ctx->stream>>>(x, labels, B, C, c, terms, dx, bad)
-  if (C <= 32 && max_r >= 1) {
-    GT_XENT_ROWS(1);
-  } else if (C <= 64) {
-    GT_XENT_ROWS(2);
-  } else if (C <= 128) {
-    GT_XENT_ROWS(4);
-  } else if (C <= 256) {
-    GT_XENT_ROWS(8);
-  } else if (C <= 512) {
-    GT_XENT_ROWS(16);
-  } else if (C <= 1024 && max_r >= 32) {
-    if constexpr (sizeof(T) == 4) GT_XENT_ROWS(32);
-  } else {
-    GT_XENT_ROWS(0);
-  }
-#undef GT_XENT_ROWS
 }
 
 // loss = -(sum_i row_terms[i] * c), one block, fixed reduction order.
@@ -188,7 +131,8 @@ extern "C" char* gt_xent_fwd_bwd_noalloc(gt_ctx* ctx, int dtype, const void* log
   GT_TRY(xent_rows_buffer(ctx, &terms));
   GT_DISPATCH(dtype, {
     T c = (T)(1.0 / (double)B);
-    launch_rows<T>(ctx, (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
+    xent_rows_kernel<T><<<grid_for(ctx, B * 32, 256), 256, 0, ctx->stream>>>(
+        (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
     xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
   });
   count_launch(2);
@@ -207,7 +151,8 @@ extern "C" char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, con
   GT_TRY(scratch(ctx, B * es, &terms));
   GT_DISPATCH(dtype, {
     T c = (T)(1.0 / (double)B);  // MulScalar(1/float64(N)) rounds the scalar to T
-    launch_rows<T>(ctx, (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
+    xent_rows_kernel<T><<<grid_for(ctx, B * 32, 256), 256, 0, ctx->stream>>>(
+        (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
     xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
   });
   count_launch(2);
