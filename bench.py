@@ -214,6 +214,9 @@ def run_ours(args):
     model.load_state_dict(sd)
     model.sgd(LR, MOM, WD)
     if world > 1:
+        # rank 0's stdout carries exactly one JSON line: keep NCCL's version banner off it
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         model.dp_init(rank, world, exchange_unique_id(rank), timeout_ms=120000, bucket_bytes=args.bucket_mb << 20)
     model.enable_graph(not args.no_graph)
 

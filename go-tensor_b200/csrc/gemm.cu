@@ -88,6 +88,7 @@ using namespace gt;
 extern "C" {
 
 void gt_debug_set_gemm_path(int path) { set_gemm_path(path); }
+void gt_debug_set_gemm_splits(int splits) { set_gemm_splits(splits < 0 ? 0 : splits); }
 int gt_gemm_path_taken(void) { return g_gemm_taken; }
 
 char* gt_gemm_timer_start(gt_ctx* ctx, int64_t capacity) {

@@ -68,5 +68,6 @@ char* gemm(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>
 // shape does not qualify).
 void set_gemm_path(int path);
 int gemm_path();
+void set_gemm_splits(int splits);  // tcgen05 path: 0 = automatic, else this many K-splits
 
 }  // namespace gt

@@ -42,6 +42,9 @@
 // closing cluster barrier is always reached by every thread.
 #include <cuda.h>
 
+#include <algorithm>
+#include <cmath>
+
 #include "gemm.cuh"
 
 namespace gt {
@@ -293,14 +296,18 @@ enum EpiKind : int {
   EK_PLAIN = 0,      // C stored row-major
   EK_BIAS_RELU = 1,  // + bias[n] (optional), then ReLU (optional): Linear forward
   EK_MASK = 2,       // * act'(mask[m][n]): the dX of a Linear after an activation
-  EK_GENERIC = 3,    // anything else (tanh/sigmoid forward, bias by row, NCHW order)
+  EK_CONV = 3,       // + bias[m] (optional), then ReLU (optional), stored in NCHW order: Conv2d forward
+  EK_GENERIC = 4,    // anything else (tanh / sigmoid forward)
 };
 
-inline int epi_kind(const Epi<float>& e) {
+inline int epi_kind(const Epi<float>& e, int64_t n_cols) {
   const bool rowmajor = e.nchw_L == 0;
   if (!e.bias && e.act == GT_ACT_NONE && !e.dmask && rowmajor) return EK_PLAIN;
   if (!e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask && rowmajor) return EK_BIAS_RELU;
   if (!e.bias && e.act == GT_ACT_NONE && e.dmask && rowmajor) return EK_MASK;
+  if ((!e.bias || e.bias_by_row) && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask && !rowmajor &&
+      e.nchw_L < (1ll << 31) && n_cols < (1ll << 31))
+    return EK_CONV;  // positions fit 32-bit arithmetic
   return EK_GENERIC;
 }
 
@@ -309,10 +316,10 @@ inline int epi_kind(const Epi<float>& e) {
 // bytes. Same operations, in the same order, as Epi::store.
 template <int EK>
 __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const GemmShape& s, const float* xpose, int lane,
-                                               int64_t m0, int64_t n) {
+                                               int64_t m0, int64_t n, int64_t out_offset) {
   if (n >= s.N) return;
   const int rows = (int)(s.M - m0 < 32 ? s.M - m0 : 32);
-  float* op = epi.out + m0 * epi.ldc + n;
+  float* op = epi.out + out_offset + m0 * epi.ldc + n;
   if (EK == EK_PLAIN) {
 #pragma unroll 4
     for (int r = 0; r < rows; r++) op[r * epi.ldc] = xpose[r * EPI_LD + lane];
@@ -338,10 +345,36 @@ __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const Gemm
       for (int r = 0; r < 8; r++)
         if (r0 + r < rows) op[(r0 + r) * epi.ldc] = act_bwd(epi.dact, xpose[(r0 + r) * EPI_LD + lane], mask[r]);
     }
+  } else if (EK == EK_CONV) {
+    // C(m, n) -> out[((n / L) * M + m) * L + n % L]: a warp's row is 32
+    // consecutive positions of one channel plane (image boundaries aside).
+    const uint32_t L32 = (uint32_t)epi.nchw_L, img = (uint32_t)n / L32;
+    const int64_t L = epi.nchw_L;
+    float* base = epi.out + (int64_t)img * epi.nchw_M * L + ((uint32_t)n - img * L32);
+    const bool relu = epi.act == GT_ACT_RELU;
+#pragma unroll 4
+    for (int r = 0; r < rows; r++) {
+      const int64_t m = m0 + r;
+      float v = xpose[r * EPI_LD + lane];
+      if (epi.bias) v = __fadd_rn(v, __ldg(epi.bias + m));
+      if (relu) v = go_max(v, 0.0f);
+      base[m * L] = v;
+    }
   } else {
 #pragma unroll 1
     for (int r = 0; r < rows; r++) epi.store(m0 + r, n, xpose[r * EPI_LD + lane]);
   }
+}
+
+// Work unit u of a launch with `splits` K-splits: tile t (of `tiles`) over
+// K-slices [kb, ke); the splits of one tile are `tiles` units apart, so the
+// units running at the same time share operand panels of one K range.
+__device__ __forceinline__ int unit_of(int u, int tiles, int splits, int num_k, int& t, int& kb, int& ke) {
+  const int sidx = u / tiles;
+  t = u - sidx * tiles;
+  kb = (int)((int64_t)sidx * num_k / splits);
+  ke = (int)((int64_t)(sidx + 1) * num_k / splits);
+  return sidx;
 }
 
 struct Shared {
@@ -358,7 +391,7 @@ struct Shared {
 template <bool A_MN, bool B_MN, int EK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            GemmShape s, Epi<float> epi) {
+                            GemmShape s, Epi<float> epi, int splits, int64_t split_stride) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   Shared* sh = (Shared*)(smem + BAR_OFFSET);
@@ -371,6 +404,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int m_tiles = (int)((s.M + 2 * BM - 1) / (2 * BM));
   const int n_tiles = (int)((s.N + BN - 1) / BN);
   const int tiles = m_tiles * n_tiles;
+  const int units = tiles * splits;  // splits > 1: each unit writes a partial at out + split * split_stride
   const int pair = (int)cluster_id(), pairs = (int)num_clusters();
 
   if (threadIdx.x == 0) {
@@ -405,11 +439,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     if (warp == 0) {
       if (lane == 0) {  // ---- TMA producer (both CTAs)
         int it = 0, issued_to = 0;
-        for (int t = pair; t < tiles && !*failed; t += pairs) {
+        for (int u = pair; u < units && !*failed; u += pairs) {
+          int t, kb, ke;
+          unit_of(u, tiles, splits, num_k, t, kb, ke);
           const int mt = t / n_tiles, nt = t % n_tiles;
           const int a_row = mt * 2 * BM + (int)rank * BM;
           const int b_row = nt * BN + (int)rank * BNH;
-          for (int kt = 0; kt < num_k; kt++, it++) {
+          for (int kt = kb; kt < ke; kt++, it++) {
             const int st = it % STAGES;
             if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1)) {
               *failed = 1;
@@ -445,9 +481,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const uint32_t idesc = instr_desc<A_MN, B_MN>();
         int it = 0, group = 0;
         bool stop = false;
-        for (int t = pair; t < tiles && !stop; t += pairs) {
-          for (int kt = 0; kt < num_k; kt++, it++) {
-            const bool group_start = kt % GROUP == 0;
+        for (int u = pair; u < units && !stop; u += pairs) {
+          int t, kb, ke;
+          unit_of(u, tiles, splits, num_k, t, kb, ke);
+          for (int kt = kb; kt < ke; kt++, it++) {
+            const bool group_start = (kt - kb) % GROUP == 0;
             const uint32_t buf = (uint32_t)(group & 1);
             if (group_start) {  // the promoters must have read this buffer's previous partial
               if (!mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2)) {
@@ -474,7 +512,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               mma_tf32_pair(d, dah, dbh, idesc, 1u);
             }
             mma_commit_pair(&sh->empty[st]);  // frees the slot in both CTAs
-            if (kt % GROUP == GROUP - 1 || kt == num_k - 1) {
+            if ((kt - kb) % GROUP == GROUP - 1 || kt == ke - 1) {
               mma_commit_pair(&sh->pfull[buf]);
               group++;
             }
@@ -491,7 +529,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       // ---- splitters (both CTAs): this warp owns ring slot st, i.e. every
       // STAGES-th slice, starting with slice st.
       const int st = warp - SPLIT_WARP0;
-      const int total = ((tiles - pair + pairs - 1) / pairs) * num_k;  // slices this pair streams
+      int total = 0;  // slices this pair streams
+      for (int u = pair; u < units; u += pairs) {
+        int t, kb, ke;
+        unit_of(u, tiles, splits, num_k, t, kb, ke);
+        total += ke - kb;
+      }
       for (int it = st; it < total; it += STAGES) {
         if (__shfl_sync(0xffffffffu, *failed, 0)) break;
         if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4)) {
@@ -513,9 +556,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int q = warp & 3, h = (warp - 8) >> 2;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + 128 * h;
     float* xpose = (float*)(smem + EPI_OFFSET) + (warp - 8) * 32 * EPI_LD;
-    const int groups = (num_k + GROUP - 1) / GROUP;
     int group = 0;
-    for (int t = pair; t < tiles && !__shfl_sync(0xffffffffu, *failed, 0); t += pairs) {
+    for (int u = pair; u < units && !__shfl_sync(0xffffffffu, *failed, 0); u += pairs) {
+      int t, kb, ke;
+      const int sidx = unit_of(u, tiles, splits, num_k, t, kb, ke);
+      const int groups = (ke - kb + GROUP - 1) / GROUP;
       const int mt = t / n_tiles, nt = t % n_tiles;
       // The running total starts at +0 and every partial is added with
       // round-to-nearest, like the reference's c = 0; c += a*b.
@@ -561,7 +606,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #undef GT_XPOSE_CASE
         }
         __syncwarp();
-        epilogue_block<EK>(epi, s, xpose, lane, m0, (int64_t)nt * BN + 128 * h + 32 * j + lane);
+        epilogue_block<EK>(epi, s, xpose, lane, m0, (int64_t)nt * BN + 128 * h + 32 * j + lane, sidx * split_stride);
         __syncwarp();
       }
     }
@@ -600,7 +645,8 @@ static char* make_map(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t 
 }
 
 template <bool A_MN, bool B_MN, int EK>
-static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {
+static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
+                    int splits, int64_t split_stride) {
   CUtensorMap ta, tb;
   if (A_MN)
     GT_TRY(make_map(ctx, &ta, A, s.M, s.K, s.lda, true));
@@ -616,28 +662,71 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
     GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
   }
-  const int64_t tiles = ceil_div(s.M, 2 * BM) * ceil_div(s.N, BN);
-  const int64_t pairs = tiles < ctx->sm_count / 2 ? tiles : ctx->sm_count / 2;
+  const int64_t units = ceil_div(s.M, 2 * BM) * ceil_div(s.N, BN) * splits;
+  const int64_t pairs = units < ctx->sm_count / 2 ? units : ctx->sm_count / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = ctx->stream;
-  GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi));
+  GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi, splits, split_stride));
   GT_LAUNCH_CHECK();
   return nullptr;
 }
 
 template <int EK>
 static char* launch_layout(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
-                           bool a_mn, bool b_mn) {
-  if (!a_mn && !b_mn) return launch<false, false, EK>(ctx, s, A, B, epi);
-  if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi);
-  if (a_mn && !b_mn) return launch<true, false, EK>(ctx, s, A, B, epi);
-  return launch<true, true, EK>(ctx, s, A, B, epi);
+                           bool a_mn, bool b_mn, int splits = 1, int64_t split_stride = 0) {
+  if (!a_mn && !b_mn) return launch<false, false, EK>(ctx, s, A, B, epi, splits, split_stride);
+  if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi, splits, split_stride);
+  if (a_mn && !b_mn) return launch<true, false, EK>(ctx, s, A, B, epi, splits, split_stride);
+  return launch<true, true, EK>(ctx, s, A, B, epi, splits, split_stride);
+}
+
+// out = epilogue(sum of the `splits` partials), the partials added in split
+// order, so the result does not depend on which unit finished first.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t M, int64_t N, Epi<float> epi) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = ws[i];
+    for (int k = 1; k < splits; k++) acc = __fadd_rn(acc, ws[k * total + i]);
+    const int64_t m = i / N;
+    epi.store(m, i - m * N, acc);
+  }
+}
+
+// K-splits for a GEMM: more units than tiles when the tiles alone leave SM
+// pairs idle (too few tiles, or a last round that is mostly empty). Cost in
+// units of one K-slice of MMA on a pair (~0.54 us): rounds x (slices per unit
+// + a fixed per-unit overhead), plus, for splits > 1, the partials' trip
+// through memory (written, read back, final write) at ~5 TB/s.
+static int g_force_splits = 0;
+
+static int choose_splits(int64_t tiles, int64_t pairs, int64_t num_k, int64_t M, int64_t N) {
+  if (g_force_splits > 0) return (int)std::min<int64_t>(g_force_splits, std::max<int64_t>(num_k, 1));
+  auto cost = [&](int S) {
+    const double rounds = std::ceil((double)(tiles * S) / (double)pairs);
+    double c = rounds * (std::ceil((double)num_k / S) + 40.0);
+    if (S > 1) c += (S + 1) * (double)M * (double)N * 4.0 / 5e6 / 0.54;
+    return c;
+  };
+  int best = 1;
+  double best_cost = cost(1);
+  for (int S = 2; S <= 8; S++) {
+    if (num_k / S < 2 * GROUP) break;
+    if ((double)S * M * N * 4 > (double)(1ull << 30)) break;  // workspace bound
+    const double c = cost(S);
+    if (c < 0.9 * best_cost) {  // measured: a split that saves less does not pay
+      best = S;
+      best_cost = c;
+    }
+  }
+  return best;
 }
 
 }  // namespace tc
+
+void set_gemm_splits(int splits) { tc::g_force_splits = splits; }
 
 // Reports (and clears) a timed-out pipeline wait of an earlier tcgen05 GEMM.
 char* tc_check_errors() {
@@ -661,11 +750,34 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
   if (ctx->sm_count < 2) return nullptr;
   if (gemm_path() != 2 && s.M * s.N * s.K < (int64_t)1 << 21) return nullptr;
   const bool a_mn = s.trans_a, b_mn = !s.trans_b;
+  const int64_t tiles = ceil_div(s.M, 2 * tc::BM) * ceil_div(s.N, tc::BN);
+  const int splits = tc::choose_splits(tiles, ctx->sm_count / 2, ceil_div(s.K, tc::BK), s.M, s.N);
   char* err;
-  switch (tc::epi_kind(epi)) {
+  if (splits > 1) {
+    // Partials into a workspace (plain epilogue), then the fixed-order sum
+    // with the real epilogue.
+    void* ws = nullptr;
+    GT_TRY(scratch(ctx, (size_t)splits * s.M * s.N * sizeof(float), &ws));
+    Epi<float> part;
+    part.out = (float*)ws;
+    part.ldc = s.N;
+    err = tc::launch_layout<tc::EK_PLAIN>(ctx, s, A, B, part, a_mn, b_mn, splits, s.M * s.N);
+    if (!err) {
+      tc::splitk_reduce_kernel<<<grid_for(ctx, s.M * s.N, 256), 256, 0, ctx->stream>>>((const float*)ws, splits, s.M,
+                                                                                        s.N, epi);
+      count_launch();
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) err = cuda_error(e, "splitk_reduce_kernel launch", __FILE__, __LINE__);
+    }
+    release(ctx, ws);
+    if (!err) *done = true;
+    return err;
+  }
+  switch (tc::epi_kind(epi, s.N)) {
     case tc::EK_PLAIN: err = tc::launch_layout<tc::EK_PLAIN>(ctx, s, A, B, epi, a_mn, b_mn); break;
     case tc::EK_BIAS_RELU: err = tc::launch_layout<tc::EK_BIAS_RELU>(ctx, s, A, B, epi, a_mn, b_mn); break;
     case tc::EK_MASK: err = tc::launch_layout<tc::EK_MASK>(ctx, s, A, B, epi, a_mn, b_mn); break;
+    case tc::EK_CONV: err = tc::launch_layout<tc::EK_CONV>(ctx, s, A, B, epi, a_mn, b_mn); break;
     default: err = tc::launch_layout<tc::EK_GENERIC>(ctx, s, A, B, epi, a_mn, b_mn); break;
   }
   if (!err) *done = true;

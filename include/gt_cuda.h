@@ -329,6 +329,10 @@ GT_API char* gt_gemm_timer_read(gt_ctx* ctx, int64_t i, int64_t mnk[3], int* pat
 /* Pins the float32 GEMM path: 0 automatic, 1 SIMT only, 2 tcgen05 only (shapes
  * that do not qualify then fail). Process-wide; for tests and benchmarks. */
 GT_API void gt_debug_set_gemm_path(int path);
+/* Pins the number of K-splits of tcgen05 GEMMs (0: chosen per shape). A GEMM
+ * with S > 1 splits computes S partial products over consecutive K ranges and
+ * sums them in order with its epilogue. Process-wide; for tests. */
+GT_API void gt_debug_set_gemm_splits(int splits);
 /* The path the most recent float32 GEMM took: 1 SIMT, 2 tcgen05 (0: none yet). */
 GT_API int gt_gemm_path_taken(void);
 

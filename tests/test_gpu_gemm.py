@@ -49,7 +49,8 @@ def test_tc_matches_oracle(mkn, ta, tb):
     assert_close(got, want, 1e-4, f"tc {mkn} ta={ta} tb={tb}")
 
 
-@pytest.mark.parametrize("mkn", [(4096, 4096, 1024), (1024, 8192, 4096), (8192, 1000, 512), (256, 1000, 384)])
+@pytest.mark.parametrize("mkn", [(4096, 4096, 1024), (1024, 8192, 4096), (8192, 1000, 512), (256, 1000, 384),
+                                 (1024, 4096, 1000)])  # the last one runs as 4 K-splits (16 tiles)
 @pytest.mark.parametrize("ta,tb", [(False, True), (False, False), (True, False)])
 def test_tc_large_against_float64(mkn, ta, tb):
     """The three operand layouts of a Linear layer's forward, dX and dW GEMMs at
@@ -120,3 +121,55 @@ def test_gemm_timer_records_each_launch_outside_capture():
         check(lib.gt_gemm_timer_stop(ctx))
     with pytest.raises(GTError, match="no timer"):
         check(lib.gt_gemm_timer_count(ctx, None, None))
+
+
+def _f64_error(a, b, got, m, k, n, ta, tb):
+    A = a.reshape(k, m).T if ta else a.reshape(m, k)
+    B = b.reshape(n, k).T if tb else b.reshape(k, n)
+    exact = A.astype(np.float64) @ B.astype(np.float64)
+    scale = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64)
+    err = np.abs(got.reshape(m, n) - exact) / scale
+    err32 = np.abs((A @ B).astype(np.float64) - exact) / scale
+    return err.max(), err32.max()
+
+
+@pytest.mark.parametrize("splits", [2, 3, 8])
+@pytest.mark.parametrize("ta,tb", [(False, True), (False, False), (True, False)])
+def test_tc_split_k_against_float64_and_deterministic(splits, ta, tb):
+    """K-split GEMMs (partials over consecutive K ranges, summed in split
+    order): fp32-class error, and the same bits on every run whatever the
+    order in which the units finish."""
+    lib = _lib.cuda_lib()
+    lib.gt_debug_set_gemm_splits(splits)
+    try:
+        m, k, n = 300, 4096, 520
+        rng = np.random.default_rng(splits)
+        a, b, got = run(m, k, n, ta, tb, rng, weight_like=False)
+        err, err32 = _f64_error(a, b, got, m, k, n, ta, tb)
+        assert err <= max(4 * err32, 2.0 ** -20), (err, err32)
+        be = cuda_backend()
+        ga, gb = be.FromHost(a), be.FromHost(b)
+        for _ in range(2):
+            again = be.ToHost(be.MatMul(ga, gb, m, k, n, ta, tb))
+            assert np.array_equal(again, got)
+    finally:
+        lib.gt_debug_set_gemm_splits(0)
+
+
+@pytest.mark.parametrize("splits", [2, 4])
+def test_fused_epilogues_under_split_k(splits):
+    """The fused Linear/Conv2d entry points when their GEMM is K-split: the
+    bias, activation, derivative mask and NCHW order are applied once, to the
+    summed result (checked against the oracle's op chains)."""
+    import test_gpu_fused as F
+    lib = _lib.cuda_lib()
+    lib.gt_debug_set_gemm_splits(splits)
+    try:
+        F.test_linear_fwd(T.Float32, np.float32, 1e-4, 1, (257, 1024, 300))  # bias + ReLU
+        F.test_linear_fwd(T.Float32, np.float32, 1e-4, 3, (64, 784, 128))  # sigmoid (generic epilogue)
+        F.test_linear_bwd(T.Float32, np.float32, 1e-4, 1, (257, 1024, 300))  # ReLU mask on dX; dW
+        F.test_conv_fwd_bwd(T.Float32, np.float32, 1e-4, (4, 32, 14, 14, 64, 3, 1, 1))  # NCHW store, bias by row
+    finally:
+        lib.gt_debug_set_gemm_splits(0)
+        cuda_backend().Sync()
+        F._keep.clear()
