@@ -388,6 +388,7 @@ def step_roofline(lib, model, steps):
     if dropped.value:
         raise SystemExit(f"GEMM timer dropped {dropped.value} launches")
     shapes = {}
+    last_step = []  # (M x N x K, ms) of every GEMM of the pass's last step, in launch order
     total_ms = total_flops = 0.0
     tc = True
     mnk = (ctypes.c_int64 * 3)()
@@ -396,6 +397,8 @@ def step_roofline(lib, model, steps):
     for i in range(n.value):
         check(lib.gt_gemm_timer_read(ctx, i, mnk, ctypes.byref(path), ctypes.byref(ms)))
         key = f"{mnk[0]}x{mnk[1]}x{mnk[2]}"
+        if i >= n.value - n.value // steps:
+            last_step.append((key, round(ms.value, 4)))
         flops = 2.0 * mnk[0] * mnk[1] * mnk[2]
         e = shapes.setdefault(key, {"launches": 0, "ms": 0.0, "flops": flops})
         e["launches"] += 1
@@ -418,7 +421,8 @@ def step_roofline(lib, model, steps):
                                    "step (forward, dW, dX), M x N x K below",
                          "flops_per_launch": total_flops / n.value, "ms_per_launch": total_ms / n.value,
                          "gemm_share_of_step": total_ms / pass_ms.value, "step_ms_timed_pass": pass_ms.value / steps,
-                         "by_shape": breakdown, "peak_note": note + " (of measured)",
+                         "by_shape": breakdown, "last_step_launches": last_step,
+                         "peak_note": note + " (of measured)",
                          "peak_sustained": _peak_3xtf32_sustained(),
                          "frac_of_sustained": (achieved / _peak_3xtf32_sustained()) if _peak_3xtf32_sustained() else None},
             "optimizer": optimizer}

@@ -70,6 +70,7 @@ Model::Model(gt_ctx* ctx, int dtype, const std::vector<gth_layer>& layers, const
 
 Model::~Model() {
   drop_graph();
+  free_bucket_events();
   for (int p = 0; p < 2; p++) {
     gt_event_free(ready_[p]);
     gt_event_free(free_[p]);
@@ -348,12 +349,19 @@ void Model::forward() {
 
 void Model::issue_ready_buckets(int64_t boundary) {
   while (next_bucket_ < buckets_.size() && buckets_[next_bucket_].first >= boundary) {
-    auto b = buckets_[next_bucket_++];
+    auto b = buckets_[next_bucket_];
     check(gt_allreduce_avg_async(ctx_, dtype_, (char*)gbuf_.get() + b.first * es_, b.second - b.first));
+    check(gt_event_record(ctx_, bucket_done_[next_bucket_], GT_STREAM_COMM));
+    next_bucket_++;
   }
 }
 
-void Model::backward() {
+void Model::free_bucket_events() {
+  for (auto* e : bucket_done_) gt_event_free(e);
+  bucket_done_.clear();
+}
+
+void Model::backward(bool join) {
   char* p = (char*)pbuf_.get();
   char* gr = (char*)gbuf_.get();
   // Invariant: g is the gradient w.r.t. the output of op i; g_pre says the
@@ -412,7 +420,7 @@ void Model::backward() {
   if (world_ > 1) {
     issue_ready_buckets(0);
     check(gt_allreduce_avg_async(ctx_, dtype_, loss_.get(), 1));
-    check(gt_comm_wait(ctx_));
+    if (join) check(gt_comm_wait(ctx_));
   }
 }
 
@@ -425,9 +433,25 @@ void Model::forward_backward() {
 
 void Model::optimizer_step() {
   if (opt_ == OPT_NONE) throw Error("no optimizer: call gth_set_sgd or gth_set_adam");
-  if (opt_ == OPT_SGD) {
+  if (opt_ == OPT_SGD && world_ > 1 && !bucket_done_.empty()) {
+    // Bucket by bucket, each as soon as its all-reduce is done: the updates of
+    // the buckets averaged first overlap the all-reduce of the last ones.
+    // (The update is elementwise, so the ranges give the same result as one
+    // launch over the whole buffer.)
+    char* p = (char*)pbuf_.get();
+    char* g = (char*)gbuf_.get();
+    char* v = (char*)opt_a_.get();
+    for (size_t i = 0; i < buckets_.size(); i++) {
+      const int64_t lo = buckets_[i].first, n = buckets_[i].second - buckets_[i].first;
+      check(gt_stream_wait_event(ctx_, GT_STREAM_COMPUTE, bucket_done_[i]));
+      check(gt_sgd_step(ctx_, dtype_, p + lo * es_, g + lo * es_, v + lo * es_, n, &sgd_, opt_steps_ == 0));
+    }
+    check(gt_comm_wait(ctx_));  // the loss average, and every stream joined
+  } else if (opt_ == OPT_SGD) {
+    if (world_ > 1) check(gt_comm_wait(ctx_));
     check(gt_sgd_step(ctx_, dtype_, pbuf_.get(), gbuf_.get(), opt_a_.get(), dev_params_, &sgd_, opt_steps_ == 0));
   } else {
+    if (world_ > 1) check(gt_comm_wait(ctx_));
     check(gt_adam_step_dev(ctx_, dtype_, pbuf_.get(), gbuf_.get(), opt_a_.get(), opt_b_.get(), dev_params_, &adam_,
                            (int64_t*)step_dev_.get()));
   }
@@ -449,7 +473,7 @@ void Model::train_step() {
     if (capture) check(gt_capture_begin(ctx_));
     try {
       forward();
-      backward();
+      backward(false);  // the optimizer waits for the gradient buckets itself
       optimizer_step();
     } catch (...) {
       if (capture) {
@@ -511,6 +535,12 @@ void Model::dp_init(int rank, int world, const unsigned char id[128], int timeou
                            bounds.data(), (int)sizes.size());
   buckets_.clear();
   for (int b = 0; b < nb; b++) buckets_.emplace_back(bounds[2 * b], bounds[2 * b + 1]);
+  free_bucket_events();
+  for (int b = 0; b < nb; b++) {
+    gt_event* e = nullptr;
+    check(gt_event_new(ctx_, &e));
+    bucket_done_.push_back(e);
+  }
 }
 
 }  // namespace gotensor

@@ -123,7 +123,9 @@ class Model {
  private:
   void plan(const std::vector<gth_layer>& layers, const std::vector<int64_t>& input_shape);
   void forward();
-  void backward();
+  // join: the compute stream waits for the gradient all-reduce before
+  // returning (else the optimizer waits bucket by bucket).
+  void backward(bool join = true);
   void issue_ready_buckets(int64_t boundary);
   void drop_graph();
   void bind_input(int p);  // points the plan at input/label buffer pair p
@@ -159,7 +161,9 @@ class Model {
 
   int rank_ = 0, world_ = 1;
   std::vector<std::pair<int64_t, int64_t>> buckets_;  // device element ranges, last first
+  std::vector<gt_event*> bucket_done_;                 // comm stream: bucket i's all-reduce is done
   size_t next_bucket_ = 0;
+  void free_bucket_events();
 
   bool use_graph_ = false;
   gt_graph* graph_[2] = {};  // the captured step for each input pair
