@@ -87,6 +87,13 @@ using namespace gt;
 
 extern "C" {
 
+char* gt_set_gemm_sm_reserve(gt_ctx* ctx, int sms) {
+  GT_ENTER(ctx);
+  if (sms < 0 || sms > ctx->sm_count - 2) return errorf("gt_set_gemm_sm_reserve: %d of %d SMs", sms, ctx->sm_count);
+  ctx->gemm_sm_reserve = sms;
+  return nullptr;
+}
+
 void gt_debug_set_gemm_path(int path) { set_gemm_path(path); }
 void gt_debug_set_gemm_splits(int splits) { set_gemm_splits(splits < 0 ? 0 : splits); }
 int gt_gemm_path_taken(void) { return g_gemm_taken; }

@@ -644,6 +644,13 @@ static char* make_map(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t 
   return nullptr;
 }
 
+// SM pairs a GEMM may occupy: all of them, less the SMs reserved for kernels
+// that run beside it (a collective on another stream).
+static int64_t pairs_available(const gt_ctx* ctx) {
+  const int64_t free_sms = (int64_t)ctx->sm_count - ctx->gemm_sm_reserve;
+  return free_sms >= 2 ? free_sms / 2 : 1;
+}
+
 template <bool A_MN, bool B_MN, int EK>
 static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
                     int splits, int64_t split_stride) {
@@ -663,7 +670,8 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
     if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
   }
   const int64_t units = ceil_div(s.M, 2 * BM) * ceil_div(s.N, BN) * splits;
-  const int64_t pairs = units < ctx->sm_count / 2 ? units : ctx->sm_count / 2;
+  const int64_t avail = pairs_available(ctx);
+  const int64_t pairs = units < avail ? units : avail;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);
@@ -751,7 +759,7 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
   if (gemm_path() != 2 && s.M * s.N * s.K < (int64_t)1 << 21) return nullptr;
   const bool a_mn = s.trans_a, b_mn = !s.trans_b;
   const int64_t tiles = ceil_div(s.M, 2 * tc::BM) * ceil_div(s.N, tc::BN);
-  const int splits = tc::choose_splits(tiles, ctx->sm_count / 2, ceil_div(s.K, tc::BK), s.M, s.N);
+  const int splits = tc::choose_splits(tiles, tc::pairs_available(ctx), ceil_div(s.K, tc::BK), s.M, s.N);
   char* err;
   if (splits > 1) {
     // Partials into a workspace (plain epilogue), then the fixed-order sum

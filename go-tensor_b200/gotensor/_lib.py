@@ -120,6 +120,7 @@ CUDA_API = {
     "gt_gemm_timer_stop": ("err", [_P]),
     "gt_gemm_timer_count": ("err", [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     "gt_gemm_timer_read": ("err", [_P, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_INT), ctypes.POINTER(ctypes.c_float)]),
+    "gt_set_gemm_sm_reserve": ("err", [_P, _INT]),
     "gt_debug_set_gemm_path": (None, [_INT]),
     "gt_debug_set_gemm_splits": (None, [_INT]),
     "gt_gemm_path_taken": (_INT, []),

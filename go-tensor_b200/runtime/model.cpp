@@ -18,6 +18,7 @@
 #include "model.hpp"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 namespace gotensor {
@@ -348,6 +349,8 @@ void Model::forward() {
 }
 
 void Model::issue_ready_buckets(int64_t boundary) {
+  if (next_bucket_ == 0 && next_bucket_ < buckets_.size() && buckets_[0].first >= boundary && sm_reserve_ > 0)
+    check(gt_set_gemm_sm_reserve(ctx_, sm_reserve_));  // the all-reduce kernels run beside the GEMMs from here
   while (next_bucket_ < buckets_.size() && buckets_[next_bucket_].first >= boundary) {
     auto b = buckets_[next_bucket_];
     check(gt_allreduce_avg_async(ctx_, dtype_, (char*)gbuf_.get() + b.first * es_, b.second - b.first));
@@ -419,6 +422,7 @@ void Model::backward(bool join) {
   }
   if (world_ > 1) {
     issue_ready_buckets(0);
+    if (sm_reserve_ > 0) check(gt_set_gemm_sm_reserve(ctx_, 0));
     check(gt_allreduce_avg_async(ctx_, dtype_, loss_.get(), 1));
     if (join) check(gt_comm_wait(ctx_));
   }
@@ -522,6 +526,9 @@ void Model::forward_eval(void* logits_host) {
 
 void Model::dp_init(int rank, int world, const unsigned char id[128], int timeout_ms, int64_t bucket_bytes) {
   drop_graph();
+  // SMs the backward GEMMs leave to the all-reduce kernels running beside
+  // them (GT_DP_SM_RESERVE; 0 = none).
+  if (const char* r = getenv("GT_DP_SM_RESERVE")) sm_reserve_ = std::max(0, atoi(r));
   if (world > 1) check(gt_comm_init(ctx_, rank, world, id, timeout_ms));
   rank_ = rank;
   world_ = world;

@@ -160,6 +160,7 @@ class Model {
   int64_t opt_steps_ = 0;
 
   int rank_ = 0, world_ = 1;
+  int sm_reserve_ = 0;  // SMs left to the all-reduce while it overlaps backward GEMMs
   std::vector<std::pair<int64_t, int64_t>> buckets_;  // device element ranges, last first
   std::vector<gt_event*> bucket_done_;                 // comm stream: bucket i's all-reduce is done
   size_t next_bucket_ = 0;

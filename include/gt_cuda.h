@@ -283,6 +283,13 @@ GT_API void gt_graph_free(gt_graph* graph);
 GT_API char* gt_mark(gt_ctx* ctx, int slot);
 GT_API char* gt_elapsed_ms(gt_ctx* ctx, int from, int to, float* ms);
 
+/* GEMM kernels launched on ctx from now on occupy at most sm_count - sms SMs,
+ * leaving `sms` free for kernels that run beside them on other streams (the
+ * collective kernels of a gradient all-reduce): a persistent GEMM that finds
+ * fewer free SMs than it has CTAs runs its remaining tiles in an extra round.
+ * 0 (the default) uses every SM. No counterpart in the reference. */
+GT_API char* gt_set_gemm_sm_reserve(gt_ctx* ctx, int sms);
+
 /* ---- overlapping uploads ------------------------------------------------- */
 /* A context has three streams: compute (every kernel), copy (uploads that
  * overlap compute) and comm (gradient all-reduce). Events order one stream
