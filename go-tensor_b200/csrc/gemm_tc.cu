@@ -316,10 +316,10 @@ inline int epi_kind(const Epi<float>& e, int64_t n_cols) {
 // bytes. Same operations, in the same order, as Epi::store.
 template <int EK>
 __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const GemmShape& s, const float* xpose, int lane,
-                                               int64_t m0, int64_t n, int64_t out_offset) {
+                                               int64_t m0, int64_t n) {
   if (n >= s.N) return;
   const int rows = (int)(s.M - m0 < 32 ? s.M - m0 : 32);
-  float* op = epi.out + out_offset + m0 * epi.ldc + n;
+  float* op = epi.out + m0 * epi.ldc + n;
   if (EK == EK_PLAIN) {
 #pragma unroll 4
     for (int r = 0; r < rows; r++) op[r * epi.ldc] = xpose[r * EPI_LD + lane];
@@ -366,14 +366,31 @@ __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const Gemm
   }
 }
 
-// Work unit u of a launch with `splits` K-splits: tile t (of `tiles`) over
-// K-slices [kb, ke); the splits of one tile are `tiles` units apart, so the
-// units running at the same time share operand panels of one K range.
-__device__ __forceinline__ int unit_of(int u, int tiles, int splits, int num_k, int& t, int& kb, int& ke) {
-  const int sidx = u / tiles;
-  t = u - sidx * tiles;
-  kb = (int)((int64_t)sidx * num_k / splits);
-  ke = (int)((int64_t)(sidx + 1) * num_k / splits);
+// How a launch covers its tiles: tiles [0, whole) as single units over all
+// of K, the remaining tiles in `splits` units each over consecutive K ranges.
+// A split unit stores its partial 256 x 256 tile in the workspace; a second
+// kernel adds a tile's partials in split order and applies the epilogue.
+struct SplitPlan {
+  int whole = 0;
+  int splits = 1;
+  float* ws = nullptr;  // [splits][tiles - whole][256 * 256]
+};
+
+constexpr int64_t TILE_ELEMS = 2 * BM * BN;
+
+// Work unit u: tile t over K-slices [kb, ke). Returns the split index, or -1
+// for a whole tile. The splits of one tile are (tiles - whole) units apart,
+// so the units running at the same time share operand panels of one K range.
+__device__ __forceinline__ int unit_of(int u, int tiles, const SplitPlan& sp, int num_k, int& t, int& kb, int& ke) {
+  if (u < sp.whole) {
+    t = u, kb = 0, ke = num_k;
+    return -1;
+  }
+  const int rest = tiles - sp.whole, v = u - sp.whole;
+  const int sidx = v / rest;
+  t = sp.whole + (v - sidx * rest);
+  kb = (int)((int64_t)sidx * num_k / sp.splits);
+  ke = (int)((int64_t)(sidx + 1) * num_k / sp.splits);
   return sidx;
 }
 
@@ -391,7 +408,7 @@ struct Shared {
 template <bool A_MN, bool B_MN, int EK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            GemmShape s, Epi<float> epi, int splits, int64_t split_stride) {
+                            GemmShape s, Epi<float> epi, SplitPlan sp) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   Shared* sh = (Shared*)(smem + BAR_OFFSET);
@@ -404,7 +421,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int m_tiles = (int)((s.M + 2 * BM - 1) / (2 * BM));
   const int n_tiles = (int)((s.N + BN - 1) / BN);
   const int tiles = m_tiles * n_tiles;
-  const int units = tiles * splits;  // splits > 1: each unit writes a partial at out + split * split_stride
+  const int units = sp.whole + (tiles - sp.whole) * sp.splits;
   const int pair = (int)cluster_id(), pairs = (int)num_clusters();
 
   if (threadIdx.x == 0) {
@@ -441,7 +458,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         int it = 0, issued_to = 0;
         for (int u = pair; u < units && !*failed; u += pairs) {
           int t, kb, ke;
-          unit_of(u, tiles, splits, num_k, t, kb, ke);
+          unit_of(u, tiles, sp, num_k, t, kb, ke);
           const int mt = t / n_tiles, nt = t % n_tiles;
           const int a_row = mt * 2 * BM + (int)rank * BM;
           const int b_row = nt * BN + (int)rank * BNH;
@@ -483,7 +500,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         bool stop = false;
         for (int u = pair; u < units && !stop; u += pairs) {
           int t, kb, ke;
-          unit_of(u, tiles, splits, num_k, t, kb, ke);
+          unit_of(u, tiles, sp, num_k, t, kb, ke);
           for (int kt = kb; kt < ke; kt++, it++) {
             const bool group_start = (kt - kb) % GROUP == 0;
             const uint32_t buf = (uint32_t)(group & 1);
@@ -532,7 +549,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int total = 0;  // slices this pair streams
       for (int u = pair; u < units; u += pairs) {
         int t, kb, ke;
-        unit_of(u, tiles, splits, num_k, t, kb, ke);
+        unit_of(u, tiles, sp, num_k, t, kb, ke);
         total += ke - kb;
       }
       for (int it = st; it < total; it += STAGES) {
@@ -559,7 +576,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int group = 0;
     for (int u = pair; u < units && !__shfl_sync(0xffffffffu, *failed, 0); u += pairs) {
       int t, kb, ke;
-      const int sidx = unit_of(u, tiles, splits, num_k, t, kb, ke);
+      const int sidx = unit_of(u, tiles, sp, num_k, t, kb, ke);
+      // a split unit's partial tile in the workspace (row-major 256 x 256)
+      float* part = sidx < 0 ? nullptr
+                             : sp.ws + ((int64_t)sidx * (tiles - sp.whole) + (t - sp.whole)) * TILE_ELEMS +
+                                   (int64_t)(rank * BM + 32 * q) * BN + 128 * h + lane;
       const int groups = (ke - kb + GROUP - 1) / GROUP;
       const int mt = t / n_tiles, nt = t % n_tiles;
       // The running total starts at +0 and every partial is added with
@@ -606,7 +627,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #undef GT_XPOSE_CASE
         }
         __syncwarp();
-        epilogue_block<EK>(epi, s, xpose, lane, m0, (int64_t)nt * BN + 128 * h + 32 * j + lane, sidx * split_stride);
+        if (!part) {
+          epilogue_block<EK>(epi, s, xpose, lane, m0, (int64_t)nt * BN + 128 * h + 32 * j + lane);
+        } else {
+#pragma unroll 4
+          for (int r = 0; r < 32; r++) part[r * BN + 32 * j] = xpose[r * EPI_LD + lane];
+        }
         __syncwarp();
       }
     }
@@ -653,7 +679,7 @@ static int64_t pairs_available(const gt_ctx* ctx) {
 
 template <bool A_MN, bool B_MN, int EK>
 static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
-                    int splits, int64_t split_stride) {
+                    const SplitPlan& sp) {
   CUtensorMap ta, tb;
   if (A_MN)
     GT_TRY(make_map(ctx, &ta, A, s.M, s.K, s.lda, true));
@@ -669,7 +695,8 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
     GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
   }
-  const int64_t units = ceil_div(s.M, 2 * BM) * ceil_div(s.N, BN) * splits;
+  const int64_t tiles = ceil_div(s.M, 2 * BM) * ceil_div(s.N, BN);
+  const int64_t units = sp.whole + (tiles - sp.whole) * sp.splits;
   const int64_t avail = pairs_available(ctx);
   const int64_t pairs = units < avail ? units : avail;
   cudaLaunchConfig_t cfg = {};
@@ -677,57 +704,94 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
   cfg.blockDim = dim3(THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = ctx->stream;
-  GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi, splits, split_stride));
+  GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi, sp));
   GT_LAUNCH_CHECK();
   return nullptr;
 }
 
 template <int EK>
 static char* launch_layout(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
-                           bool a_mn, bool b_mn, int splits = 1, int64_t split_stride = 0) {
-  if (!a_mn && !b_mn) return launch<false, false, EK>(ctx, s, A, B, epi, splits, split_stride);
-  if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi, splits, split_stride);
-  if (a_mn && !b_mn) return launch<true, false, EK>(ctx, s, A, B, epi, splits, split_stride);
-  return launch<true, true, EK>(ctx, s, A, B, epi, splits, split_stride);
+                           bool a_mn, bool b_mn, const SplitPlan& sp) {
+  if (!a_mn && !b_mn) return launch<false, false, EK>(ctx, s, A, B, epi, sp);
+  if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi, sp);
+  if (a_mn && !b_mn) return launch<true, false, EK>(ctx, s, A, B, epi, sp);
+  return launch<true, true, EK>(ctx, s, A, B, epi, sp);
 }
 
-// out = epilogue(sum of the `splits` partials), the partials added in split
-// order, so the result does not depend on which unit finished first.
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t M, int64_t N, Epi<float> epi) {
-  const int64_t total = M * N;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    float acc = ws[i];
-    for (int k = 1; k < splits; k++) acc = __fadd_rn(acc, ws[k * total + i]);
-    const int64_t m = i / N;
-    epi.store(m, i - m * N, acc);
+static char* launch_kind(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
+                         bool a_mn, bool b_mn, const SplitPlan& sp) {
+  switch (epi_kind(epi, s.N)) {
+    case EK_PLAIN: return launch_layout<EK_PLAIN>(ctx, s, A, B, epi, a_mn, b_mn, sp);
+    case EK_BIAS_RELU: return launch_layout<EK_BIAS_RELU>(ctx, s, A, B, epi, a_mn, b_mn, sp);
+    case EK_MASK: return launch_layout<EK_MASK>(ctx, s, A, B, epi, a_mn, b_mn, sp);
+    case EK_CONV: return launch_layout<EK_CONV>(ctx, s, A, B, epi, a_mn, b_mn, sp);
+    default: return launch_layout<EK_GENERIC>(ctx, s, A, B, epi, a_mn, b_mn, sp);
   }
 }
 
-// K-splits for a GEMM: more units than tiles when the tiles alone leave SM
-// pairs idle (too few tiles, or a last round that is mostly empty). Cost in
-// units of one K-slice of MMA on a pair (~0.54 us): rounds x (slices per unit
-// + a fixed per-unit overhead), plus, for splits > 1, the partials' trip
-// through memory (written, read back, final write) at ~5 TB/s.
+// C of the split tiles = epilogue(sum of their partials), the partials added
+// in split order, so the result does not depend on which unit finished first.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, SplitPlan sp, int tiles, int n_tiles, int64_t M,
+                                     int64_t N, Epi<float> epi) {
+  const int rest = tiles - sp.whole;
+  const int64_t total = (int64_t)rest * TILE_ELEMS;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / TILE_ELEMS);
+    const int64_t e = i - (int64_t)r * TILE_ELEMS;
+    const int t = sp.whole + r;
+    const int64_t m = (int64_t)(t / n_tiles) * 2 * BM + e / BN, n = (int64_t)(t % n_tiles) * BN + e % BN;
+    if (m >= M || n >= N) continue;
+    float acc = ws[i];
+    for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
+    epi.store(m, n, acc);
+  }
+}
+
+// The split plan of a GEMM, from a cost model in units of one K-slice of MMA
+// on a pair (~0.54 us): rounds x (slices per unit + a fixed per-unit
+// overhead), plus the partials' trip through memory at ~5 TB/s. Candidates:
+// no split; every tile split S ways (too few tiles for the SM pairs); or only
+// the tiles of a mostly empty last round split S ways (wave quantisation).
 static int g_force_splits = 0;
 
-static int choose_splits(int64_t tiles, int64_t pairs, int64_t num_k, int64_t M, int64_t N) {
-  if (g_force_splits > 0) return (int)std::min<int64_t>(g_force_splits, std::max<int64_t>(num_k, 1));
-  auto cost = [&](int S) {
-    const double rounds = std::ceil((double)(tiles * S) / (double)pairs);
-    double c = rounds * (std::ceil((double)num_k / S) + 40.0);
-    if (S > 1) c += (S + 1) * (double)M * (double)N * 4.0 / 5e6 / 0.54;
-    return c;
+static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k) {
+  SplitPlan best;
+  best.whole = (int)tiles;
+  if (g_force_splits > 1) {
+    best.whole = 0;
+    best.splits = (int)std::min<int64_t>(g_force_splits, std::max<int64_t>(num_k, 1));
+    return best;
+  }
+  constexpr double kUnitOverhead = 40.0;
+  auto reduce_cost = [&](int64_t split_tiles, int S) {
+    return (S + 1) * (double)split_tiles * TILE_ELEMS * 4.0 / 5e6 / 0.54;
   };
-  int best = 1;
-  double best_cost = cost(1);
-  for (int S = 2; S <= 8; S++) {
-    if (num_k / S < 2 * GROUP) break;
-    if ((double)S * M * N * 4 > (double)(1ull << 30)) break;  // workspace bound
-    const double c = cost(S);
-    if (c < 0.9 * best_cost) {  // measured: a split that saves less does not pay
-      best = S;
+  const double base = std::ceil((double)tiles / pairs) * (num_k + kUnitOverhead);
+  double best_cost = base;
+  for (int S = 2; S <= 8 && num_k / S >= 2 * GROUP; S++) {
+    // every tile split
+    double c = std::ceil((double)(tiles * S) / pairs) * (std::ceil((double)num_k / S) + kUnitOverhead) +
+               reduce_cost(tiles, S);
+    if (c < best_cost) {
       best_cost = c;
+      best.whole = 0;
+      best.splits = S;
     }
+    // only the last round's tiles split
+    const int64_t full = tiles / pairs * pairs, rest = tiles - full;
+    if (full > 0 && rest > 0 && rest * S <= pairs) {
+      c = (double)(tiles / pairs) * (num_k + kUnitOverhead) + std::ceil((double)num_k / S) + kUnitOverhead +
+          reduce_cost(rest, S);
+      if (c < best_cost) {
+        best_cost = c;
+        best.whole = (int)full;
+        best.splits = S;
+      }
+    }
+  }
+  if (best_cost > 0.93 * base) {  // measured: smaller gains do not pay
+    best.whole = (int)tiles;
+    best.splits = 1;
   }
   return best;
 }
@@ -759,20 +823,20 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
   if (gemm_path() != 2 && s.M * s.N * s.K < (int64_t)1 << 21) return nullptr;
   const bool a_mn = s.trans_a, b_mn = !s.trans_b;
   const int64_t tiles = ceil_div(s.M, 2 * tc::BM) * ceil_div(s.N, tc::BN);
-  const int splits = tc::choose_splits(tiles, tc::pairs_available(ctx), ceil_div(s.K, tc::BK), s.M, s.N);
+  const int64_t n_tiles = ceil_div(s.N, tc::BN);
+  tc::SplitPlan sp = tc::choose_plan(tiles, tc::pairs_available(ctx), ceil_div(s.K, tc::BK));
   char* err;
-  if (splits > 1) {
-    // Partials into a workspace (plain epilogue), then the fixed-order sum
-    // with the real epilogue.
+  if (sp.splits > 1) {
+    const int64_t rest = tiles - sp.whole;
     void* ws = nullptr;
-    GT_TRY(scratch(ctx, (size_t)splits * s.M * s.N * sizeof(float), &ws));
-    Epi<float> part;
-    part.out = (float*)ws;
-    part.ldc = s.N;
-    err = tc::launch_layout<tc::EK_PLAIN>(ctx, s, A, B, part, a_mn, b_mn, splits, s.M * s.N);
+    GT_TRY(scratch(ctx, (size_t)sp.splits * rest * tc::TILE_ELEMS * sizeof(float), &ws));
+    sp.ws = (float*)ws;
+    // Whole tiles finish with their own epilogue; the split tiles' partials
+    // go to the workspace and are summed, in order, by the second kernel.
+    err = tc::launch_kind(ctx, s, A, B, epi, a_mn, b_mn, sp);
     if (!err) {
-      tc::splitk_reduce_kernel<<<grid_for(ctx, s.M * s.N, 256), 256, 0, ctx->stream>>>((const float*)ws, splits, s.M,
-                                                                                        s.N, epi);
+      tc::splitk_reduce_kernel<<<grid_for(ctx, rest * tc::TILE_ELEMS, 256), 256, 0, ctx->stream>>>(
+          sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
       count_launch();
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) err = cuda_error(e, "splitk_reduce_kernel launch", __FILE__, __LINE__);
@@ -781,13 +845,7 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
     if (!err) *done = true;
     return err;
   }
-  switch (tc::epi_kind(epi, s.N)) {
-    case tc::EK_PLAIN: err = tc::launch_layout<tc::EK_PLAIN>(ctx, s, A, B, epi, a_mn, b_mn); break;
-    case tc::EK_BIAS_RELU: err = tc::launch_layout<tc::EK_BIAS_RELU>(ctx, s, A, B, epi, a_mn, b_mn); break;
-    case tc::EK_MASK: err = tc::launch_layout<tc::EK_MASK>(ctx, s, A, B, epi, a_mn, b_mn); break;
-    case tc::EK_CONV: err = tc::launch_layout<tc::EK_CONV>(ctx, s, A, B, epi, a_mn, b_mn); break;
-    default: err = tc::launch_layout<tc::EK_GENERIC>(ctx, s, A, B, epi, a_mn, b_mn); break;
-  }
+  err = tc::launch_kind(ctx, s, A, B, epi, a_mn, b_mn, sp);
   if (!err) *done = true;
   return err;
 }

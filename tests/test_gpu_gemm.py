@@ -50,7 +50,8 @@ def test_tc_matches_oracle(mkn, ta, tb):
 
 
 @pytest.mark.parametrize("mkn", [(4096, 4096, 1024), (1024, 8192, 4096), (8192, 1000, 512), (256, 1000, 384),
-                                 (1024, 4096, 1000)])  # the last one runs as 4 K-splits (16 tiles)
+                                 (1024, 4096, 1000),  # 16 tiles: every tile in 4 K-splits
+                                 (4096, 8192, 4096)])  # 256 tiles: the last round's 34 tiles in 2 K-splits
 @pytest.mark.parametrize("ta,tb", [(False, True), (False, False), (True, False)])
 def test_tc_large_against_float64(mkn, ta, tb):
     """The three operand layouts of a Linear layer's forward, dX and dW GEMMs at
@@ -173,3 +174,26 @@ def test_fused_epilogues_under_split_k(splits):
         lib.gt_debug_set_gemm_splits(0)
         cuda_backend().Sync()
         F._keep.clear()
+
+
+def test_sm_reserve_leaves_results_unchanged():
+    """GEMMs launched with SMs reserved for other streams (the all-reduce of
+    data parallelism) run on fewer SM pairs, in more rounds, with the same
+    bits; an out-of-range reserve is refused."""
+    from gotensor._lib import GTError, check
+    lib = _lib.cuda_lib()
+    be = cuda_backend()
+    rng = np.random.default_rng(21)
+    m, k, n = 2048, 512, 2048  # 64 tiles, no K-split either way
+    a = be.FromHost(rng.standard_normal(m * k).astype(np.float32))
+    b = be.FromHost(rng.standard_normal(k * n).astype(np.float32))
+    want = be.ToHost(be.MatMul(a, b, m, k, n, False, False))
+    try:
+        for sms in (20, 100):
+            check(lib.gt_set_gemm_sm_reserve(be.ctx.ptr, sms))
+            got = be.ToHost(be.MatMul(a, b, m, k, n, False, False))
+            assert np.array_equal(got, want), sms
+        with pytest.raises(GTError, match="SMs"):
+            check(lib.gt_set_gemm_sm_reserve(be.ctx.ptr, 10_000))
+    finally:
+        check(lib.gt_set_gemm_sm_reserve(be.ctx.ptr, 0))
