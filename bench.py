@@ -331,12 +331,12 @@ def run_ours(args):
 # dram__bytes_read.sum + dram__bytes_write.sum of the GEMM launches of one
 # training step of this workload, from one ncu capture (the command and the
 # per-launch figures are in profiles/wide_mlp_b8192_step_launches.md).
-GEMM_TRAFFIC_BYTES_PER_STEP = 4_526_827_008
+GEMM_TRAFFIC_BYTES_PER_STEP = 4_503_205_888
 GEMM_LAUNCHES_PER_STEP = 8
 # The SGD update: read p, g, v and write p, v (float32), and the DRAM traffic
 # of its launch in the same capture.
 SGD_BYTES_PER_PARAM = 20
-SGD_TRAFFIC_BYTES = 697_041_152
+SGD_TRAFFIC_BYTES = 697_423_104
 
 
 def _peak_3xtf32():
