@@ -479,6 +479,8 @@ def main():
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the dominant kernel (the backward GEMMs at the workload's shapes), for profiling")
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--eval-only", action="store_true",
+                    help="time evaluation instead (forward + Argmax + correct count on the device)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -486,6 +488,8 @@ def main():
         return run_reference(args)
     if args.gemm_only:
         return run_gemm_only(args)
+    if args.eval_only:
+        return run_eval_only(args)
     return run_ours(args)
 
 
@@ -497,6 +501,58 @@ def run_gemm_only(args):
     lib = cuda_lib()
     model = gm.Model([gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, OUT)], [GLOBAL_BATCH, IN])
     print(json.dumps(gemm_isolated(lib, model, GLOBAL_BATCH, args.reps)), flush=True)
+    return 0
+
+
+def run_eval_only(args):
+    """Evaluation of the workload's model at batch 8192 (NoGrad forward,
+    Argmax of every row and the correct count on the device, one 8-byte
+    count read back per batch), and the Argmax kernel alone on the 8192 x
+    1000 logits against HBM bandwidth. Prints one JSON line."""
+    import torch
+
+    from gotensor import model as gm
+    from gotensor._lib import check, cuda_lib
+    lib = cuda_lib()
+    model = gm.Model([gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, HID), gm.ReLU(), gm.Linear(HID, OUT)],
+                     [GLOBAL_BATCH, IN])
+    rng = np.random.default_rng(1)
+    model.set_flat_params((rng.standard_normal(model.num_params) * 0.01).astype(np.float32))
+    model.set_batch(rng.standard_normal((GLOBAL_BATCH, IN)).astype(np.float32), rng.integers(0, OUT, GLOBAL_BATCH))
+    ctx = model.ctx.ptr
+    for _ in range(max(args.warmup, 3)):
+        model.count_correct()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.count_correct()
+    wall = (time.perf_counter() - t0) / args.steps
+    # the Argmax kernel alone, CUDA events on the context's stream
+    logits = model.ctx.alloc(GLOBAL_BATCH * OUT * 4)
+    preds = model.ctx.alloc(GLOBAL_BATCH * 4)
+    h = rng.standard_normal(GLOBAL_BATCH * OUT).astype(np.float32)
+    check(lib.gt_upload(ctx, logits, h.ctypes.data, h.nbytes))
+    for _ in range(3):
+        check(lib.gt_argmax_rows(ctx, 0, logits, GLOBAL_BATCH, OUT, preds))
+    check(lib.gt_mark(ctx, 0))
+    reps = 50
+    for _ in range(reps):
+        check(lib.gt_argmax_rows(ctx, 0, logits, GLOBAL_BATCH, OUT, preds))
+    check(lib.gt_mark(ctx, 1))
+    ms = ctypes.c_float()
+    check(lib.gt_elapsed_ms(ctx, 0, 1, ctypes.byref(ms)))
+    per = ms.value / reps
+    nbytes = GLOBAL_BATCH * OUT * 4 + GLOBAL_BATCH * 4
+    hbm, _, kind = peaks()
+    gbs = nbytes / (per / 1e3) / 1e9
+    model.ctx.release(logits)
+    model.ctx.release(preds)
+    print(json.dumps({"metric": "eval samples/sec (forward + argmax + correct count)", "value": GLOBAL_BATCH / wall,
+                      "unit": "samples/s", "ms_per_batch": wall * 1e3, "workload": WORKLOAD + "_eval",
+                      "argmax_kernel": {"bound": "hbm", "ms": per, "bytes": nbytes, "achieved": gbs,
+                                        "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                                        "note": f"logits 8192 x 1000 fp32 + int32 indices; peak = {kind} copy "
+                                                "bandwidth (the logits fit in L2 across repetitions)"}}),
+          flush=True)
     return 0
 
 

@@ -91,6 +91,8 @@ CUDA_API = {
     "gt_conv_bwd_weight": ("err", [_P, _INT, _P, _P, _P, _P, ctypes.POINTER(GtGeom), _I64]),
     "gt_maxpool_fwd_idx": ("err", [_P, _INT, _P, _P, _P, ctypes.POINTER(GtGeom)]),
     "gt_maxpool_bwd_idx": ("err", [_P, _INT, _P, _P, _P, _INT, _P, ctypes.POINTER(GtGeom)]),
+    "gt_argmax_rows": ("err", [_P, _INT, _P, _I64, _I64, _P]),
+    "gt_count_equal": ("err", [_P, _P, _P, _I64, _P]),
     "gt_xent_fwd_bwd": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P]),
     "gt_xent_fwd_bwd_noalloc": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P]),
     "gt_sgd_step": ("err", [_P, _INT, _P, _P, _P, _I64, ctypes.POINTER(SgdCfg), _INT]),
@@ -152,6 +154,8 @@ HOST_API = {
     "gth_loss": ("err", [_P, ctypes.POINTER(_D)]),
     "gth_forward": ("err", [_P, _P]),
     "gth_step_launches": (_INT, [_P]),
+    "gth_predict": ("err", [_P, _P]),
+    "gth_count_correct": ("err", [_P, ctypes.POINTER(_I64)]),
     "gth_dp_init": ("err", [_P, _INT, _INT, ctypes.c_char_p, _INT, _I64]),
     "gth_bucket_plan": (_INT, [ctypes.POINTER(_I64), _INT, _I64, ctypes.POINTER(_I64), _INT]),
 }

@@ -204,6 +204,20 @@ class Model:
         check(self.lib.gth_forward(self.ptr, out.ctypes.data))
         return out
 
+    def predict(self) -> np.ndarray:
+        """Forward of the current batch and Argmax of every row on the device
+        (model.Forward(x).Argmax(), tensor/ops.go:176-192): int32 (batch,)."""
+        out = np.empty(self.input_shape[0], dtype=np.int32)
+        check(self.lib.gth_predict(self.ptr, out.ctypes.data))
+        return out
+
+    def count_correct(self) -> int:
+        """Rows of the current batch whose Argmax equals their label, counted
+        on the device (the accuracy loop of examples/mnist/main.go:120-133)."""
+        out = ctypes.c_int64()
+        check(self.lib.gth_count_correct(self.ptr, ctypes.byref(out)))
+        return out.value
+
     @property
     def step_launches(self) -> int:
         return self.lib.gth_step_launches(self.ptr)

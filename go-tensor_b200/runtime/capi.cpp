@@ -111,6 +111,18 @@ GT_API char* gth_loss(gth_model* m, double* out) {
 }
 GT_API char* gth_forward(gth_model* m, void* logits_host) { return guard([&] { m->m->forward_eval(logits_host); }); }
 GT_API int gth_step_launches(const gth_model* m) { return m->m->step_launches(); }
+GT_API char* gth_predict(gth_model* m, int32_t* predictions_host) {
+  return guard([&] {
+    if (!predictions_host) throw Error("gth_predict: null output");
+    m->m->predict(predictions_host, nullptr);
+  });
+}
+GT_API char* gth_count_correct(gth_model* m, int64_t* correct) {
+  return guard([&] {
+    if (!correct) throw Error("gth_count_correct: null output");
+    m->m->predict(nullptr, correct);
+  });
+}
 
 GT_API char* gth_dp_init(gth_model* m, int rank, int world, const unsigned char id[128], int timeout_ms,
                          int64_t bucket_bytes) {

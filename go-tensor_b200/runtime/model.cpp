@@ -515,6 +515,21 @@ double Model::loss() {
   return out;
 }
 
+void Model::predict(int32_t* preds, int64_t* correct) {
+  if (!pred_.get()) {
+    pred_ = DevBuf(ctx_, batch_ * sizeof(int32_t));
+    count_ = DevBuf(ctx_, sizeof(int64_t));
+  }
+  begin_read();
+  const int32_t* labels = labels_device();  // the pair this evaluation reads
+  forward();
+  check(gt_argmax_rows(ctx_, dtype_, ops_.back().out, batch_, classes_, (int32_t*)pred_.get()));
+  if (correct) check(gt_count_equal(ctx_, (const int32_t*)pred_.get(), labels, batch_, (int64_t*)count_.get()));
+  end_read();
+  if (preds) check(gt_download(ctx_, preds, pred_.get(), batch_ * sizeof(int32_t)));
+  if (correct) check(gt_download(ctx_, correct, count_.get(), sizeof(int64_t)));
+}
+
 void Model::forward_eval(void* logits_host) {
   begin_read();
   forward();

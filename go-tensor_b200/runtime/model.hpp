@@ -116,6 +116,9 @@ class Model {
   void enable_graph(bool on);
   double loss();
   void forward_eval(void* logits_host);
+  // Evaluation reduced on the device: per-row Argmax to host (if preds) and
+  // the number of rows whose Argmax equals the label (if correct).
+  void predict(int32_t* preds, int64_t* correct);
   int step_launches() const { return launches_; }
 
   void dp_init(int rank, int world, const unsigned char id[128], int timeout_ms, int64_t bucket_bytes);
@@ -152,6 +155,7 @@ class Model {
   std::vector<std::pair<int, int>> input_refs_;  // (op, 0 = in / 1 = out) that point at the input
   int64_t input_bytes_ = 0;
   DevBuf loss_, grad_a_, grad_b_;
+  DevBuf pred_, count_;  // evaluation outputs (allocated on first use)
   int64_t grad_elems_ = 0;
 
   enum { OPT_NONE, OPT_SGD, OPT_ADAM } opt_ = OPT_NONE;

@@ -196,6 +196,17 @@ GT_API char* gt_maxpool_fwd_idx(gt_ctx* ctx, int dtype, const void* x, void* out
 GT_API char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t* idx, const void* pooled,
                          int relu_mask, void* dx, const gt_geom* g);
 
+/* out[r] (int32) = Tensor.Argmax of row r of x (rows x n) (tensor/ops.go:176-192):
+ * the first index of the row's maximum, comparing as the reference does
+ * (x[j] > x[best], starting from index 0), so a NaN at index 0 is returned and
+ * a NaN elsewhere is never chosen. n >= 1. */
+GT_API char* gt_argmax_rows(gt_ctx* ctx, int dtype, const void* x, int64_t rows, int64_t n, int32_t* out);
+/* *count (device int64, overwritten) = number of i < n with a[i] == b[i]: the
+ * correct-prediction count of the reference's accuracy loop
+ * (examples/mnist/main.go:120-133), computed without copying predictions to
+ * the host. */
+GT_API char* gt_count_equal(gt_ctx* ctx, const int32_t* a, const int32_t* b, int64_t n, int64_t* count);
+
 /* Softmax cross-entropy over logits (B, C) with int32 labels on the device:
  * loss (1 element, device) = -mean_i log softmax(x_i)[y_i] and, if dlogits is
  * not NULL, dlogits = (softmax(x) - onehot(y)) / B. Replaces CrossEntropyLoss

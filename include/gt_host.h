@@ -103,6 +103,12 @@ GT_API char* gth_enable_graph(gth_model* m, int on);
 GT_API char* gth_loss(gth_model* m, double* out);
 /* Evaluation forward pass (no gradients): logits (batch, classes) to host. */
 GT_API char* gth_forward(gth_model* m, void* logits_host);
+/* Evaluation of the batch in the input buffers (no gradients), reduced on
+ * the device: the model.Forward(x).Argmax() of every row as int32 (batch
+ * values to host), or the number of rows whose Argmax equals the label
+ * (NoGrad accuracy loop, examples/mnist/main.go:120-133). */
+GT_API char* gth_predict(gth_model* m, int32_t* predictions_host);
+GT_API char* gth_count_correct(gth_model* m, int64_t* correct);
 /* Number of GPU kernel launches one training step issues (the plan's size). */
 GT_API int gth_step_launches(const gth_model* m);
 
