@@ -479,6 +479,8 @@ def main():
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the dominant kernel (the backward GEMMs at the workload's shapes), for profiling")
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--checkpoint-only", action="store_true",
+                    help="time checkpoints of the workload's model (safetensors F32 and GOTN, save and load)")
     ap.add_argument("--eval-only", action="store_true",
                     help="time evaluation instead (forward + Argmax + correct count on the device)")
     args = ap.parse_args()
@@ -490,6 +492,8 @@ def main():
         return run_gemm_only(args)
     if args.eval_only:
         return run_eval_only(args)
+    if args.checkpoint_only:
+        return run_checkpoint_only(args)
     return run_ours(args)
 
 
@@ -501,6 +505,47 @@ def run_gemm_only(args):
     lib = cuda_lib()
     model = gm.Model([gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, OUT)], [GLOBAL_BATCH, IN])
     print(json.dumps(gemm_isolated(lib, model, GLOBAL_BATCH, args.reps)), flush=True)
+    return 0
+
+
+def run_checkpoint_only(args):
+    """Checkpoints of the workload's model (37.7M float32 parameters) through
+    the native writer and reader, to a file in memory-backed /dev/shm when
+    there is one (so the file system does not dominate). Prints one JSON
+    line with the wall time and file bytes per second of each."""
+    from gotensor import model as gm
+    from gotensor._lib import check
+    model = gm.Model([gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, HID), gm.ReLU(), gm.Linear(HID, OUT)],
+                     [GLOBAL_BATCH, IN])
+    rng = np.random.default_rng(1)
+    model.set_flat_params(rng.standard_normal(model.num_params).astype(np.float32))
+    lib = model.lib
+    folder = "/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir()
+    out = {}
+    for fmt in ("safetensors_f32", "gotn_f64"):
+        path = os.path.join(folder, f"gotensor_bench.{fmt}")
+        if fmt.startswith("safetensors"):
+            save = lambda: check(lib.gth_save_safetensors(model.ptr, path.encode(), b"F32", None, None, 0))
+            load = lambda: check(lib.gth_load_safetensors(model.ptr, path.encode(), 1))
+        else:
+            save = lambda: check(lib.gth_save_gotn(model.ptr, path.encode()))
+            load = lambda: check(lib.gth_load_gotn(model.ptr, path.encode()))
+        res = {}
+        for name, fn in (("save", save), ("load", load)):
+            fn()
+            times = []
+            for _ in range(max(args.steps, 3)):
+                t = time.perf_counter()
+                fn()
+                model.ctx.sync()
+                times.append(time.perf_counter() - t)
+            size = os.path.getsize(path)
+            res[name] = {"ms": 1e3 * statistics.median(times), "file_bytes": size,
+                         "gb_per_s": size / statistics.median(times) / 1e9}
+        os.unlink(path)
+        out[fmt] = res
+    print(json.dumps({"metric": "checkpoint of the wide MLP (37.7M float32 parameters)", "folder": folder,
+                      "results": out}), flush=True)
     return 0
 
 

@@ -155,6 +155,15 @@ HOST_API = {
     "gth_forward": ("err", [_P, _P]),
     "gth_step_launches": (_INT, [_P]),
     "gth_predict": ("err", [_P, _P]),
+    "gth_save_safetensors": ("err", [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p),
+                                     ctypes.POINTER(ctypes.c_char_p), _INT]),
+    "gth_load_safetensors": ("err", [_P, ctypes.c_char_p, _INT]),
+    "gth_save_gotn": ("err", [_P, ctypes.c_char_p]),
+    "gth_load_gotn": ("err", [_P, ctypes.c_char_p]),
+    "gth_safetensors_read": ("err", [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), _I64,
+                                     ctypes.POINTER(_I64), _INT, ctypes.POINTER(_INT), ctypes.POINTER(_I64)]),
+    "gth_safetensors_metadata": ("err", [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _INT,
+                                         ctypes.POINTER(_INT)]),
     "gth_count_correct": ("err", [_P, ctypes.POINTER(_I64)]),
     "gth_dp_init": ("err", [_P, _INT, _INT, ctypes.c_char_p, _INT, _I64]),
     "gth_bucket_plan": (_INT, [ctypes.POINTER(_I64), _INT, _I64, ctypes.POINTER(_I64), _INT]),

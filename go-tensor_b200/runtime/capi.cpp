@@ -117,6 +117,34 @@ GT_API char* gth_predict(gth_model* m, int32_t* predictions_host) {
     m->m->predict(predictions_host, nullptr);
   });
 }
+GT_API char* gth_save_safetensors(gth_model* m, const char* path, const char* dtype, const char* const* meta_keys,
+                                  const char* const* meta_values, int n_meta) {
+  return guard([&] {
+    if (!path || !dtype || n_meta < 0 || (n_meta > 0 && (!meta_keys || !meta_values)))
+      throw Error("gth_save_safetensors: bad arguments");
+    std::vector<std::pair<std::string, std::string>> meta;
+    for (int i = 0; i < n_meta; i++) meta.emplace_back(meta_keys[i], meta_values[i]);
+    m->m->save_safetensors(path, dtype, meta);
+  });
+}
+GT_API char* gth_load_safetensors(gth_model* m, const char* path, int strict) {
+  return guard([&] {
+    if (!path) throw Error("gth_load_safetensors: null path");
+    m->m->load_safetensors(path, strict != 0);
+  });
+}
+GT_API char* gth_save_gotn(gth_model* m, const char* path) {
+  return guard([&] {
+    if (!path) throw Error("gth_save_gotn: null path");
+    m->m->save_gotn(path);
+  });
+}
+GT_API char* gth_load_gotn(gth_model* m, const char* path) {
+  return guard([&] {
+    if (!path) throw Error("gth_load_gotn: null path");
+    m->m->load_gotn(path);
+  });
+}
 GT_API char* gth_count_correct(gth_model* m, int64_t* correct) {
   return guard([&] {
     if (!correct) throw Error("gth_count_correct: null output");

@@ -71,6 +71,7 @@ Model::Model(gt_ctx* ctx, int dtype, const std::vector<gth_layer>& layers, const
 
 Model::~Model() {
   drop_graph();
+  gt_host_free(staging_);
   free_bucket_events();
   for (int p = 0; p < 2; p++) {
     gt_event_free(ready_[p]);

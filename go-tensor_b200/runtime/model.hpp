@@ -119,6 +119,12 @@ class Model {
   // Evaluation reduced on the device: per-row Argmax to host (if preds) and
   // the number of rows whose Argmax equals the label (if correct).
   void predict(int32_t* preds, int64_t* correct);
+  // Checkpoints (checkpoint.cpp): safetensors by name, GOTN v1 by position.
+  void save_safetensors(const std::string& path, const std::string& dtype,
+                        const std::vector<std::pair<std::string, std::string>>& metadata);
+  void load_safetensors(const std::string& path, bool strict);
+  void save_gotn(const std::string& path);
+  void load_gotn(const std::string& path);
   int step_launches() const { return launches_; }
 
   void dp_init(int rank, int world, const unsigned char id[128], int timeout_ms, int64_t bucket_bytes);
@@ -156,6 +162,10 @@ class Model {
   int64_t input_bytes_ = 0;
   DevBuf loss_, grad_a_, grad_b_;
   DevBuf pred_, count_;  // evaluation outputs (allocated on first use)
+  // Pinned host copy of the flat parameter buffer in the device layout, for
+  // checkpoints (allocated on first use, kept for the next).
+  void* staging_ = nullptr;
+  char* param_staging();
   int64_t grad_elems_ = 0;
 
   enum { OPT_NONE, OPT_SGD, OPT_ADAM } opt_ = OPT_NONE;

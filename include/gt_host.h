@@ -109,6 +109,35 @@ GT_API char* gth_forward(gth_model* m, void* logits_host);
  * (NoGrad accuracy loop, examples/mnist/main.go:120-133). */
 GT_API char* gth_predict(gth_model* m, int32_t* predictions_host);
 GT_API char* gth_count_correct(gth_model* m, int64_t* correct);
+/* ---- checkpoints ------------------------------------------------------------
+ * The parameters come from (and go to) the device in one copy of the flat
+ * buffer, in the model's dtype; the reference goes through float64 host
+ * copies of every tensor (Tensor.Float64s).
+ *
+ * safetensors.Save(path, nn.StateDict(m), dtype, metadata)
+ * (weights/safetensors/safetensors.go:116-175): the same bytes; dtype is "F32"
+ * or "F64"; n_meta key/value strings (or none). */
+GT_API char* gth_save_safetensors(gth_model* m, const char* path, const char* dtype, const char* const* meta_keys,
+                                  const char* const* meta_values, int n_meta);
+/* safetensors.Load(path) + nn.LoadStateDict(m, sd, strict)
+ * (safetensors.go:55-100, nn/state.go:84-126): every dtype of the format, the
+ * reference's checks and error messages; all or nothing. */
+GT_API char* gth_load_safetensors(gth_model* m, const char* path, int strict);
+/* nn.SaveFile / nn.LoadFile (nn/serialize.go:11-89): GOTN v1, parameters by
+ * position as float64. Loading applies nothing unless the whole file is
+ * read (the reference copies parameter by parameter as it reads). */
+GT_API char* gth_save_gotn(gth_model* m, const char* path);
+GT_API char* gth_load_gotn(gth_model* m, const char* path);
+/* One tensor of a safetensors file as float64 (safetensors.Load for one
+ * name): *numel values into out (cap of them; NULL to query), its shape into
+ * shape (up to shape_cap dims) and *ndim. A scalar (shape []) holds one value.
+ * Host only. */
+GT_API char* gth_safetensors_read(const char* path, const char* name, double* out, int64_t cap, int64_t* shape,
+                                  int shape_cap, int* ndim, int64_t* numel);
+/* The "__metadata__" value for key (NUL-terminated, truncated to cap - 1
+ * bytes; *len = its full length). Host only. */
+GT_API char* gth_safetensors_metadata(const char* path, const char* key, char* value, int cap, int* len);
+
 /* Number of GPU kernel launches one training step issues (the plan's size). */
 GT_API int gth_step_launches(const gth_model* m);
 

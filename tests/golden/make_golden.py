@@ -1,4 +1,5 @@
-"""Regenerates the golden fixtures in this folder from go-tensor's own test data.
+"""Regenerates the golden fixtures in this folder from go-tensor's own test data
+(numbers and data files only, no code).
 
 go-tensor's weight-loading test (weights/weights_test.go:18-74) checks its
 forward pass of a small CNN against PyTorch's output for the same input. The
@@ -16,6 +17,7 @@ Usage: python tests/golden/make_golden.py [reference_root]
 """
 import json
 import os
+import shutil
 import sys
 
 from safetensors.numpy import load_file
@@ -34,10 +36,25 @@ def main(root: str) -> None:
         "params": {k: {"shape": list(v.shape), "values": [float(x) for x in v.reshape(-1)]}
                    for k, v in sorted(weights.items())},
     }
-    dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "cnn_forward.json")
+    here = os.path.dirname(os.path.abspath(__file__))
+    dst = os.path.join(here, "cnn_forward.json")
     with open(dst, "w") as f:
         json.dump(out, f, indent=1)
     print("wrote", dst)
+
+    # The safetensors decoder's known answers (weights/safetensors/
+    # safetensors_test.go:12-21): zoo.safetensors holds one tensor of every
+    # dtype the format defines, with metadata; zoo_expected.json its values.
+    # cnn.safetensors is the PyTorch-written weight file of the CNN above.
+    for name in ("zoo.safetensors", "cnn.safetensors"):
+        shutil.copyfile(os.path.join(data, name), os.path.join(here, name))
+        print("copied", name)
+    with open(os.path.join(data, "zoo_expected.json")) as f:
+        zoo = json.load(f)["safetensors"]
+    with open(os.path.join(here, "zoo_safetensors_expected.json"), "w") as f:
+        json.dump({"source": "go-tensor weights/testdata/zoo_expected.json, entry \"safetensors\"",
+                   "metadata": {"note": "zoo", "format": "pt"}, "tensors": zoo}, f, indent=1)
+    print("wrote zoo_safetensors_expected.json")
 
 
 if __name__ == "__main__":
