@@ -768,10 +768,12 @@ static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k) {
   };
   const double base = std::ceil((double)tiles / pairs) * (num_k + kUnitOverhead);
   double best_cost = base;
-  for (int S = 2; S <= 8 && num_k / S >= 2 * GROUP; S++) {
-    // every tile split
-    double c = std::ceil((double)(tiles * S) / pairs) * (std::ceil((double)num_k / S) + kUnitOverhead) +
-               reduce_cost(tiles, S);
+  for (int S = 2; S <= 64 && num_k / S >= 2 * GROUP; S++) {
+    // every tile split (the workspace holds S partial tiles per tile: at most 1 GB)
+    double c = (double)S * tiles * TILE_ELEMS * 4 > (double)(1ull << 30)
+                   ? INFINITY
+                   : std::ceil((double)(tiles * S) / pairs) * (std::ceil((double)num_k / S) + kUnitOverhead) +
+                         reduce_cost(tiles, S);
     if (c < best_cost) {
       best_cost = c;
       best.whole = 0;

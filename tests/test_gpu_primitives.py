@@ -202,3 +202,24 @@ def test_memory_primitives(dt, npdt, tol):
         be.Write(z, 8, src)
     with pytest.raises(TypeError):
         be.Unary(T.NEG, 0, cpu_backend().FromHost(x))
+
+
+@pytest.mark.parametrize("dt,npdt,bound", [(T.Float32, np.float32, 2.0 ** -20), (T.Float64, np.float64, 1e-14)])
+def test_simt_split_k_long_k(dt, npdt, bound):
+    """A convolution's first-layer weight gradient: 64 x 27 outputs over K =
+    200,000 (the SIMT path, as 27-wide rows are not 16-byte aligned). It runs
+    as many K-splits summed in order: error at the dtype's level against the
+    float64 product, and the same bits on every run."""
+    be = cuda_backend()
+    rng = np.random.default_rng(12)
+    m, k, n = 64, 200_000, 27
+    a = rng.standard_normal(k * m).astype(npdt)  # stored (k, m): dY of the layer
+    b = rng.standard_normal(k * n).astype(npdt)  # stored (k, n): the im2col rows
+    ga, gb = be.FromHost(a), be.FromHost(b)
+    got = be.ToHost(be.MatMul(ga, gb, m, k, n, True, False))
+    A = a.reshape(k, m).T.astype(np.float64)
+    B = b.reshape(k, n).astype(np.float64)
+    exact = A @ B
+    scale = np.abs(A) @ np.abs(B)
+    assert (np.abs(got.reshape(m, n) - exact) / scale).max() <= bound
+    assert np.array_equal(be.ToHost(be.MatMul(ga, gb, m, k, n, True, False)), got)

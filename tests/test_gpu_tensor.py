@@ -8,6 +8,7 @@ import pytest
 from gpu_common import assert_close, cuda_backend
 from gradcases import close_enough, grad_cases, sample_inputs
 from oracle import gotensor_ref as T
+from oracle import nn_ref as nn
 
 pytestmark = pytest.mark.gpu
 
@@ -108,3 +109,34 @@ def test_conv_values_on_cuda():
     got = T.Conv2d(x, w, T.New([10]).To(CUDA0), 1, 0)
     assert list(got.Float64s()) == [22, 26, 34, 38]
     assert list(T.MaxPool2d(x, 2, 1).Float64s()) == [5, 6, 8, 9]
+
+
+LOSS_CASES = {
+    # nn/loss.go:6-22 and the Softmax module (nn/module.go): prediction, target
+    "MSELoss": lambda p, t: nn.MSELoss(p, t),
+    "BCELoss": lambda p, t: nn.BCELoss(p.Sigmoid(), t),
+    "SoftmaxMSE": lambda p, t: nn.MSELoss(nn.NewSoftmax().Forward(p), t),
+}
+
+
+@pytest.mark.parametrize("name", list(LOSS_CASES))
+@pytest.mark.parametrize("dt,tol", [(T.Float32, 1e-4), (T.Float64, 1e-10)])
+def test_losses_on_cuda_match_cpu(name, dt, tol):
+    """The losses and module the fused step does not cover run through the
+    tape on the CUDA device: loss value and prediction gradient as on the CPU."""
+    rng = np.random.default_rng(8)
+    B, C = 64, 10
+    pred = rng.standard_normal(B * C)
+    target = rng.random(B * C)  # in [0, 1): valid for BCE and MSE
+
+    def run(dev):
+        p = T.FromFloat64(pred, B, C).ToDType(dt).To(dev).SetRequiresGrad(True)
+        t = T.FromFloat64(target, B, C).ToDType(dt).To(dev)
+        loss = LOSS_CASES[name](p, t)
+        loss.Backward()
+        return loss.Item(), p.Grad().Float64s()
+
+    cpu_loss, cpu_grad = run(T.CPU)
+    gpu_loss, gpu_grad = run(CUDA0)
+    assert_close(gpu_loss, cpu_loss, tol, f"{name} loss")
+    assert_close(gpu_grad, cpu_grad, tol, f"{name} grad")
