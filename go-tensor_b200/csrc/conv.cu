@@ -8,6 +8,8 @@
 // Here each output element gathers instead, visiting its contributions in the
 // same order the reference adds them, so both are bit-exact and need no
 // atomics.
+#include <algorithm>
+
 #include "gemm.cuh"
 
 namespace gt {
@@ -30,25 +32,71 @@ __global__ void im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, gt_
 }
 
 // x[n][c][ih][iw] = sum over the patches (oh, ow) that read it, in row order.
+// The same, one warp per row of cols: the row's (n, oh, ow) is decoded once
+// and each (c, kh, kw) comes from a table in shared memory, so no element
+// pays for divisions, and a row's K values are written contiguously.
+// 32-bit arithmetic: the host uses it only when every index fits.
 template <typename T>
-__global__ void col2im_kernel(const T* __restrict__ cols, T* __restrict__ x, gt_geom g, int64_t total) {
-  const int64_t K = g.C * g.KH * g.KW;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    int64_t iw = e % g.W, t = e / g.W;
-    int64_t ih = t % g.H, t2 = t / g.H;
-    int64_t c = t2 % g.C, n = t2 / g.C;
-    int64_t hp = ih + g.pad, wp = iw + g.pad;
+__global__ void im2col_rows_kernel(const T* __restrict__ x, T* __restrict__ cols, gt_geom g64, int rows, int K) {
+  extern __shared__ int2 ktab[];  // (offset of (c, kh, kw) in the image, kh << 16 | kw)
+  const int C = (int)g64.C, H = (int)g64.H, W = (int)g64.W, KH = (int)g64.KH, KW = (int)g64.KW;
+  const int OH = (int)g64.OH, OW = (int)g64.OW, stride = (int)g64.stride, pad = (int)g64.pad;
+  const int KHW = KH * KW, HW = H * W, OHW = OH * OW;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const int c = k / KHW, r = k - c * KHW, kh = r / KW, kw = r - kh * KW;
+    ktab[k] = make_int2(c * HW + kh * W + kw, (kh << 16) | kw);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int warps = (int)((gridDim.x * blockDim.x) >> 5);
+  for (int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < rows; row += warps) {
+    const int n = row / OHW, r = row - n * OHW, oh = r / OW, ow = r - oh * OW;
+    const int h0 = oh * stride - pad, w0 = ow * stride - pad;
+    const T* img = x + (int64_t)n * C * HW;
+    T* out = cols + (int64_t)row * K;
+    for (int k = lane; k < K; k += 32) {
+      const int2 t = ktab[k];
+      const int ih = h0 + (t.y >> 16), iw = w0 + (t.y & 0xFFFF);
+      out[k] = (ih >= 0 && ih < H && iw >= 0 && iw < W) ? img[t.x + h0 * W + w0] : (T)0;
+    }
+  }
+}
+
+// dy (N, O, L) -> dyp (O, N, L): contiguous runs of L on both sides.
+template <typename T>
+__global__ void permute_nol_kernel(const T* __restrict__ dy, T* __restrict__ dyp, int64_t N, int64_t O, int64_t L) {
+  for (int64_t r = blockIdx.x; r < O * N; r += gridDim.x) {  // r = o * N + n
+    const int64_t o = r / N, n = r - o * N;
+    const T* src = dy + (n * O + o) * L;
+    T* dst = dyp + r * L;
+    for (int64_t l = threadIdx.x; l < L; l += blockDim.x) dst[l] = src[l];
+  }
+}
+
+// I: the index type, int32_t when every index of the call fits (chosen on the
+// host), which keeps the divisions cheap.
+template <typename T, typename I>
+__global__ void col2im_kernel(const T* __restrict__ cols, T* __restrict__ x, gt_geom g64, I total) {
+  struct {
+    I C, H, W, KH, KW, OH, OW, stride, pad;
+  } g = {(I)g64.C, (I)g64.H, (I)g64.W, (I)g64.KH, (I)g64.KW, (I)g64.OH, (I)g64.OW, (I)g64.stride, (I)g64.pad};
+  const I K = g.C * g.KH * g.KW;
+  for (I e = (I)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
+    I iw = e % g.W, t = e / g.W;
+    I ih = t % g.H, t2 = t / g.H;
+    I c = t2 % g.C, n = t2 / g.C;
+    I hp = ih + g.pad, wp = iw + g.pad;
     // oh*stride <= hp and oh*stride > hp - KH
-    int64_t oh_lo = hp - g.KH + 1 > 0 ? (hp - g.KH + 1 + g.stride - 1) / g.stride : 0;
-    int64_t oh_hi = hp / g.stride < g.OH - 1 ? hp / g.stride : g.OH - 1;
-    int64_t ow_lo = wp - g.KW + 1 > 0 ? (wp - g.KW + 1 + g.stride - 1) / g.stride : 0;
-    int64_t ow_hi = wp / g.stride < g.OW - 1 ? wp / g.stride : g.OW - 1;
+    I oh_lo = hp - g.KH + 1 > 0 ? (hp - g.KH + 1 + g.stride - 1) / g.stride : 0;
+    I oh_hi = hp / g.stride < g.OH - 1 ? hp / g.stride : g.OH - 1;
+    I ow_lo = wp - g.KW + 1 > 0 ? (wp - g.KW + 1 + g.stride - 1) / g.stride : 0;
+    I ow_hi = wp / g.stride < g.OW - 1 ? wp / g.stride : g.OW - 1;
     T acc = (T)0;
-    for (int64_t oh = oh_lo; oh <= oh_hi; oh++) {
-      int64_t kh = hp - oh * g.stride;
-      for (int64_t ow = ow_lo; ow <= ow_hi; ow++) {
-        int64_t kw = wp - ow * g.stride;
-        int64_t row = (n * g.OH + oh) * g.OW + ow;
+    for (I oh = oh_lo; oh <= oh_hi; oh++) {
+      I kh = hp - oh * g.stride;
+      for (I ow = ow_lo; ow <= ow_hi; ow++) {
+        I kw = wp - ow * g.stride;
+        I row = (n * g.OH + oh) * g.OW + ow;
         acc = add_rn(acc, cols[row * K + (c * g.KH + kh) * g.KW + kw]);
       }
     }
@@ -116,18 +164,21 @@ __global__ void maxpool_bwd_kernel(const T* __restrict__ x, const T* __restrict_
 // Non-overlapping windows: each input element lies in at most one window, so
 // dx is grad at the recorded maximum (times relu'(pooled) when the pool
 // follows a ReLU) and zero elsewhere.
-template <typename T>
+template <typename T, typename I>
 __global__ void maxpool_bwd_idx_kernel(const T* __restrict__ grad, const uint8_t* __restrict__ idx,
-                                       const T* __restrict__ pooled, int relu_mask, T* __restrict__ dx, gt_geom g,
-                                       int64_t total) {
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    int64_t iw = e % g.W, t = e / g.W;
-    int64_t ih = t % g.H, pl = t / g.H;
-    int64_t oh = ih / g.stride, ow = iw / g.stride;
-    int64_t kh = ih - oh * g.stride, kw = iw - ow * g.stride;
+                                       const T* __restrict__ pooled, int relu_mask, T* __restrict__ dx, gt_geom g64,
+                                       I total) {
+  struct {
+    I H, W, KH, KW, OH, OW, stride;
+  } g = {(I)g64.H, (I)g64.W, (I)g64.KH, (I)g64.KW, (I)g64.OH, (I)g64.OW, (I)g64.stride};
+  for (I e = (I)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
+    I iw = e % g.W, t = e / g.W;
+    I ih = t % g.H, pl = t / g.H;
+    I oh = ih / g.stride, ow = iw / g.stride;
+    I kh = ih - oh * g.stride, kw = iw - ow * g.stride;
     T v = (T)0;
     if (oh < g.OH && ow < g.OW && kh < g.KH && kw < g.KW) {
-      int64_t w = (pl * g.OH + oh) * g.OW + ow;
+      I w = (pl * g.OH + oh) * g.OW + ow;
       if (idx[w] == (uint8_t)(kh * g.KW + kw)) {
         v = grad[w];
         if (relu_mask) v = mul_rn(v, pooled[w] > (T)0 ? (T)1 : (T)0);
@@ -151,7 +202,15 @@ template <typename T>
 static char* im2col_launch(gt_ctx* ctx, const T* x, T* cols, const gt_geom& g) {
   int64_t total = g.N * g.OH * g.OW * g.C * g.KH * g.KW;
   if (total == 0) return nullptr;
-  im2col_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(x, cols, g, total);
+  const int64_t rows = g.N * g.OH * g.OW, K = g.C * g.KH * g.KW;
+  const bool fits = K <= 6144 && g.KH < 32768 && g.KW < 32768 && rows < INT32_MAX &&
+                    g.C * g.H * g.W < INT32_MAX / 2 && (g.H + 2 * g.pad) * (g.W + 2 * g.pad) < INT32_MAX / 4;
+  if (fits) {
+    const int grid = (int)std::min<int64_t>(ceil_div(rows, 8), (int64_t)ctx->sm_count * 16);
+    im2col_rows_kernel<T><<<grid, 256, K * sizeof(int2), ctx->stream>>>(x, cols, g, (int)rows, (int)K);
+  } else {
+    im2col_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(x, cols, g, total);
+  }
   GT_LAUNCH_CHECK();
   return nullptr;
 }
@@ -160,7 +219,11 @@ template <typename T>
 static char* col2im_launch(gt_ctx* ctx, const T* cols, T* x, const gt_geom& g) {
   int64_t total = g.N * g.C * g.H * g.W;
   if (total == 0) return nullptr;
-  col2im_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(cols, x, g, total);
+  const int64_t colsize = g.N * g.OH * g.OW * g.C * g.KH * g.KW;
+  if (total < INT32_MAX / 2 && colsize < INT32_MAX / 2 && (g.H + g.pad) * g.stride < INT32_MAX / 4)
+    col2im_kernel<T, int32_t><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(cols, x, g, (int32_t)total);
+  else
+    col2im_kernel<T, int64_t><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(cols, x, g, total);
   GT_LAUNCH_CHECK();
   return nullptr;
 }
@@ -232,8 +295,12 @@ char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t
   int64_t total = g->N * g->C * g->H * g->W;
   if (total == 0) return nullptr;
   GT_DISPATCH(dtype, {
-    maxpool_bwd_idx_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(
-        (const T*)grad, idx, (const T*)pooled, relu_mask, (T*)dx, *g, total);
+    if (total < INT32_MAX / 2)
+      maxpool_bwd_idx_kernel<T, int32_t><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(
+          (const T*)grad, idx, (const T*)pooled, relu_mask, (T*)dx, *g, (int32_t)total);
+    else
+      maxpool_bwd_idx_kernel<T, int64_t><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(
+          (const T*)grad, idx, (const T*)pooled, relu_mask, (T*)dx, *g, total);
   });
   GT_LAUNCH_CHECK();
   return nullptr;
@@ -274,11 +341,14 @@ char* gt_conv_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const vo
 
 // dy (N, O, L) -> dyp (O, N*L): the layout of the GEMMs below.
 static char* permute_nol(gt_ctx* ctx, int dtype, const void* dy, void* dyp, int64_t N, int64_t O, int64_t L) {
-  gt_view v{};
-  v.ndim = 3;
-  v.shape[0] = O, v.shape[1] = N, v.shape[2] = L;
-  v.strides[0] = L, v.strides[1] = O * L, v.strides[2] = 1;
-  return gt_copy(ctx, dtype, dy, &v, dyp);
+  if (N * O * L == 0) return nullptr;
+  const int threads = L >= 256 ? 256 : L >= 64 ? 64 : 32;
+  const int blocks = (int)std::min<int64_t>(N * O, (int64_t)ctx->sm_count * 32);
+  GT_DISPATCH(dtype, {
+    permute_nol_kernel<T><<<blocks, threads, 0, ctx->stream>>>((const T*)dy, (T*)dyp, N, O, L);
+  });
+  GT_LAUNCH_CHECK();
+  return nullptr;
 }
 
 char* gt_conv_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db, const gt_geom* g,
