@@ -158,7 +158,16 @@ static char* simt_launch(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B
 template <typename T>
 char* gemm_simt(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>& epi) {
   if (s.M <= 0 || s.N <= 0) return nullptr;
-  if (sizeof(T) == 4) return simt_launch<T, 128, 128, 8, 8, 8>(ctx, s, A, B, epi);
+  if (sizeof(T) == 4) {
+    // Block tile by shape (always 16 x 16 threads): skinny outputs such as a
+    // conv's first-layer weight gradient (64 x 27) would leave most of a
+    // 128 x 128 tile idle.
+    const bool short_m = s.M <= 64, narrow_n = s.N <= 32;
+    if (short_m && narrow_n) return simt_launch<T, 64, 32, 8, 4, 2>(ctx, s, A, B, epi);
+    if (short_m) return simt_launch<T, 64, 128, 8, 4, 8>(ctx, s, A, B, epi);
+    if (narrow_n) return simt_launch<T, 128, 32, 8, 8, 2>(ctx, s, A, B, epi);
+    return simt_launch<T, 128, 128, 8, 8, 8>(ctx, s, A, B, epi);
+  }
   return simt_launch<T, 64, 64, 8, 4, 4>(ctx, s, A, B, epi);
 }
 
