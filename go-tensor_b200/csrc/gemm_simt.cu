@@ -112,6 +112,131 @@ __global__ void simt_split_reduce_kernel(const T* __restrict__ ws, int splits, i
   }
 }
 
+// FP64 main kernel on the FP64 tensor-core path (mma.sync m8n8k4 f64, 256
+// fused multiply-adds per warp instruction, so eight warps per SM keep the
+// pipe busy where DFMA would be issue-bound): a 128 x 128 tile per CTA over
+// 16-deep K slices, staged k-major in shared memory by cp.async (8-byte
+// elements, out-of-range ones zero-filled) in a two-slice ring, so the next
+// slice's loads run under this slice's MMAs. Sixteen warps (four per
+// scheduler, which the MMA latency needs): warp w computes rows
+// 32 * (w / 4) .. +32 and columns 32 * (w % 4) .. +32 as 4 x 4 MMA tiles.
+// Fragment reads: thread t takes k = t % 4 and m (or n) = t / 4 of a tile;
+// with rows of 132 doubles those 32 reads fall in distinct banks.
+namespace f64k {
+constexpr int BM = 128, BN = 128, BK = 16, PITCH = 132, THREADS = 512;
+constexpr int STAGES = 2;  // slices in the shared-memory ring
+constexpr size_t SMEM = (size_t)STAGES * 2 * BK * PITCH * sizeof(double);
+
+__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
+}
+
+__device__ __forceinline__ void mma_f64(double (&c)[2], double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+               : "+d"(c[0]), "+d"(c[1])
+               : "d"(a), "d"(b));
+}
+}  // namespace f64k
+
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(f64k::THREADS, 1)
+    gemm_f64_kernel(GemmShape s, const double* __restrict__ A, const double* __restrict__ B, Epi<double> epi,
+                    int64_t k_per_split, double* __restrict__ ws) {
+  using namespace f64k;
+  extern __shared__ double sm[];
+  double* As = sm;                         // [STAGES][BK][PITCH]
+  double* Bs = sm + STAGES * BK * PITCH;   // [STAGES][BK][PITCH]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = 32 * (warp >> 2), wn = 32 * (warp & 3);
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int64_t k_begin = (int64_t)blockIdx.z * k_per_split;
+  const int64_t k_end = k_begin + k_per_split < s.K ? k_begin + k_per_split : s.K;
+  const int slices = (int)((k_end - k_begin + BK - 1) / BK);
+
+  // Each thread copies 4 elements of A and 4 of B per slice, coalesced along
+  // whichever index is contiguous in global memory (no bytes are read for an
+  // out-of-range element; its address is clamped to the base).
+  auto load = [&](int slice, int stage) {
+    const int64_t k0 = k_begin + (int64_t)slice * BK;
+    double* as = As + stage * BK * PITCH;
+    double* bs = Bs + stage * BK * PITCH;
+#pragma unroll
+    for (int r = 0; r < BM * BK / THREADS; r++) {
+      const int e = tid + THREADS * r;
+      const int kk = TA ? e / BM : e % BK, mm = TA ? e % BM : e / BK;
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      const bool ok = gm < s.M && gk < k_end;
+      cp_async8(as + kk * PITCH + mm, ok ? (TA ? A + gk * s.lda + gm : A + gm * s.lda + gk) : A, ok);
+    }
+#pragma unroll
+    for (int r = 0; r < BN * BK / THREADS; r++) {
+      const int e = tid + THREADS * r;
+      const int kk = TB ? e % BK : e / BN, nn = TB ? e / BK : e % BN;
+      const int64_t gn = n0 + nn, gk = k0 + kk;
+      const bool ok = gn < s.N && gk < k_end;
+      cp_async8(bs + kk * PITCH + nn, ok ? (TB ? B + gn * s.ldb + gk : B + gk * s.ldb + gn) : B, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  double acc[4][4][2];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
+
+  const int fk = lane & 3, fr = lane >> 2;  // fragment k and row / column
+  // One commit group per slice (empty past the end), so waiting until at
+  // most STAGES - 1 groups are pending means slice t has landed.
+#pragma unroll
+  for (int p = 0; p < STAGES - 1; p++) {
+    if (p < slices) load(p, p);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int t = 0; t < slices; t++) {
+    const int next = t + STAGES - 1;
+    if (next < slices) load(next, next % STAGES);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group %0;" ::"n"(STAGES - 1) : "memory");
+    __syncthreads();
+    const double* as = As + (t % STAGES) * BK * PITCH + fk * PITCH + wm + fr;
+    const double* bs = Bs + (t % STAGES) * BK * PITCH + fk * PITCH + wn + fr;
+#pragma unroll
+    for (int k4 = 0; k4 < BK; k4 += 4) {
+      double a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) a[i] = as[k4 * PITCH + 8 * i];
+#pragma unroll
+      for (int j = 0; j < 4; j++) b[j] = bs[k4 * PITCH + 8 * j];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) mma_f64(acc[i][j], a[i], b[j]);
+    }
+    __syncthreads();  // the stage is refilled STAGES - 1 slices on
+  }
+
+  // Thread t holds C(8 i + t / 4, 8 j + 2 (t % 4) + {0, 1}) of the warp's tile.
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int64_t m = m0 + wm + 8 * i + fr;
+    if (m >= s.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int64_t n = n0 + wn + 8 * j + 2 * fk + h;
+        if (n >= s.N) continue;
+        if (ws)
+          ws[((int64_t)blockIdx.z * s.M + m) * s.N + n] = acc[i][j][h];
+        else
+          epi.store(m, n, acc[i][j][h]);
+      }
+    }
+  }
+}
+
 // Splits for a launch of `blocks` output tiles: enough to give every SM two
 // blocks, each split at least 128 deep in K, at most 1024 splits and a 256 MB
 // workspace.
@@ -155,20 +280,71 @@ static char* simt_launch(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B
   return nullptr;
 }
 
+// The FP64 main kernel (one CTA per SM). K is split when the tiles cannot
+// fill the SMs once: S = SMs / tiles ways, each split at least 256 deep.
+template <bool TA, bool TB>
+static char* f64_launch(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
+  using namespace f64k;
+  const int64_t gx = ceil_div(s.N, BN), gy = ceil_div(s.M, BM);
+  if (gy > 65535) return errorf("gemm_simt: M = %lld is too large", (long long)s.M);
+  auto kern = gemm_f64_kernel<TA, TB>;
+  static bool configured[64] = {};
+  if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
+    GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
+    if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
+  }
+  int64_t S = gx * gy < ctx->sm_count ? ctx->sm_count / (gx * gy) : 1;
+  S = S < s.K / 256 ? S : s.K / 256;
+  while (S > 1 && (double)S * s.M * s.N * sizeof(double) > (double)(256u << 20)) S /= 2;
+  if (S <= 1) {
+    kern<<<dim3((unsigned)gx, (unsigned)gy), THREADS, SMEM, ctx->stream>>>(s, A, B, epi, s.K, nullptr);
+    GT_LAUNCH_CHECK();
+    return nullptr;
+  }
+  const int64_t k_per = ceil_div(ceil_div(s.K, S), (int64_t)BK) * BK;
+  const int splits = (int)ceil_div(s.K, k_per);
+  void* ws = nullptr;
+  GT_TRY(scratch(ctx, (size_t)splits * s.M * s.N * sizeof(double), &ws));
+  kern<<<dim3((unsigned)gx, (unsigned)gy, (unsigned)splits), THREADS, SMEM, ctx->stream>>>(s, A, B, epi, k_per,
+                                                                                         (double*)ws);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    simt_split_reduce_kernel<double>
+        <<<grid_for(ctx, s.M * s.N, 256), 256, 0, ctx->stream>>>((const double*)ws, splits, s.M, s.N, epi);
+    count_launch();
+    e = cudaGetLastError();
+  }
+  release(ctx, ws);
+  if (e != cudaSuccess) return cuda_error(e, "gemm_f64 launch", __FILE__, __LINE__);
+  return nullptr;
+}
+
+static char* f64_main(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
+  if (s.trans_a) return s.trans_b ? f64_launch<true, true>(ctx, s, A, B, epi) : f64_launch<true, false>(ctx, s, A, B, epi);
+  return s.trans_b ? f64_launch<false, true>(ctx, s, A, B, epi) : f64_launch<false, false>(ctx, s, A, B, epi);
+}
+
 template <typename T>
 char* gemm_simt(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>& epi) {
   if (s.M <= 0 || s.N <= 0) return nullptr;
-  if (sizeof(T) == 4) {
-    // Block tile by shape (always 16 x 16 threads): skinny outputs such as a
-    // conv's first-layer weight gradient (64 x 27) would leave most of a
-    // 128 x 128 tile idle.
-    const bool short_m = s.M <= 64, narrow_n = s.N <= 32;
-    if (short_m && narrow_n) return simt_launch<T, 64, 32, 8, 4, 2>(ctx, s, A, B, epi);
-    if (short_m) return simt_launch<T, 64, 128, 8, 4, 8>(ctx, s, A, B, epi);
-    if (narrow_n) return simt_launch<T, 128, 32, 8, 8, 2>(ctx, s, A, B, epi);
+  // float64 outputs of at least 128 x 128 with K long enough to amortise the
+  // one-CTA-per-SM epilogue go to the tensor-core kernel.
+  if constexpr (sizeof(T) == 8)
+    if (s.M >= 128 && s.N >= 128 && s.K >= 128) return f64_main(ctx, s, A, B, epi);
+  // Block tile by shape (always 16 x 16 threads): skinny outputs such as a
+  // conv's first-layer weight gradient (64 x 27) or a 10-class classifier
+  // (and its 10-row weight gradient) would leave most of a square tile idle.
+  const bool tiny_m = s.M <= 16, short_m = s.M <= 64, narrow_n = s.N <= 32;
+  if (tiny_m) return narrow_n ? simt_launch<T, 16, 32, 8, 1, 2>(ctx, s, A, B, epi)
+                              : simt_launch<T, 16, 128, 8, 1, 8>(ctx, s, A, B, epi);
+  if (short_m && narrow_n) return simt_launch<T, 64, 32, 8, 4, 2>(ctx, s, A, B, epi);
+  if (short_m) return simt_launch<T, 64, 128, 8, 4, 8>(ctx, s, A, B, epi);
+  if (narrow_n) return simt_launch<T, 128, 32, 8, 8, 2>(ctx, s, A, B, epi);
+  if constexpr (sizeof(T) == 4)
     return simt_launch<T, 128, 128, 8, 8, 8>(ctx, s, A, B, epi);
-  }
-  return simt_launch<T, 64, 64, 8, 4, 4>(ctx, s, A, B, epi);
+  else
+    return simt_launch<T, 64, 64, 8, 4, 4>(ctx, s, A, B, epi);
 }
 
 template char* gemm_simt<float>(gt_ctx*, const GemmShape&, const float*, const float*, const Epi<float>&);

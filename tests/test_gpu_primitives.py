@@ -112,7 +112,7 @@ def test_reduce_max_nan_and_signed_zero():
 
 @pytest.mark.parametrize("dt,npdt,tol", DTYPES)
 @pytest.mark.parametrize("mkn", [(2, 3, 2), (70, 50, 40), (257, 129, 65), (64, 784, 128), (33, 17, 9), (1, 1, 1),
-                                 (300, 1000, 10), (512, 256, 384)])
+                                 (300, 1000, 10), (512, 256, 384), (10, 4096, 200), (16, 70, 129)])
 def test_matmul_trans(dt, npdt, tol, mkn):
     """Activations N(0,1) against weight-scaled operands U(+-1/sqrt(k)) (the
     scales a training step multiplies) at the device tolerance; unscaled
@@ -131,6 +131,28 @@ def test_matmul_trans(dt, npdt, tol, mkn):
                 want = cpu_backend().MatMul(ca, cb, m, k, n, ta, tb).data
                 got = cuda_backend().ToHost(cuda_backend().MatMul(ga, gb, m, k, n, ta, tb))
                 assert_close(got, want, t, f"matmul {mkn} ta={ta} tb={tb} weight_like={weight_like}")
+
+
+@pytest.mark.parametrize("mkn", [(130, 33, 129), (1100, 64, 1500), (384, 1000, 256), (512, 2048, 512)])
+def test_matmul_f64_main_kernel(mkn):
+    """The float64 kernel for outputs of at least 128 x 128: ragged tiles in
+    both directions, K not a multiple of its 16-deep slices, and K-splits
+    (3 ways for 384 x 256 over K = 1000, 8 ways for 512 x 512 over K = 2048),
+    in all four transpose layouts, against the oracle at the float64 device
+    tolerance, and the same bits on a second run."""
+    m, k, n = mkn
+    rng = np.random.default_rng(m + 7 * k + n)
+    be = cuda_backend()
+    for ta in (False, True):
+        for tb in (False, True):
+            a = rng.standard_normal(m * k)
+            b = rng.standard_normal(k * n) / np.sqrt(k)
+            ca, ga = both(a)
+            cb, gb = both(b)
+            want = cpu_backend().MatMul(ca, cb, m, k, n, ta, tb).data
+            got = be.ToHost(be.MatMul(ga, gb, m, k, n, ta, tb))
+            assert_close(got, want, 1e-10, f"f64 matmul {mkn} ta={ta} tb={tb}")
+            assert np.array_equal(be.ToHost(be.MatMul(ga, gb, m, k, n, ta, tb)), got)
 
 
 def test_matmul_known_values():
