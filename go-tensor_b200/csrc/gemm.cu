@@ -85,6 +85,24 @@ static char* gemm_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const flo
 
 using namespace gt;
 
+namespace gt {
+
+// bits[n * ldw + b] bit j = (y[32 b + j][n] > 0), ldw = ceil(M / 32): a
+// thread per word; consecutive threads take consecutive columns, so each of
+// the 32 row reads is coalesced.
+template <typename T>
+__global__ void relu_bits_kernel(const T* __restrict__ y, uint32_t* __restrict__ bits, int64_t M, int64_t N,
+                                 int64_t ldw) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < N * ldw; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / N, n = i - b * N;
+    uint32_t w = 0;
+    for (int j = 0; j < 32 && 32 * b + j < M; j++) w |= (uint32_t)(y[(32 * b + j) * N + n] > (T)0) << j;
+    bits[n * ldw + b] = w;
+  }
+}
+
+}  // namespace gt
+
 extern "C" {
 
 char* gt_set_gemm_sm_reserve(gt_ctx* ctx, int sms) {
@@ -211,6 +229,58 @@ char* gt_linear_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, 
       e.dact = act_prev;
       e.ldm = K;
     }
+    return gemm<T>(ctx, s, (const T*)dy, (const T*)w, e);
+  });
+  return nullptr;
+}
+
+char* gt_relu_bits(gt_ctx* ctx, int dtype, const void* y, uint32_t* bits, int64_t M, int64_t N) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M < 0 || N < 0 || (M > 0 && N > 0 && (!y || !bits))) return errorf("gt_relu_bits: bad arguments");
+  if (M == 0 || N == 0) return nullptr;
+  const int64_t ldw = (M + 31) / 32;
+  GT_DISPATCH(dtype, {
+    relu_bits_kernel<T><<<grid_for(ctx, N * ldw, 256), 256, 0, ctx->stream>>>((const T*)y, bits, M, N, ldw);
+  });
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+char* gt_linear_fwd_bits(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y,
+                         uint32_t* bits, int64_t M, int64_t K, int64_t N) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M < 0 || K <= 0 || N < 0 || !bits) return errorf("gt_linear_fwd_bits: bad arguments");
+  if (M == 0 || N == 0) return nullptr;
+  GemmShape s{M, N, K, false, true, K, K};
+  bool fused = false;
+  GT_DISPATCH(dtype, {
+    Epi<T> e;
+    e.out = (T*)y;
+    e.ldc = N;
+    e.bias = (const T*)bias;
+    e.act = GT_ACT_RELU;
+    e.bits_out = (uint32_t*)bits;
+    e.ldw = (M + 31) / 32;
+    GT_TRY(gemm<T>(ctx, s, (const T*)x, (const T*)w, e));
+    fused = sizeof(T) == 4 && g_gemm_taken == 2;  // the tcgen05 epilogues wrote the mask
+  });
+  return fused ? nullptr : gt_relu_bits(ctx, dtype, y, bits, M, N);
+}
+
+char* gt_linear_bwd_data_bits(gt_ctx* ctx, int dtype, const void* dy, const void* w, const uint32_t* bits, void* dx,
+                              int64_t M, int64_t K, int64_t N) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M <= 0 || K <= 0 || N <= 0 || !bits) return errorf("gt_linear_bwd_data_bits: bad arguments");
+  GemmShape s{M, K, N, false, false, N, K};
+  GT_DISPATCH(dtype, {
+    Epi<T> e;
+    e.out = (T*)dx;
+    e.ldc = K;
+    e.dbits = bits;
+    e.ldw = (M + 31) / 32;
     return gemm<T>(ctx, s, (const T*)dy, (const T*)w, e);
   });
   return nullptr;

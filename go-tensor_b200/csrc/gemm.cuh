@@ -25,14 +25,27 @@ struct Epi {
   // nchw_L > 0 stores C (M = channels, N = images * L) into an (images, M, L)
   // tensor: out[(n / L) * M * L + m * L + n % L], with M given in nchw_M.
   int64_t nchw_L = 0, nchw_M = 0;
+  // ReLU bit masks in column words: bit m % 32 of bits[n * ldw + m / 32],
+  // ldw = ceil(M / 32), so a thread that owns column n of 32 rows reads or
+  // writes one word. bits_out (forward): bit = (stored value > 0), written by
+  // the tcgen05 epilogues only (other paths leave it to gt_relu_bits). dbits
+  // (dX): out = acc * (bit ? 1 : 0), ReLU's derivative g * Step(y) read from
+  // the forward's bits instead of the activation itself.
+  uint32_t* bits_out = nullptr;
+  const uint32_t* dbits = nullptr;
+  int64_t ldw = 0;
 
-  __device__ __forceinline__ void store(int64_t m, int64_t n, T acc) const {
+  // The finished value of C(m, n): bias, activation, activation derivative.
+  __device__ __forceinline__ T finish(int64_t m, int64_t n, T acc) const {
     T v = acc;
     if (bias) v = add_rn(v, bias[bias_by_row ? m : n]);
     if (act != GT_ACT_NONE) v = act_fwd(act, v);
     if (dmask) v = act_bwd(dact, v, dmask[m * ldm + n]);
-    put(m, n, v);
+    if (dbits) v = mul_rn(v, ((dbits[n * ldw + (m >> 5)] >> (m & 31)) & 1u) ? (T)1 : (T)0);
+    return v;
   }
+
+  __device__ __forceinline__ void store(int64_t m, int64_t n, T acc) const { put(m, n, finish(m, n, acc)); }
 
   // Writes the finished value of C(m, n) (row-major or the NCHW order).
   __device__ __forceinline__ void put(int64_t m, int64_t n, T v) const {

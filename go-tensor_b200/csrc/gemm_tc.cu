@@ -298,10 +298,16 @@ enum EpiKind : int {
   EK_MASK = 2,       // * act'(mask[m][n]): the dX of a Linear after an activation
   EK_CONV = 3,       // + bias[m] (optional), then ReLU (optional), stored in NCHW order: Conv2d forward
   EK_GENERIC = 4,    // anything else (tanh / sigmoid forward)
+  EK_MASKBITS = 5,   // * Step from a ReLU bit mask: the dX of a Linear after a ReLU
 };
 
 inline int epi_kind(const Epi<float>& e, int64_t n_cols) {
   const bool rowmajor = e.nchw_L == 0;
+  if (e.bits_out)  // only this kind writes the bit mask
+    return !e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask && !e.dbits && rowmajor
+               ? EK_BIAS_RELU
+               : -1;
+  if (e.dbits) return !e.bias && e.act == GT_ACT_NONE && !e.dmask && rowmajor ? EK_MASKBITS : EK_GENERIC;
   if (!e.bias && e.act == GT_ACT_NONE && !e.dmask && rowmajor) return EK_PLAIN;
   if (!e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask && rowmajor) return EK_BIAS_RELU;
   if (!e.bias && e.act == GT_ACT_NONE && e.dmask && rowmajor) return EK_MASK;
@@ -315,24 +321,35 @@ inline int epi_kind(const Epi<float>& e, int64_t n_cols) {
 // owns column n of rows m0 .. m0+31, so each row's access is 128 contiguous
 // bytes. Same operations, in the same order, as Epi::store.
 template <int EK>
-__device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const GemmShape& s, const float* xpose, int lane,
+__device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const GemmShape& s, float* xpose, int lane,
                                                int64_t m0, int64_t n) {
-  if (n >= s.N) return;
   const int rows = (int)(s.M - m0 < 32 ? s.M - m0 : 32);
   float* op = epi.out + m0 * epi.ldc + n;
+  if (n >= s.N) return;
   if (EK == EK_PLAIN) {
 #pragma unroll 4
     for (int r = 0; r < rows; r++) op[r * epi.ldc] = xpose[r * EPI_LD + lane];
   } else if (EK == EK_BIAS_RELU) {
+    // With a bit mask, this lane's column of the block (m0 is a multiple of
+    // 32) becomes one word: bit r = (row r's value > 0).
     const float b = epi.bias ? __ldg(epi.bias + n) : 0.0f;
     const bool relu = epi.act == GT_ACT_RELU;
+    uint32_t w = 0;
 #pragma unroll 4
     for (int r = 0; r < rows; r++) {
       float v = xpose[r * EPI_LD + lane];
       if (epi.bias) v = __fadd_rn(v, b);
       if (relu) v = go_max(v, 0.0f);
       op[r * epi.ldc] = v;
+      w |= (uint32_t)(v > 0.0f) << r;
     }
+    if (epi.bits_out && rows > 0) epi.bits_out[n * epi.ldw + (m0 >> 5)] = w;
+  } else if (EK == EK_MASKBITS) {
+    // One word holds this column's factor for all 32 rows of the block: 4
+    // bytes per lane instead of 128 bytes of activations.
+    const uint32_t w = rows > 0 ? __ldg(epi.dbits + n * epi.ldw + (m0 >> 5)) : 0u;
+#pragma unroll 4
+    for (int r = 0; r < rows; r++) op[r * epi.ldc] = __fmul_rn(xpose[r * EPI_LD + lane], ((w >> r) & 1u) ? 1.0f : 0.0f);
   } else if (EK == EK_MASK) {
     // The mask values of 8 rows are requested before any is used.
     const float* mp = epi.dmask + m0 * epi.ldm + n;
@@ -712,15 +729,22 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
 template <int EK>
 static char* launch_layout(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
                            bool a_mn, bool b_mn, const SplitPlan& sp) {
-  if (!a_mn && !b_mn) return launch<false, false, EK>(ctx, s, A, B, epi, sp);
-  if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi, sp);
-  if (a_mn && !b_mn) return launch<true, false, EK>(ctx, s, A, B, epi, sp);
-  return launch<true, true, EK>(ctx, s, A, B, epi, sp);
+  if constexpr (EK == EK_MASKBITS) {  // only the dX layout (dy row-major, W as N/K-major) is compiled
+    if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi, sp);
+    return launch_layout<EK_GENERIC>(ctx, s, A, B, epi, a_mn, b_mn, sp);
+  } else {
+    if (!a_mn && !b_mn) return launch<false, false, EK>(ctx, s, A, B, epi, sp);
+    if (!a_mn && b_mn) return launch<false, true, EK>(ctx, s, A, B, epi, sp);
+    if (a_mn && !b_mn) return launch<true, false, EK>(ctx, s, A, B, epi, sp);
+    return launch<true, true, EK>(ctx, s, A, B, epi, sp);
+  }
 }
 
 static char* launch_kind(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
                          bool a_mn, bool b_mn, const SplitPlan& sp) {
   switch (epi_kind(epi, s.N)) {
+    case -1: return errorf("gemm_tc: a ReLU bit mask needs a row-major bias / ReLU epilogue");
+    case EK_MASKBITS: return launch_layout<EK_MASKBITS>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_PLAIN: return launch_layout<EK_PLAIN>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_BIAS_RELU: return launch_layout<EK_BIAS_RELU>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_MASK: return launch_layout<EK_MASK>(ctx, s, A, B, epi, a_mn, b_mn, sp);
@@ -744,6 +768,33 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, SplitPlan sp,
     float acc = ws[i];
     for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
     epi.store(m, n, acc);
+  }
+}
+
+// The same with a ReLU bit mask: a thread finishes one column of 32 rows of
+// a split tile (consecutive threads, consecutive columns) and writes its word.
+__global__ void splitk_reduce_bits_kernel(const float* __restrict__ ws, SplitPlan sp, int tiles, int n_tiles,
+                                          int64_t M, int64_t N, Epi<float> epi) {
+  const int rest = tiles - sp.whole;
+  const int64_t total = (int64_t)rest * TILE_ELEMS;
+  const int64_t units = total / 32;  // (tile, 32-row block, column)
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(u / (TILE_ELEMS / 32));
+    const int64_t v = u - (int64_t)r * (TILE_ELEMS / 32);
+    const int rb = (int)(v / BN), c = (int)(v % BN);
+    const int t = sp.whole + r;
+    const int64_t m0 = (int64_t)(t / n_tiles) * 2 * BM + 32 * rb, n = (int64_t)(t % n_tiles) * BN + c;
+    if (m0 >= M || n >= N) continue;
+    uint32_t w = 0;
+    for (int j = 0; j < 32 && m0 + j < M; j++) {
+      const int64_t i = (int64_t)r * TILE_ELEMS + (int64_t)(32 * rb + j) * BN + c;
+      float acc = ws[i];
+      for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
+      const float y = epi.finish(m0 + j, n, acc);
+      epi.put(m0 + j, n, y);
+      w |= (uint32_t)(y > 0.0f) << j;
+    }
+    epi.bits_out[n * epi.ldw + (m0 >> 5)] = w;
   }
 }
 
@@ -837,8 +888,12 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
     // go to the workspace and are summed, in order, by the second kernel.
     err = tc::launch_kind(ctx, s, A, B, epi, a_mn, b_mn, sp);
     if (!err) {
-      tc::splitk_reduce_kernel<<<grid_for(ctx, rest * tc::TILE_ELEMS, 256), 256, 0, ctx->stream>>>(
-          sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
+      if (epi.bits_out)
+        tc::splitk_reduce_bits_kernel<<<grid_for(ctx, rest * tc::TILE_ELEMS / 32, 256), 256, 0, ctx->stream>>>(
+            sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
+      else
+        tc::splitk_reduce_kernel<<<grid_for(ctx, rest * tc::TILE_ELEMS, 256), 256, 0, ctx->stream>>>(
+            sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
       count_launch();
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) err = cuda_error(e, "splitk_reduce_kernel launch", __FILE__, __LINE__);

@@ -83,6 +83,9 @@ CUDA_API = {
     "gt_maxpool_bwd": ("err", [_P, _INT, _P, _P, _P, ctypes.POINTER(GtGeom)]),
     "gt_linear_fwd": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _INT]),
     "gt_linear_bwd_data": ("err", [_P, _INT, _P, _P, _P, _INT, _P, _I64, _I64, _I64]),
+    "gt_relu_bits": ("err", [_P, _INT, _P, _P, _I64, _I64]),
+    "gt_linear_fwd_bits": ("err", [_P, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64]),
+    "gt_linear_bwd_data_bits": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64]),
     "gt_linear_bwd_weight": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64]),
     "gt_act_bwd": ("err", [_P, _INT, _INT, _P, _P, _P, _I64]),
     "gt_bias_act": ("err", [_P, _INT, _P, _P, _I64, _I64, _I64, _INT]),

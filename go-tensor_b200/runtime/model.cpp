@@ -263,6 +263,16 @@ void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t
     if (ops_[i].in == input_[0].get()) input_refs_.emplace_back((int)i, 0);
     if (ops_[i].out == input_[0].get()) input_refs_.emplace_back((int)i, 1);
   }
+  // A float32 Linear + ReLU whose output feeds a Linear that needs dX also
+  // writes the output's sign bits; that dX reads them instead of the output.
+  if (dtype_ == GT_FLOAT32)
+    for (auto& op : ops_) {
+      if (op.kind != Op::LINEAR || !op.needs_dx || op.src < 0) continue;
+      Op& src = ops_[op.src];
+      if (src.kind != Op::LINEAR || src.act != GT_ACT_RELU || src.bits) continue;
+      bits_.emplace_back(ctx_, (size_t)src.N * (size_t)((src.M + 31) / 32) * sizeof(uint32_t));
+      src.bits = (uint32_t*)bits_.back().get();
+    }
   if (shape.size() != 2) throw Error("the model must end in (batch, classes) logits, got " + shape_str(shape));
   if (!seen_params) throw Error("the model has no parameters");
   classes_ = shape[1];
@@ -331,8 +341,12 @@ void Model::forward() {
   for (auto& op : ops_) {
     switch (op.kind) {
       case Op::LINEAR:
-        check(gt_linear_fwd(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, op.M, op.K, op.N,
-                            op.act));
+        if (op.bits)
+          check(gt_linear_fwd_bits(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, op.bits,
+                                   op.M, op.K, op.N));
+        else
+          check(gt_linear_fwd(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, op.M, op.K,
+                              op.N, op.act));
         break;
       case Op::CONV:
         check(gt_conv_fwd(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, &op.g, op.O, op.act));
@@ -390,8 +404,11 @@ void Model::backward(bool join) {
           // into the GEMM epilogue when the producer is a Linear/Conv/act.
           const Op* src = op.src >= 0 ? &ops_[op.src] : nullptr;
           bool fuse = src && src->kind != Op::POOL && src->act != GT_ACT_NONE;
-          check(gt_linear_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, fuse ? op.in : nullptr,
-                                   fuse ? src->act : GT_ACT_NONE, spare, op.M, op.K, op.N));
+          if (fuse && src->bits)
+            check(gt_linear_bwd_data_bits(ctx_, dtype_, g, p + op.w_off * es_, src->bits, spare, op.M, op.K, op.N));
+          else
+            check(gt_linear_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, fuse ? op.in : nullptr,
+                                     fuse ? src->act : GT_ACT_NONE, spare, op.M, op.K, op.N));
           std::swap(g, spare);
           g_pre = fuse;
         }

@@ -84,6 +84,7 @@ struct Op {
   bool needs_dx = true;         // false for the first op with parameters
   bool produces_act = false;    // output is an activation's output (derivative can be fused upstream)
   int src = -1;                 // op that produced this op's input, identities skipped (-1: the batch)
+  uint32_t* bits = nullptr;     // LINEAR + ReLU, float32: bit mask of the output for the next Linear's dX
 };
 
 class Model {
@@ -150,6 +151,7 @@ class Model {
   std::vector<ParamInfo> params_;
   int64_t dense_params_ = 0, dev_params_ = 0;
   std::vector<DevBuf> acts_;  // activation buffers owned by ops
+  std::vector<DevBuf> bits_;  // ReLU bit masks (Op::bits)
   DevBuf pbuf_, gbuf_, opt_a_, opt_b_, step_dev_;
   // Two input/label buffer pairs: while a step reads one, the next batch can
   // be uploaded into the other on the copy stream.

@@ -162,6 +162,21 @@ GT_API char* gt_linear_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w,
  * (tensor/ops.go:110, 116, 123). */
 GT_API char* gt_linear_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, const void* y_prev,
                          int act_prev, void* dx, int64_t M, int64_t K, int64_t N);
+/* ReLU bit masks (no counterpart in the reference, which keeps the ReLU
+ * input and multiplies by Step(x), tensor/ops.go:110): for y (M, N), bit
+ * m % 32 of word bits[n * ceil(M / 32) + m / 32] is (y[m][n] > 0), the factor
+ * the ReLU backward applies; N * ceil(M / 32) words in all. The backward then
+ * reads 1 bit per element instead of the 4-byte activation. */
+/* bits = (y (M, N) > 0), packed. */
+GT_API char* gt_relu_bits(gt_ctx* ctx, int dtype, const void* y, uint32_t* bits, int64_t M, int64_t N);
+/* gt_linear_fwd with act = ReLU that also writes the output's bit mask
+ * (in the GEMM epilogue on the tensor-core path, else by gt_relu_bits). */
+GT_API char* gt_linear_fwd_bits(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y,
+                                uint32_t* bits, int64_t M, int64_t K, int64_t N);
+/* gt_linear_bwd_data with act_prev = ReLU, the factor Step(y_prev) taken from
+ * the bit mask of y_prev (M, K): the same result bit for bit. */
+GT_API char* gt_linear_bwd_data_bits(gt_ctx* ctx, int dtype, const void* dy, const void* w, const uint32_t* bits,
+                                     void* dx, int64_t M, int64_t K, int64_t N);
 /* dw (N, K) = dy (M, N)^T @ x (M, K); db (N) = sum over rows of dy (NULL: skip).
  * Replaces the MatMul backward for the weight (tensor/ops.go:324-326), the
  * Permute backward of W.T() and sumTo for the bias (tensor/ops.go:418-433). */

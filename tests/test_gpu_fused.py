@@ -106,6 +106,52 @@ def test_linear_bwd(dt, npdt, tol, act_prev, mkn):
     assert_close(host(db), want_db, tol, "db")
 
 
+def _relu_bits(y, M, N):
+    """Word (n, b) holds bit j = (y[32 b + j, n] > 0): N rows of ceil(M / 32) words."""
+    ldw = (M + 31) // 32
+    pos = np.zeros((ldw * 32, N), dtype=np.uint64)
+    pos[:M] = np.asarray(y).reshape(M, N) > 0
+    return (pos.T.reshape(N, ldw, 32) << np.arange(32, dtype=np.uint64)).sum(axis=2).astype(np.uint32)
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("mkn2", [(2048, 512, 1024, 96), (256, 8192, 256, 4096), (64, 27, 50, 40),
+                                  (257, 129, 65, 33), (1, 5, 33, 7)])
+def test_relu_bits_forward_and_dx(dt, npdt, tol, mkn2):
+    """gt_linear_fwd_bits stores what gt_linear_fwd with ReLU stores, plus the
+    bits (y > 0) (NaN gives 0); gt_relu_bits packs the same bits; and the next
+    layer's gt_linear_bwd_data_bits equals gt_linear_bwd_data with the ReLU
+    output, bit for bit. The shapes take the tensor-core path whole and
+    K-split (forward and dX), and the SIMT path (K = 27 or 129), with word
+    rows that end mid-word; NaN and infinities come in through the bias."""
+    M, K, N, N2 = mkn2
+    rng = np.random.default_rng(M + 2 * K + N)
+    x = rng.standard_normal((M, K)).astype(npdt)
+    w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(npdt)
+    b = rng.standard_normal(N).astype(npdt)
+    b[1:4] = [np.nan, -np.inf, np.inf]
+    ldw = (M + 31) // 32
+    y1, y2 = new(M * N, dt), new(M * N, dt)
+    bits, bits2 = new(N * ldw, T.Float32), new(N * ldw, T.Float32)  # 4-byte words
+    xd, wd, bd = dev(x), dev(w), dev(b)
+    check(lib().gt_linear_fwd(ctx(), dt, xd.ptr, wd.ptr, bd.ptr, y1.ptr, M, K, N, 1))
+    check(lib().gt_linear_fwd_bits(ctx(), dt, xd.ptr, wd.ptr, bd.ptr, y2.ptr, bits.ptr, M, K, N))
+    check(lib().gt_relu_bits(ctx(), dt, y1.ptr, bits2.ptr, M, N))
+    y = host(y1)
+    assert_bits(host(y2), y, "y")
+    want_bits = _relu_bits(y, M, N)
+    assert np.array_equal(host(bits).view(np.uint32).reshape(N, ldw), want_bits)
+    assert np.array_equal(host(bits2).view(np.uint32).reshape(N, ldw), want_bits)
+    # the next layer: dx (M, N) = dy (M, N2) @ w2 (N2, N) * Step(y)
+    w2 = (rng.standard_normal((N2, N)) / np.sqrt(N)).astype(npdt)
+    dy = (rng.standard_normal((M, N2)) / np.sqrt(M)).astype(npdt)
+    dx1, dx2 = new(M * N, dt), new(M * N, dt)
+    dyd, w2d = dev(dy), dev(w2)
+    check(lib().gt_linear_bwd_data(ctx(), dt, dyd.ptr, w2d.ptr, y1.ptr, 1, dx1.ptr, M, N, N2))
+    check(lib().gt_linear_bwd_data_bits(ctx(), dt, dyd.ptr, w2d.ptr, bits.ptr, dx2.ptr, M, N, N2))
+    assert_bits(host(dx2), host(dx1), "dx")
+
+
 CONVS = [(2, 3, 5, 5, 4, 3, 1, 0), (2, 2, 5, 4, 3, 3, 2, 1), (8, 1, 28, 28, 32, 3, 1, 1), (4, 32, 14, 14, 64, 3, 1, 1),
          (2, 3, 32, 32, 64, 3, 1, 1)]
 
