@@ -329,14 +329,15 @@ def run_ours(args):
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of the GEMM launches of one
-# training step of this workload, from one ncu capture (the command and the
-# per-launch figures are in profiles/wide_mlp_b8192_step_launches.md).
-GEMM_TRAFFIC_BYTES_PER_STEP = 4_503_205_888
+# training step of this workload, from one ncu capture of
+# `bench.py --steps 1 --warmup 3 --skip-cpu` (launches 19-37: the second
+# warm-up step, replayed from the CUDA graph).
+GEMM_TRAFFIC_BYTES_PER_STEP = 4_224_623_616
 GEMM_LAUNCHES_PER_STEP = 8
 # The SGD update: read p, g, v and write p, v (float32), and the DRAM traffic
 # of its launch in the same capture.
 SGD_BYTES_PER_PARAM = 20
-SGD_TRAFFIC_BYTES = 697_423_104
+SGD_TRAFFIC_BYTES = 698_175_488
 
 
 def _peak_3xtf32():

@@ -87,17 +87,17 @@ using namespace gt;
 
 namespace gt {
 
-// bits[n * ldw + b] bit j = (y[32 b + j][n] > 0), ldw = ceil(M / 32): a
-// thread per word; consecutive threads take consecutive columns, so each of
-// the 32 row reads is coalesced.
+// bits[b * N + n] bit j = (y[32 b + j][n] > 0): a thread per word;
+// consecutive threads take consecutive columns, so the 32 row reads and the
+// word stores are coalesced.
 template <typename T>
-__global__ void relu_bits_kernel(const T* __restrict__ y, uint32_t* __restrict__ bits, int64_t M, int64_t N,
-                                 int64_t ldw) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < N * ldw; i += (int64_t)gridDim.x * blockDim.x) {
+__global__ void relu_bits_kernel(const T* __restrict__ y, uint32_t* __restrict__ bits, int64_t M, int64_t N) {
+  const int64_t words = (M + 31) / 32 * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = i / N, n = i - b * N;
     uint32_t w = 0;
     for (int j = 0; j < 32 && 32 * b + j < M; j++) w |= (uint32_t)(y[(32 * b + j) * N + n] > (T)0) << j;
-    bits[n * ldw + b] = w;
+    bits[i] = w;
   }
 }
 
@@ -239,9 +239,8 @@ char* gt_relu_bits(gt_ctx* ctx, int dtype, const void* y, uint32_t* bits, int64_
   GT_CHECK_DTYPE(dtype);
   if (M < 0 || N < 0 || (M > 0 && N > 0 && (!y || !bits))) return errorf("gt_relu_bits: bad arguments");
   if (M == 0 || N == 0) return nullptr;
-  const int64_t ldw = (M + 31) / 32;
   GT_DISPATCH(dtype, {
-    relu_bits_kernel<T><<<grid_for(ctx, N * ldw, 256), 256, 0, ctx->stream>>>((const T*)y, bits, M, N, ldw);
+    relu_bits_kernel<T><<<grid_for(ctx, (M + 31) / 32 * N, 256), 256, 0, ctx->stream>>>((const T*)y, bits, M, N);
   });
   GT_LAUNCH_CHECK();
   return nullptr;
@@ -262,7 +261,7 @@ char* gt_linear_fwd_bits(gt_ctx* ctx, int dtype, const void* x, const void* w, c
     e.bias = (const T*)bias;
     e.act = GT_ACT_RELU;
     e.bits_out = (uint32_t*)bits;
-    e.ldw = (M + 31) / 32;
+    e.ldw = N;
     GT_TRY(gemm<T>(ctx, s, (const T*)x, (const T*)w, e));
     fused = sizeof(T) == 4 && g_gemm_taken == 2;  // the tcgen05 epilogues wrote the mask
   });
@@ -280,7 +279,7 @@ char* gt_linear_bwd_data_bits(gt_ctx* ctx, int dtype, const void* dy, const void
     e.out = (T*)dx;
     e.ldc = K;
     e.dbits = bits;
-    e.ldw = (M + 31) / 32;
+    e.ldw = K;
     return gemm<T>(ctx, s, (const T*)dy, (const T*)w, e);
   });
   return nullptr;

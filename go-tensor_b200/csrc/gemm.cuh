@@ -25,9 +25,10 @@ struct Epi {
   // nchw_L > 0 stores C (M = channels, N = images * L) into an (images, M, L)
   // tensor: out[(n / L) * M * L + m * L + n % L], with M given in nchw_M.
   int64_t nchw_L = 0, nchw_M = 0;
-  // ReLU bit masks in column words: bit m % 32 of bits[n * ldw + m / 32],
-  // ldw = ceil(M / 32), so a thread that owns column n of 32 rows reads or
-  // writes one word. bits_out (forward): bit = (stored value > 0), written by
+  // ReLU bit masks in column words: bit m % 32 of bits[(m / 32) * ldw + n],
+  // ldw = the number of columns, so a thread that owns column n of 32 rows
+  // reads or writes one word, and a warp's 32 columns are 128 contiguous
+  // bytes. bits_out (forward): bit = (stored value > 0), written by
   // the tcgen05 epilogues only (other paths leave it to gt_relu_bits). dbits
   // (dX): out = acc * (bit ? 1 : 0), ReLU's derivative g * Step(y) read from
   // the forward's bits instead of the activation itself.
@@ -41,7 +42,7 @@ struct Epi {
     if (bias) v = add_rn(v, bias[bias_by_row ? m : n]);
     if (act != GT_ACT_NONE) v = act_fwd(act, v);
     if (dmask) v = act_bwd(dact, v, dmask[m * ldm + n]);
-    if (dbits) v = mul_rn(v, ((dbits[n * ldw + (m >> 5)] >> (m & 31)) & 1u) ? (T)1 : (T)0);
+    if (dbits) v = mul_rn(v, ((dbits[(m >> 5) * ldw + n] >> (m & 31)) & 1u) ? (T)1 : (T)0);
     return v;
   }
 

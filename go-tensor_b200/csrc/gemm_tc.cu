@@ -343,11 +343,11 @@ __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const Gemm
       op[r * epi.ldc] = v;
       w |= (uint32_t)(v > 0.0f) << r;
     }
-    if (epi.bits_out && rows > 0) epi.bits_out[n * epi.ldw + (m0 >> 5)] = w;
+    if (epi.bits_out && rows > 0) epi.bits_out[(m0 >> 5) * epi.ldw + n] = w;
   } else if (EK == EK_MASKBITS) {
     // One word holds this column's factor for all 32 rows of the block: 4
     // bytes per lane instead of 128 bytes of activations.
-    const uint32_t w = rows > 0 ? __ldg(epi.dbits + n * epi.ldw + (m0 >> 5)) : 0u;
+    const uint32_t w = rows > 0 ? __ldg(epi.dbits + (m0 >> 5) * epi.ldw + n) : 0u;
 #pragma unroll 4
     for (int r = 0; r < rows; r++) op[r * epi.ldc] = __fmul_rn(xpose[r * EPI_LD + lane], ((w >> r) & 1u) ? 1.0f : 0.0f);
   } else if (EK == EK_MASK) {
@@ -794,7 +794,7 @@ __global__ void splitk_reduce_bits_kernel(const float* __restrict__ ws, SplitPla
       epi.put(m0 + j, n, y);
       w |= (uint32_t)(y > 0.0f) << j;
     }
-    epi.bits_out[n * epi.ldw + (m0 >> 5)] = w;
+    epi.bits_out[(m0 >> 5) * epi.ldw + n] = w;
   }
 }
 

@@ -270,7 +270,7 @@ void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t
       if (op.kind != Op::LINEAR || !op.needs_dx || op.src < 0) continue;
       Op& src = ops_[op.src];
       if (src.kind != Op::LINEAR || src.act != GT_ACT_RELU || src.bits) continue;
-      bits_.emplace_back(ctx_, (size_t)src.N * (size_t)((src.M + 31) / 32) * sizeof(uint32_t));
+      bits_.emplace_back(ctx_, (size_t)((src.M + 31) / 32) * (size_t)src.N * sizeof(uint32_t));
       src.bits = (uint32_t*)bits_.back().get();
     }
   if (shape.size() != 2) throw Error("the model must end in (batch, classes) logits, got " + shape_str(shape));

@@ -164,9 +164,9 @@ GT_API char* gt_linear_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const vo
                          int act_prev, void* dx, int64_t M, int64_t K, int64_t N);
 /* ReLU bit masks (no counterpart in the reference, which keeps the ReLU
  * input and multiplies by Step(x), tensor/ops.go:110): for y (M, N), bit
- * m % 32 of word bits[n * ceil(M / 32) + m / 32] is (y[m][n] > 0), the factor
- * the ReLU backward applies; N * ceil(M / 32) words in all. The backward then
- * reads 1 bit per element instead of the 4-byte activation. */
+ * m % 32 of word bits[(m / 32) * N + n] is (y[m][n] > 0), the factor the ReLU
+ * backward applies; ceil(M / 32) * N words in all. The backward then reads
+ * 1 bit per element instead of the 4-byte activation. */
 /* bits = (y (M, N) > 0), packed. */
 GT_API char* gt_relu_bits(gt_ctx* ctx, int dtype, const void* y, uint32_t* bits, int64_t M, int64_t N);
 /* gt_linear_fwd with act = ReLU that also writes the output's bit mask

@@ -107,11 +107,11 @@ def test_linear_bwd(dt, npdt, tol, act_prev, mkn):
 
 
 def _relu_bits(y, M, N):
-    """Word (n, b) holds bit j = (y[32 b + j, n] > 0): N rows of ceil(M / 32) words."""
-    ldw = (M + 31) // 32
-    pos = np.zeros((ldw * 32, N), dtype=np.uint64)
+    """Word (b, n) holds bit j = (y[32 b + j, n] > 0): ceil(M / 32) rows of N words."""
+    nb = (M + 31) // 32
+    pos = np.zeros((nb * 32, N), dtype=np.uint64)
     pos[:M] = np.asarray(y).reshape(M, N) > 0
-    return (pos.T.reshape(N, ldw, 32) << np.arange(32, dtype=np.uint64)).sum(axis=2).astype(np.uint32)
+    return (pos.reshape(nb, 32, N) << np.arange(32, dtype=np.uint64)[None, :, None]).sum(axis=1).astype(np.uint32)
 
 
 @pytest.mark.parametrize("dt,npdt,tol", DT)
@@ -140,8 +140,8 @@ def test_relu_bits_forward_and_dx(dt, npdt, tol, mkn2):
     y = host(y1)
     assert_bits(host(y2), y, "y")
     want_bits = _relu_bits(y, M, N)
-    assert np.array_equal(host(bits).view(np.uint32).reshape(N, ldw), want_bits)
-    assert np.array_equal(host(bits2).view(np.uint32).reshape(N, ldw), want_bits)
+    assert np.array_equal(host(bits).view(np.uint32).reshape(ldw, N), want_bits)
+    assert np.array_equal(host(bits2).view(np.uint32).reshape(ldw, N), want_bits)
     # the next layer: dx (M, N) = dy (M, N2) @ w2 (N2, N) * Step(y)
     w2 = (rng.standard_normal((N2, N)) / np.sqrt(N)).astype(npdt)
     dy = (rng.standard_normal((M, N2)) / np.sqrt(M)).astype(npdt)
