@@ -84,6 +84,8 @@ CUDA_API = {
     "gt_linear_fwd": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _INT]),
     "gt_linear_bwd_data": ("err", [_P, _INT, _P, _P, _P, _INT, _P, _I64, _I64, _I64]),
     "gt_relu_bits": ("err", [_P, _INT, _P, _P, _I64, _I64]),
+    "gt_mse_fwd_bwd": ("err", [_P, _INT, _P, _P, _I64, _P, _P]),
+    "gt_bce_fwd_bwd": ("err", [_P, _INT, _P, _P, _I64, _P, _P]),
     "gt_linear_fwd_bits": ("err", [_P, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64]),
     "gt_linear_bwd_data_bits": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64]),
     "gt_linear_bwd_weight": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64]),

@@ -222,6 +222,22 @@ GT_API char* gt_argmax_rows(gt_ctx* ctx, int dtype, const void* x, int64_t rows,
  * the host. */
 GT_API char* gt_count_equal(gt_ctx* ctx, const int32_t* a, const int32_t* b, int64_t n, int64_t* count);
 
+/* Mean-squared error over n elements: loss (1 element, device) =
+ * mean((pred - target)^2) and, if dpred is not NULL, dpred = 2 (pred - target)
+ * / n. Replaces MSELoss (nn/loss.go:6-9: Sub, Pow, Mean) and its backward,
+ * with the reference's rounding of each intermediate, so dpred equals the
+ * tape's bit for bit; n = 0 gives a NaN loss, as Mean of nothing does. */
+GT_API char* gt_mse_fwd_bwd(gt_ctx* ctx, int dtype, const void* pred, const void* target, int64_t n, void* loss,
+                            void* dpred);
+/* Binary cross-entropy of probabilities pred in (0, 1) against targets in
+ * [0, 1]: loss = -mean(t log p + (1 - t) log(1 - p)) and, if dpred is not
+ * NULL, the gradient the tape forms (t/p and (1 - t)/(1 - p) terms, each
+ * scaled by -1/n). Replaces BCELoss (nn/loss.go:17-22) and its backward;
+ * the logarithms are evaluated in float64 and rounded, as the reference's
+ * Log is. */
+GT_API char* gt_bce_fwd_bwd(gt_ctx* ctx, int dtype, const void* pred, const void* target, int64_t n, void* loss,
+                            void* dpred);
+
 /* Softmax cross-entropy over logits (B, C) with int32 labels on the device:
  * loss (1 element, device) = -mean_i log softmax(x_i)[y_i] and, if dlogits is
  * not NULL, dlogits = (softmax(x) - onehot(y)) / B. Replaces CrossEntropyLoss

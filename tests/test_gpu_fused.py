@@ -9,6 +9,7 @@ from gotensor import _lib
 from gotensor._lib import AdamCfg, SgdCfg, check
 from gpu_common import assert_bits, assert_close, cuda_backend
 from oracle import gotensor_ref as T
+from oracle import nn_ref as nn
 
 pytestmark = pytest.mark.gpu
 
@@ -150,6 +151,50 @@ def test_relu_bits_forward_and_dx(dt, npdt, tol, mkn2):
     check(lib().gt_linear_bwd_data(ctx(), dt, dyd.ptr, w2d.ptr, y1.ptr, 1, dx1.ptr, M, N, N2))
     check(lib().gt_linear_bwd_data_bits(ctx(), dt, dyd.ptr, w2d.ptr, bits.ptr, dx2.ptr, M, N, N2))
     assert_bits(host(dx2), host(dx1), "dx")
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("kind", ["mse", "bce"])
+@pytest.mark.parametrize("n", [1, 37, 4096, 1_000_003])
+def test_fused_losses(dt, npdt, tol, kind, n):
+    """gt_mse_fwd_bwd / gt_bce_fwd_bwd against the oracle's tape for MSELoss /
+    BCELoss (nn/loss.go:6-22) and Backward: the gradient bit for bit for MSE
+    and within the float64-log tolerance for BCE; the loss within the device
+    tolerance (the sums run in different orders; a million float32 terms
+    summed in sequence on the CPU carry ~1e-4 of error, so that size uses the
+    reference's large-op tolerance 1e-3)."""
+    rng = np.random.default_rng(n + 7 * (kind == "bce"))
+    if kind == "bce":
+        pred = (1 / (1 + np.exp(-rng.standard_normal(n)))).astype(npdt)
+        target = rng.random(n).astype(npdt)
+    else:
+        pred = rng.standard_normal(n).astype(npdt)
+        target = rng.standard_normal(n).astype(npdt)
+    p = ref(pred, n).SetRequiresGrad(True)
+    loss_t = (nn.MSELoss if kind == "mse" else nn.BCELoss)(p, ref(target, n))
+    loss_t.Backward()
+    loss, g = new(1, dt), new(n, dt)
+    fn = lib().gt_mse_fwd_bwd if kind == "mse" else lib().gt_bce_fwd_bwd
+    check(fn(ctx(), dt, dev(pred).ptr, dev(target).ptr, n, loss.ptr, g.ptr))
+    want_g = p.Grad().Float64s().astype(npdt)
+    if kind == "mse":
+        assert_bits(host(g), want_g, "mse dpred")
+    else:
+        assert_close(host(g), want_g, 1e-6 if dt == T.Float32 else 1e-15, "bce dpred")
+    lt = 1e-3 if (dt == T.Float32 and n > 4096) else tol
+    assert_close(host(loss), loss_t.Float64s(), lt, f"{kind} loss")
+    # the forward alone (dpred NULL) gives the same loss
+    loss2 = new(1, dt)
+    check(fn(ctx(), dt, dev(pred).ptr, dev(target).ptr, n, loss2.ptr, None))
+    assert_bits(host(loss2), host(loss), "loss without gradient")
+
+
+@pytest.mark.parametrize("fn", ["gt_mse_fwd_bwd", "gt_bce_fwd_bwd"])
+def test_fused_losses_empty(fn):
+    """Mean over no elements is 0 * (1/0) = NaN in the reference."""
+    loss = new(1, T.Float32)
+    check(getattr(lib(), fn)(ctx(), T.Float32, None, None, 0, loss.ptr, None))
+    assert np.isnan(host(loss)[0])
 
 
 CONVS = [(2, 3, 5, 5, 4, 3, 1, 0), (2, 2, 5, 4, 3, 3, 2, 1), (8, 1, 28, 28, 32, 3, 1, 1), (4, 32, 14, 14, 64, 3, 1, 1),
