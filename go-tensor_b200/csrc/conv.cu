@@ -413,4 +413,77 @@ char* gt_conv_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, vo
   return err;
 }
 
+// Conv2d forward that keeps its im2col columns in `cols` (N*L x C*KH*KW
+// elements, the caller's buffer) for gt_conv_bwd: the same kernels and result
+// as gt_conv_fwd.
+char* gt_conv_fwd_cols(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y, void* cols,
+                       const gt_geom* g, int64_t O, int act) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_conv_fwd_cols"));
+  if (O <= 0 || !cols) return errorf("gt_conv_fwd_cols: bad arguments");
+  const int64_t L = g->OH * g->OW, NL = g->N * L, CKK = g->C * g->KH * g->KW;
+  if (NL == 0) return nullptr;
+  GT_DISPATCH(dtype, {
+    GT_TRY(im2col_launch<T>(ctx, (const T*)x, (T*)cols, *g));
+    GemmShape s{O, NL, CKK, false, true, CKK, CKK};
+    Epi<T> e;
+    e.out = (T*)y;
+    e.bias = (const T*)bias;
+    e.bias_by_row = true;
+    e.act = act;
+    e.nchw_L = L;
+    e.nchw_M = O;
+    return gemm<T>(ctx, s, (const T*)w, (const T*)cols, e);
+  });
+  return nullptr;
+}
+
+// Conv2d backward from the forward's columns: dy is permuted to (O, N*L)
+// once for both GEMMs, dW = dyp @ cols, db = row sums of dyp, and (dx not
+// NULL) dx = col2im(dyp^T @ W). The same kernels, in the same order, as
+// gt_conv_bwd_weight followed by gt_conv_bwd_data.
+char* gt_conv_bwd(gt_ctx* ctx, int dtype, const void* cols, const void* dy, const void* w, void* dx, void* dw,
+                  void* db, const gt_geom* g, int64_t O) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_conv_bwd"));
+  if (O <= 0 || !cols || !dw) return errorf("gt_conv_bwd: bad arguments");
+  const int64_t L = g->OH * g->OW, NL = g->N * L, CKK = g->C * g->KH * g->KW;
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  if (NL == 0) {
+    GT_CUDA(cudaMemsetAsync(dw, 0, O * CKK * es, ctx->stream));
+    if (db) GT_CUDA(cudaMemsetAsync(db, 0, O * es, ctx->stream));
+    if (dx) GT_CUDA(cudaMemsetAsync(dx, 0, g->N * g->C * g->H * g->W * es, ctx->stream));
+    return nullptr;
+  }
+  void *dyp = nullptr, *dcols = nullptr;
+  GT_TRY(scratch(ctx, (size_t)(O * NL) * es, &dyp));
+  char* err = permute_nol(ctx, dtype, dy, dyp, g->N, O, L);
+  GT_DISPATCH(dtype, {
+    if (!err) {
+      GemmShape s{O, CKK, NL, false, false, NL, CKK};
+      Epi<T> e;
+      e.out = (T*)dw;
+      e.ldc = CKK;
+      err = gemm<T>(ctx, s, (const T*)dyp, (const T*)cols, e);
+    }
+  });
+  if (!err && db) err = gt_reduce(ctx, dtype, GT_SUM, dyp, db, O, NL, 1);
+  if (!err && dx) err = scratch(ctx, (size_t)(NL * CKK) * es, &dcols);
+  if (!err && dx) {
+    GT_DISPATCH(dtype, {
+      GemmShape s{NL, CKK, O, true, false, NL, CKK};
+      Epi<T> e;
+      e.out = (T*)dcols;
+      e.ldc = CKK;
+      err = gemm<T>(ctx, s, (const T*)dyp, (const T*)w, e);
+      if (!err) err = col2im_launch<T>(ctx, (const T*)dcols, (T*)dx, *g);
+    });
+  }
+  release(ctx, dcols);
+  release(ctx, dyp);
+  return err;
+}
+
 }  // extern "C"

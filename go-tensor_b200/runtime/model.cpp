@@ -273,6 +273,14 @@ void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t
       bits_.emplace_back(ctx_, (size_t)((src.M + 31) / 32) * (size_t)src.N * sizeof(uint32_t));
       src.bits = (uint32_t*)bits_.back().get();
     }
+  // Every conv keeps its forward's im2col columns for its backward.
+  for (auto& op : ops_) {
+    if (op.kind != Op::CONV) continue;
+    const int64_t rows = op.g.N * op.g.OH * op.g.OW, ckk = op.g.C * op.g.KH * op.g.KW;
+    if (rows * ckk == 0) continue;
+    cols_.emplace_back(ctx_, (size_t)(rows * ckk) * es_);
+    op.cols = cols_.back().get();
+  }
   if (shape.size() != 2) throw Error("the model must end in (batch, classes) logits, got " + shape_str(shape));
   if (!seen_params) throw Error("the model has no parameters");
   classes_ = shape[1];
@@ -349,7 +357,12 @@ void Model::forward() {
                               op.N, op.act));
         break;
       case Op::CONV:
-        check(gt_conv_fwd(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, &op.g, op.O, op.act));
+        if (op.cols)
+          check(gt_conv_fwd_cols(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, op.cols, &op.g,
+                                 op.O, op.act));
+        else
+          check(gt_conv_fwd(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, &op.g, op.O,
+                            op.act));
         break;
       case Op::POOL:
         check(gt_maxpool_fwd_idx(ctx_, dtype_, op.in, op.out, op.idx, &op.g));
@@ -415,12 +428,25 @@ void Model::backward(bool join) {
         break;
       }
       case Op::CONV:
-        check(gt_conv_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, &op.g, op.O));
-        if (world_ > 1) issue_ready_buckets(op.w_off);
-        if (op.needs_dx) {
-          check(gt_conv_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, spare, &op.g, op.O));
-          std::swap(g, spare);
+        if (!op.cols) {  // no output positions: the gradients are zero
+          check(gt_conv_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, &op.g, op.O));
+          if (world_ > 1) issue_ready_buckets(op.w_off);
+          if (op.needs_dx) {
+            check(gt_conv_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, spare, &op.g, op.O));
+            std::swap(g, spare);
+          }
+          break;
         }
+        if (world_ == 1) {  // one call: dy rearranged once for dW and dX
+          check(gt_conv_bwd(ctx_, dtype_, op.cols, g, p + op.w_off * es_, op.needs_dx ? spare : nullptr,
+                            gr + op.w_off * es_, gr + op.b_off * es_, &op.g, op.O));
+        } else {  // the bucket goes out before dX is computed
+          check(gt_conv_bwd(ctx_, dtype_, op.cols, g, p + op.w_off * es_, nullptr, gr + op.w_off * es_,
+                            gr + op.b_off * es_, &op.g, op.O));
+          issue_ready_buckets(op.w_off);
+          if (op.needs_dx) check(gt_conv_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, spare, &op.g, op.O));
+        }
+        if (op.needs_dx) std::swap(g, spare);
         break;
       case Op::POOL:
         if (op.g.stride >= op.g.KH && op.g.stride >= op.g.KW) {

@@ -85,6 +85,7 @@ struct Op {
   bool produces_act = false;    // output is an activation's output (derivative can be fused upstream)
   int src = -1;                 // op that produced this op's input, identities skipped (-1: the batch)
   uint32_t* bits = nullptr;     // LINEAR + ReLU, float32: bit mask of the output for the next Linear's dX
+  void* cols = nullptr;         // CONV: the forward's im2col columns, reused by the backward
 };
 
 class Model {
@@ -152,6 +153,7 @@ class Model {
   int64_t dense_params_ = 0, dev_params_ = 0;
   std::vector<DevBuf> acts_;  // activation buffers owned by ops
   std::vector<DevBuf> bits_;  // ReLU bit masks (Op::bits)
+  std::vector<DevBuf> cols_;  // conv columns (Op::cols)
   DevBuf pbuf_, gbuf_, opt_a_, opt_b_, step_dev_;
   // Two input/label buffer pairs: while a step reads one, the next batch can
   // be uploaded into the other on the copy stream.

@@ -201,6 +201,17 @@ GT_API char* gt_conv_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void
 /* dw (O, C, KH, KW) and db (O) (NULL: skip) of a Conv2d given x and dy. */
 GT_API char* gt_conv_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db,
                          const gt_geom* g, int64_t out_channels);
+/* gt_conv_fwd that keeps its im2col columns in cols (N*OH*OW x C*KH*KW
+ * elements, owned by the caller) for gt_conv_bwd; the same result. No
+ * counterpart in the reference, whose backward closure holds the Im2col
+ * tensor the same way (tensor/conv.go:40-59). */
+GT_API char* gt_conv_fwd_cols(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y,
+                              void* cols, const gt_geom* g, int64_t out_channels, int act);
+/* Conv2d backward from the forward's columns: dw, db (NULL: skip) and dx
+ * (NULL: skip), with dy rearranged once for both GEMMs. The same results as
+ * gt_conv_bwd_weight and gt_conv_bwd_data. */
+GT_API char* gt_conv_bwd(gt_ctx* ctx, int dtype, const void* cols, const void* dy, const void* w, void* dx, void* dw,
+                         void* db, const gt_geom* g, int64_t out_channels);
 /* MaxPool2d forward that also records, per output, the window offset of the
  * first maximum (uint8, kh*KW+kw) — the index the backward pass routes to
  * (internal/cpu/linalg.go:169-183). Non-overlapping windows (stride >= KH, KW)

@@ -202,6 +202,41 @@ CONVS = [(2, 3, 5, 5, 4, 3, 1, 0), (2, 2, 5, 4, 3, 3, 2, 1), (8, 1, 28, 28, 32, 
 
 
 @pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("cs", CONVS + [(16, 64, 16, 16, 128, 3, 1, 1)])
+def test_conv_cols_entry_points(dt, npdt, tol, cs):
+    """gt_conv_fwd_cols stores what gt_conv_fwd stores and keeps the columns
+    gt_im2col builds; gt_conv_bwd from those columns gives what
+    gt_conv_bwd_weight and gt_conv_bwd_data give, bit for bit, with and
+    without dx."""
+    N, C, H, W, O, k, s, p = cs
+    rng = np.random.default_rng(3 * sum(cs))
+    x = rng.standard_normal((N, C, H, W)).astype(npdt)
+    w = (rng.standard_normal((O, C, k, k)) / np.sqrt(C * k * k)).astype(npdt)
+    b = rng.standard_normal(O).astype(npdt)
+    g = T.conv_geom("Conv2d", [N, C, H, W], k, k, s, p)
+    gg = ctypes.byref(_lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_]))
+    L, CKK = g.OH * g.OW, C * k * k
+    xd, wd, bd = dev(x), dev(w), dev(b)
+    y1, y2, cols, cols_ref = new(N * O * L, dt), new(N * O * L, dt), new(N * L * CKK, dt), new(N * L * CKK, dt)
+    check(lib().gt_conv_fwd(ctx(), dt, xd.ptr, wd.ptr, bd.ptr, y1.ptr, gg, O, 1))
+    check(lib().gt_conv_fwd_cols(ctx(), dt, xd.ptr, wd.ptr, bd.ptr, y2.ptr, cols.ptr, gg, O, 1))
+    check(lib().gt_im2col(ctx(), dt, xd.ptr, cols_ref.ptr, gg))
+    assert_bits(host(y2), host(y1), "conv fwd")
+    assert_bits(host(cols), host(cols_ref), "cols")
+    dyd = dev(rng.standard_normal((N, O, g.OH, g.OW)).astype(npdt))
+    dx1, dw1, db1 = new(N * C * H * W, dt), new(O * CKK, dt), new(O, dt)
+    check(lib().gt_conv_bwd_weight(ctx(), dt, xd.ptr, dyd.ptr, dw1.ptr, db1.ptr, gg, O))
+    check(lib().gt_conv_bwd_data(ctx(), dt, dyd.ptr, wd.ptr, dx1.ptr, gg, O))
+    dx2, dw2, db2, dw3 = new(N * C * H * W, dt), new(O * CKK, dt), new(O, dt), new(O * CKK, dt)
+    check(lib().gt_conv_bwd(ctx(), dt, cols.ptr, dyd.ptr, wd.ptr, dx2.ptr, dw2.ptr, db2.ptr, gg, O))
+    check(lib().gt_conv_bwd(ctx(), dt, cols.ptr, dyd.ptr, wd.ptr, None, dw3.ptr, None, gg, O))
+    assert_bits(host(dx2), host(dx1), "dx")
+    assert_bits(host(dw2), host(dw1), "dw")
+    assert_bits(host(db2), host(db1), "db")
+    assert_bits(host(dw3), host(dw1), "dw without dx")
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
 @pytest.mark.parametrize("cs", CONVS)
 def test_conv_fwd_bwd(dt, npdt, tol, cs):
     N, C, H, W, O, k, s, p = cs
