@@ -136,6 +136,52 @@ __global__ void maxpool_fwd_kernel(const T* __restrict__ x, T* __restrict__ out,
   }
 }
 
+// 2 x 2 windows with stride 2 that tile the input exactly (H = 2 OH,
+// W = 2 OW), the pooling of both conv configurations: a thread per output,
+// whose window is two 8-byte pairs of adjacent inputs, so a warp's loads and
+// stores are contiguous runs. Same first-maximum rule and outputs as
+// maxpool_fwd_kernel / maxpool_bwd_idx_kernel.
+template <typename T, typename I>
+__global__ void maxpool2_fwd_kernel(const T* __restrict__ x, T* __restrict__ out, uint8_t* __restrict__ idx,
+                                    I OH, I OW, I total) {
+  for (I e = (I)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
+    const I ow = e % OW, t = e / OW;  // t = plane * OH + oh
+    const T* r0 = x + (int64_t)t * 4 * OW + 2 * ow;
+    const T v[4] = {r0[0], r0[1], r0[2 * OW], r0[2 * OW + 1]};
+    T best = v[0];
+    int k = 0;
+#pragma unroll
+    for (int j = 1; j < 4; j++)
+      if (v[j] > best) {
+        best = v[j];
+        k = j;
+      }
+    out[e] = best;
+    if (idx) idx[e] = (uint8_t)k;
+  }
+}
+
+template <typename T, typename I>
+__global__ void maxpool2_bwd_idx_kernel(const T* __restrict__ grad, const uint8_t* __restrict__ idx,
+                                        const T* __restrict__ pooled, int relu_mask, T* __restrict__ dx, I OW,
+                                        I total) {
+  for (I e = (I)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
+    const I ow = e % OW, t = e / OW;
+    T v = grad[e];
+    if (relu_mask) v = mul_rn(v, pooled[e] > (T)0 ? (T)1 : (T)0);
+    const int k = idx[e];
+    T* r0 = dx + (int64_t)t * 4 * OW + 2 * ow;
+    r0[0] = k == 0 ? v : (T)0;
+    r0[1] = k == 1 ? v : (T)0;
+    r0[2 * OW] = k == 2 ? v : (T)0;
+    r0[2 * OW + 1] = k == 3 ? v : (T)0;
+  }
+}
+
+static bool pool2_tiles(const gt_geom* g) {
+  return g->KH == 2 && g->KW == 2 && g->stride == 2 && g->pad == 0 && g->H == 2 * g->OH && g->W == 2 * g->OW;
+}
+
 // dx[pl][ih][iw] = sum of grad over the windows whose first maximum is this
 // element, visited in increasing window order (the reference's order).
 template <typename T>
@@ -263,7 +309,15 @@ char* gt_maxpool_fwd_idx(gt_ctx* ctx, int dtype, const void* x, void* out, uint8
   int64_t total = g->N * g->C * g->OH * g->OW;
   if (total == 0) return nullptr;
   GT_DISPATCH(dtype, {
-    maxpool_fwd_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>((const T*)x, (T*)out, idx, *g, total);
+    if (pool2_tiles(g) && total < INT32_MAX / 2)
+      maxpool2_fwd_kernel<T, int32_t><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(
+          (const T*)x, (T*)out, idx, (int32_t)g->OH, (int32_t)g->OW, (int32_t)total);
+    else if (pool2_tiles(g))
+      maxpool2_fwd_kernel<T, int64_t><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(
+          (const T*)x, (T*)out, idx, g->OH, g->OW, total);
+    else
+      maxpool_fwd_kernel<T><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>((const T*)x, (T*)out, idx, *g,
+                                                                               total);
   });
   GT_LAUNCH_CHECK();
   return nullptr;
@@ -294,6 +348,19 @@ char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t
   if (relu_mask && !pooled) return errorf("gt_maxpool_bwd_idx: relu_mask needs the pooled output");
   int64_t total = g->N * g->C * g->H * g->W;
   if (total == 0) return nullptr;
+  if (pool2_tiles(g)) {  // a thread per window
+    const int64_t outs = g->N * g->C * g->OH * g->OW;
+    GT_DISPATCH(dtype, {
+      if (outs < INT32_MAX / 2)
+        maxpool2_bwd_idx_kernel<T, int32_t><<<grid_for(ctx, outs, 256), 256, 0, ctx->stream>>>(
+            (const T*)grad, idx, (const T*)pooled, relu_mask, (T*)dx, (int32_t)g->OW, (int32_t)outs);
+      else
+        maxpool2_bwd_idx_kernel<T, int64_t><<<grid_for(ctx, outs, 256), 256, 0, ctx->stream>>>(
+            (const T*)grad, idx, (const T*)pooled, relu_mask, (T*)dx, g->OW, outs);
+    });
+    GT_LAUNCH_CHECK();
+    return nullptr;
+  }
   GT_DISPATCH(dtype, {
     if (total < INT32_MAX / 2)
       maxpool_bwd_idx_kernel<T, int32_t><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(

@@ -84,6 +84,26 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     __syncthreads();
   }
 
+  if (!ws && epi.nchw_L > 0) {
+    // NCHW store (a convolution's output): the thread's TN consecutive
+    // columns are split into (image, position) once and then stepped, not
+    // divided per element.
+    const int64_t nb = n0 + tx * TN;
+    int64_t img = nb / epi.nchw_L, pos = nb - img * epi.nchw_L;
+#pragma unroll
+    for (int j = 0; j < TN; j++) {
+      if (nb + j < N) {
+        T* col = epi.out + img * epi.nchw_M * epi.nchw_L + pos;
+#pragma unroll
+        for (int i = 0; i < TM; i++) {
+          const int64_t m = m0 + ty * TM + i;
+          if (m < M) col[m * epi.nchw_L] = epi.finish(m, nb + j, acc[i][j]);
+        }
+      }
+      if (++pos == epi.nchw_L) pos = 0, img++;
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < TM; i++) {
     int64_t m = m0 + ty * TM + i;
@@ -338,6 +358,9 @@ char* gemm_simt(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const E
   const bool tiny_m = s.M <= 16, short_m = s.M <= 64, narrow_n = s.N <= 32;
   if (tiny_m) return narrow_n ? simt_launch<T, 16, 32, 8, 1, 2>(ctx, s, A, B, epi)
                               : simt_launch<T, 16, 128, 8, 1, 8>(ctx, s, A, B, epi);
+  // long K over a skinny output (a first-layer conv's weight gradient): 32-deep
+  // slices, so each row of A is read 128 contiguous bytes at a time
+  if (short_m && narrow_n && s.K >= 65536 && !s.trans_a) return simt_launch<T, 64, 32, 32, 4, 2>(ctx, s, A, B, epi);
   if (short_m && narrow_n) return simt_launch<T, 64, 32, 8, 4, 2>(ctx, s, A, B, epi);
   if (short_m) return simt_launch<T, 64, 128, 8, 4, 8>(ctx, s, A, B, epi);
   if (narrow_n) return simt_launch<T, 128, 32, 8, 8, 2>(ctx, s, A, B, epi);
