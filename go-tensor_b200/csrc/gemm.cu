@@ -285,6 +285,25 @@ char* gt_linear_bwd_data_bits(gt_ctx* ctx, int dtype, const void* dy, const void
   return nullptr;
 }
 
+char* gt_linear_bwd_weight_rows(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, int64_t M,
+                                int64_t K, int64_t N, int64_t r0, int64_t r1) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M <= 0 || K <= 0 || N <= 0 || r0 < 0 || r1 > N || r0 >= r1)
+    return errorf("gt_linear_bwd_weight_rows: bad sizes or row range [%lld, %lld) of %lld", (long long)r0,
+                  (long long)r1, (long long)N);
+  // dw rows [r0, r1) = dy[:, r0:r1]^T @ x: A(m, k) = dy[k*N + r0 + m], the
+  // full row pitch N kept.
+  GemmShape s{r1 - r0, K, M, true, false, N, K};
+  GT_DISPATCH(dtype, {
+    Epi<T> e;
+    e.out = (T*)dw + r0 * K;
+    e.ldc = K;
+    return gemm<T>(ctx, s, (const T*)dy + r0, (const T*)x, e);
+  });
+  return nullptr;
+}
+
 char* gt_linear_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db, int64_t M,
                            int64_t K, int64_t N) {
   GT_ENTER(ctx);

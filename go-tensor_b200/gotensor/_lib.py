@@ -94,6 +94,7 @@ CUDA_API = {
     "gt_conv_fwd": ("err", [_P, _INT, _P, _P, _P, _P, ctypes.POINTER(GtGeom), _I64, _INT]),
     "gt_conv_bwd_data": ("err", [_P, _INT, _P, _P, _P, ctypes.POINTER(GtGeom), _I64]),
     "gt_conv_bwd_weight": ("err", [_P, _INT, _P, _P, _P, _P, ctypes.POINTER(GtGeom), _I64]),
+    "gt_linear_bwd_weight_rows": ("err", [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _I64, _I64]),
     "gt_conv_fwd_cols": ("err", [_P, _INT, _P, _P, _P, _P, _P, ctypes.POINTER(GtGeom), _I64, _INT]),
     "gt_conv_bwd": ("err", [_P, _INT, _P, _P, _P, _P, _P, _P, ctypes.POINTER(GtGeom), _I64]),
     "gt_maxpool_fwd_idx": ("err", [_P, _INT, _P, _P, _P, ctypes.POINTER(GtGeom)]),

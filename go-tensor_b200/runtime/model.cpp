@@ -409,9 +409,19 @@ void Model::backward(bool join) {
     if (op.kind != Op::IDENTITY) g_pre = false;  // g is now w.r.t. the op's pre-activation / input
     switch (op.kind) {
       case Op::LINEAR: {
-        check(gt_linear_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, op.M, op.K,
-                                   op.N));
-        if (world_ > 1) issue_ready_buckets(op.w_off);
+        if (world_ > 1 && i == first_param_op_ && !first_rows_.empty()) {
+          // db first: it sits in the bucket of the first chunk issued
+          check(gt_reduce(ctx_, dtype_, GT_SUM, g, gr + op.b_off * es_, 1, op.M, op.N));
+          for (size_t j = first_rows_.size() - 1; j-- > 0;) {
+            check(gt_linear_bwd_weight_rows(ctx_, dtype_, op.in, g, gr + op.w_off * es_, op.M, op.K, op.N,
+                                            first_rows_[j], first_rows_[j + 1]));
+            issue_ready_buckets(op.w_off + first_rows_[j] * op.K);
+          }
+        } else {
+          check(gt_linear_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, op.M, op.K,
+                                     op.N));
+          if (world_ > 1) issue_ready_buckets(op.w_off);
+        }
         if (op.needs_dx) {
           // Fold the derivative of the activation that produced this input
           // into the GEMM epilogue when the producer is a Linear/Conv/act.
@@ -601,6 +611,41 @@ void Model::dp_init(int rank, int world, const unsigned char id[128], int timeou
                            bounds.data(), (int)sizes.size());
   buckets_.clear();
   for (int b = 0; b < nb; b++) buckets_.emplace_back(bounds[2 * b], bounds[2 * b + 1]);
+  // The first layer's weight gradient is the backward's last GEMM, so its
+  // bucket's all-reduce and update cannot overlap anything. When it is a
+  // Linear whose weight starts a bucket, that bucket is split at row chunks
+  // (multiples of 256 rows, or of 32 for small layers; GT_DP_LAST_CHUNKS
+  // chunks, default 1 = off), and the
+  // backward computes the chunks from the last rows down, each bucket
+  // issued as soon as its rows are done: only the last chunk stays exposed.
+  first_rows_.clear();
+  int chunks = 1;
+  if (const char* c = getenv("GT_DP_LAST_CHUNKS")) chunks = std::max(1, atoi(c));
+  if (world > 1 && chunks > 1 && first_param_op_ >= 0 && ops_[first_param_op_].kind == Op::LINEAR) {
+    const Op& op = ops_[first_param_op_];
+    int64_t per = (op.N + chunks - 1) / chunks;
+    per = per >= 256 ? per / 256 * 256 : per / 32 * 32;  // whole tiles where they fit
+    for (size_t b = 0; per > 0 && b < buckets_.size(); b++) {
+      if (buckets_[b].first != op.w_off) continue;
+      for (int64_t r = 0; r < op.N; r += per) first_rows_.push_back(r);
+      first_rows_.push_back(op.N);
+      if (first_rows_.size() < 3) {
+        first_rows_.clear();
+        break;
+      }
+      // sub-buckets in the list's order (highest offsets first); the last
+      // one keeps the rest of the bucket (the bias and anything after it)
+      std::vector<std::pair<int64_t, int64_t>> sub;
+      const int64_t end = buckets_[b].second;
+      for (size_t j = first_rows_.size() - 1; j-- > 0;)
+        sub.emplace_back(op.w_off + first_rows_[j] * op.K,
+                         j + 2 == first_rows_.size() ? end : op.w_off + first_rows_[j + 1] * op.K);
+      buckets_.erase(buckets_.begin() + (long)b);
+      buckets_.insert(buckets_.begin() + (long)b, sub.begin(), sub.end());
+      break;
+    }
+  }
+  nb = (int)buckets_.size();
   free_bucket_events();
   for (int b = 0; b < nb; b++) {
     gt_event* e = nullptr;

@@ -154,6 +154,10 @@ class Model {
   std::vector<DevBuf> acts_;  // activation buffers owned by ops
   std::vector<DevBuf> bits_;  // ReLU bit masks (Op::bits)
   std::vector<DevBuf> cols_;  // conv columns (Op::cols)
+  // Data parallel: row boundaries of the first layer's weight gradient,
+  // computed chunk by chunk so each chunk's bucket is averaged while the
+  // next chunk is computed (empty: one GEMM).
+  std::vector<int64_t> first_rows_;
   DevBuf pbuf_, gbuf_, opt_a_, opt_b_, step_dev_;
   // Two input/label buffer pairs: while a step reads one, the next batch can
   // be uploaded into the other on the copy stream.

@@ -182,6 +182,12 @@ GT_API char* gt_linear_bwd_data_bits(gt_ctx* ctx, int dtype, const void* dy, con
  * Permute backward of W.T() and sumTo for the bias (tensor/ops.go:418-433). */
 GT_API char* gt_linear_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, void* db,
                            int64_t M, int64_t K, int64_t N);
+/* Rows [r0, r1) of gt_linear_bwd_weight's dw (no db): a weight gradient
+ * computed in row chunks, so that a data-parallel step can start averaging
+ * the first chunk while the next is computed. No counterpart in the
+ * reference (which computes the whole MatMul backward, tensor/ops.go:324). */
+GT_API char* gt_linear_bwd_weight_rows(gt_ctx* ctx, int dtype, const void* x, const void* dy, void* dw, int64_t M,
+                                       int64_t K, int64_t N, int64_t r0, int64_t r1);
 /* Activation backward on its own: dx = dy * act'(y), n elements
  * (tensor/ops.go:110, 116, 123). */
 GT_API char* gt_act_bwd(gt_ctx* ctx, int dtype, int act, const void* dy, const void* y, void* dx, int64_t n);

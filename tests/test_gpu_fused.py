@@ -107,6 +107,27 @@ def test_linear_bwd(dt, npdt, tol, act_prev, mkn):
     assert_close(host(db), want_db, tol, "db")
 
 
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("mkn_rows", [(1024, 512, 1024, (0, 256, 512, 768, 1024)), (64, 27, 50, (0, 20, 50)),
+                                      (300, 130, 257, (0, 256, 257))])
+def test_linear_bwd_weight_rows(dt, npdt, tol, mkn_rows):
+    """gt_linear_bwd_weight_rows over consecutive row ranges rebuilds the
+    weight gradient of gt_linear_bwd_weight (the chunks may take other
+    K-split plans, so equal within the device tolerance), and leaves rows
+    outside its range untouched."""
+    M, K, N, rows = mkn_rows
+    rng = np.random.default_rng(M + K + N)
+    x = dev(rng.standard_normal((M, K)).astype(npdt))
+    dy = dev((rng.standard_normal((M, N)) / np.sqrt(M)).astype(npdt))
+    dw_full, dw = new(N * K, dt), new(N * K, dt)
+    check(lib().gt_linear_bwd_weight(ctx(), dt, x.ptr, dy.ptr, dw_full.ptr, None, M, K, N))
+    for r0, r1 in zip(rows[:-1], rows[1:]):
+        check(lib().gt_linear_bwd_weight_rows(ctx(), dt, x.ptr, dy.ptr, dw.ptr, M, K, N, r0, r1))
+        got = host(dw).reshape(N, K)
+        assert (got[r1:] == 0).all(), "rows past the range were written"
+    assert_close(host(dw), host(dw_full), tol, "dw by rows")
+
+
 def _relu_bits(y, M, N):
     """Word (b, n) holds bit j = (y[32 b + j, n] > 0): ceil(M / 32) rows of N words."""
     nb = (M + 31) // 32
