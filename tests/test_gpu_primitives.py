@@ -166,6 +166,9 @@ def test_matmul_known_values():
 GEOMS = [  # (N, C, H, W, KH, KW, stride, pad)
     (2, 3, 5, 5, 3, 3, 1, 0), (2, 2, 5, 4, 3, 2, 2, 1), (1, 1, 3, 3, 2, 2, 1, 0), (4, 3, 32, 32, 3, 3, 1, 1),
     (3, 5, 7, 9, 4, 2, 3, 2), (1, 2, 4, 4, 1, 1, 1, 0),
+    # stride 1 through the tiled col2im: several channel groups, ragged
+    # column tiles (W > 32) with an odd channel count, a 5 x 5 kernel
+    (8, 64, 16, 16, 3, 3, 1, 1), (2, 37, 9, 40, 3, 3, 1, 1), (2, 5, 33, 7, 5, 5, 1, 2),
 ]
 
 
