@@ -615,11 +615,11 @@ void Model::dp_init(int rank, int world, const unsigned char id[128], int timeou
   // bucket's all-reduce and update cannot overlap anything. When it is a
   // Linear whose weight starts a bucket, that bucket is split at row chunks
   // (multiples of 256 rows, or of 32 for small layers; GT_DP_LAST_CHUNKS
-  // chunks, default 1 = off), and the
+  // chunks, default 4; 1 = off), and the
   // backward computes the chunks from the last rows down, each bucket
   // issued as soon as its rows are done: only the last chunk stays exposed.
   first_rows_.clear();
-  int chunks = 1;
+  int chunks = 4;
   if (const char* c = getenv("GT_DP_LAST_CHUNKS")) chunks = std::max(1, atoi(c));
   if (world > 1 && chunks > 1 && first_param_op_ >= 0 && ops_[first_param_op_].kind == Op::LINEAR) {
     const Op& op = ops_[first_param_op_];
