@@ -615,11 +615,13 @@ void Model::dp_init(int rank, int world, const unsigned char id[128], int timeou
   // bucket's all-reduce and update cannot overlap anything. When it is a
   // Linear whose weight starts a bucket, that bucket is split at row chunks
   // (multiples of 256 rows, or of 32 for small layers; GT_DP_LAST_CHUNKS
-  // chunks, default 4; 1 = off), and the
+  // chunks, default 1 = off: it gained 2 % per step at 2 GPUs and lost 9 %
+  // at 8, where each chunk is a one-wave GEMM that competes with NCCL for
+  // SMs), and the
   // backward computes the chunks from the last rows down, each bucket
   // issued as soon as its rows are done: only the last chunk stays exposed.
   first_rows_.clear();
-  int chunks = 4;
+  int chunks = 1;
   if (const char* c = getenv("GT_DP_LAST_CHUNKS")) chunks = std::max(1, atoi(c));
   if (world > 1 && chunks > 1 && first_param_op_ >= 0 && ops_[first_param_op_].kind == Op::LINEAR) {
     const Op& op = ops_[first_param_op_];
