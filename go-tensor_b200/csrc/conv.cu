@@ -73,6 +73,19 @@ __global__ void permute_nol_kernel(const T* __restrict__ dy, T* __restrict__ dyp
   }
 }
 
+// The same permute as 16-byte vectors over the whole tensor, a thread per
+// vector (L a multiple of 16 bytes, 32-bit indices): short rows (L = 16 or
+// 64 positions) no longer leave threads idle or loads unoverlapped.
+template <typename V>
+__global__ void permute_nol_vec_kernel(const V* __restrict__ dy, V* __restrict__ dyp, int32_t N, int32_t O,
+                                       int32_t LV, int32_t total) {
+  for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int32_t r = i / LV, l = i - r * LV;  // r = o * N + n
+    const int32_t o = r / N, n = r - o * N;
+    dyp[i] = dy[(n * O + o) * LV + l];
+  }
+}
+
 // I: the index type, int32_t when every index of the call fits (chosen on the
 // host), which keeps the divisions cheap.
 template <typename T, typename I>
@@ -409,6 +422,15 @@ char* gt_conv_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const vo
 // dy (N, O, L) -> dyp (O, N*L): the layout of the GEMMs below.
 static char* permute_nol(gt_ctx* ctx, int dtype, const void* dy, void* dyp, int64_t N, int64_t O, int64_t L) {
   if (N * O * L == 0) return nullptr;
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  if ((L * (int64_t)es) % 16 == 0 && ((uintptr_t)dy & 15) == 0 && ((uintptr_t)dyp & 15) == 0 &&
+      N * O * L * (int64_t)es / 16 < INT32_MAX / 2) {
+    const int64_t LV = L * (int64_t)es / 16, total = N * O * LV;
+    permute_nol_vec_kernel<float4><<<grid_for(ctx, total, 256), 256, 0, ctx->stream>>>(
+        (const float4*)dy, (float4*)dyp, (int32_t)N, (int32_t)O, (int32_t)LV, (int32_t)total);
+    GT_LAUNCH_CHECK();
+    return nullptr;
+  }
   const int threads = L >= 256 ? 256 : L >= 64 ? 64 : 32;
   const int blocks = (int)std::min<int64_t>(N * O, (int64_t)ctx->sm_count * 32);
   GT_DISPATCH(dtype, {
