@@ -49,8 +49,14 @@ __global__ void im2col_rows_kernel(const T* __restrict__ x, T* __restrict__ cols
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warps = (int)((gridDim.x * blockDim.x) >> 5);
-  for (int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < rows; row += warps) {
-    const int n = row / OHW, r = row - n * OHW, oh = r / OW, ow = r - oh * OW;
+  // Each warp takes a contiguous run of rows: (n, oh, ow) is decomposed once
+  // and then stepped, and consecutive rows reuse the same input sectors.
+  const int per = (rows + warps - 1) / warps;
+  const int first = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * per;
+  const int last = first + per < rows ? first + per : rows;
+  if (first >= last) return;
+  int n = first / OHW, r = first - n * OHW, oh = r / OW, ow = r - oh * OW;
+  for (int row = first; row < last; row++) {
     const int h0 = oh * stride - pad, w0 = ow * stride - pad;
     const T* img = x + (int64_t)n * C * HW;
     T* out = cols + (int64_t)row * K;
@@ -58,6 +64,10 @@ __global__ void im2col_rows_kernel(const T* __restrict__ x, T* __restrict__ cols
       const int2 t = ktab[k];
       const int ih = h0 + (t.y >> 16), iw = w0 + (t.y & 0xFFFF);
       out[k] = (ih >= 0 && ih < H && iw >= 0 && iw < W) ? img[t.x + h0 * W + w0] : (T)0;
+    }
+    if (++ow == OW) {
+      ow = 0;
+      if (++oh == OH) oh = 0, n++;
     }
   }
 }
@@ -262,7 +272,7 @@ static char* im2col_launch(gt_ctx* ctx, const T* x, T* cols, const gt_geom& g) {
   int64_t total = g.N * g.OH * g.OW * g.C * g.KH * g.KW;
   if (total == 0) return nullptr;
   const int64_t rows = g.N * g.OH * g.OW, K = g.C * g.KH * g.KW;
-  const bool fits = K <= 6144 && g.KH < 32768 && g.KW < 32768 && rows < INT32_MAX &&
+  const bool fits = K <= 6144 && g.KH < 32768 && g.KW < 32768 && rows < INT32_MAX / 2 &&
                     g.C * g.H * g.W < INT32_MAX / 2 && (g.H + 2 * g.pad) * (g.W + 2 * g.pad) < INT32_MAX / 4;
   if (fits) {
     const int grid = (int)std::min<int64_t>(ceil_div(rows, 8), (int64_t)ctx->sm_count * 16);
