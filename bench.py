@@ -1,12 +1,28 @@
 """Training-step benchmark of go-tensor's B200 backend.
 
-Workload: the wide MLP Linear(4096,4096)-ReLU-Linear(4096,4096)-ReLU-
-Linear(4096,1000), float32, global batch 8192 (N(0,1) inputs, labels uniform
-in 0..999), CrossEntropyLoss, SGD lr 0.01 momentum 0.9 weight decay 1e-4;
-the batch is sharded over the GPUs (strong scaling), gradients averaged with
-NCCL. A step is one forward + backward + optimizer update of the whole batch.
+Workloads (`--workload`, default `wide_mlp`), one per benchmark config, each
+with seeded synthetic inputs of the config's shape and distribution and
+PyTorch-style uniform initial weights (nn/module.go:43-49, nn/conv.go:20-28):
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  wide_mlp    Linear(4096,4096)-ReLU-Linear(4096,4096)-ReLU-Linear(4096,1000),
+              float32, batch 8192, N(0,1) inputs, SGD lr 0.01 momentum 0.9
+              weight decay 1e-4 (the headline)
+  mlp         Linear(784,128)-ReLU-Linear(128,10), float32, batch 64,
+              U[0,1) inputs, Adam lr 1e-3
+  cnn         Conv2d(1,32,3,p1)-ReLU-MaxPool2d(2)-Conv2d(32,64,3,p1)-ReLU-
+              MaxPool2d(2)-Flatten-Linear(3136,128)-ReLU-Dropout(0)-
+              Linear(128,10), float32, batch 256, U[0,1) inputs, Adam
+  conv_stack  four Conv2d(3x3,p1)-ReLU-MaxPool2d(2) blocks of 64/128/256/512
+              channels on [3,32,32], Flatten-Linear(2048,10), float32, batch
+              1024, N(0,1) inputs, Adam
+  fp64_mlp    Linear(1024,1024)-Tanh-Linear(1024,1024)-Sigmoid-Linear(1024,10),
+              float64, batch 4096, U[-1,1) inputs, Adam
+
+Labels are uniform over the classes. A step is one forward + backward +
+optimizer update of the whole global batch, which is sharded over the GPUs
+(strong scaling) with gradients averaged over NCCL.
+
+    python bench.py [--workload W] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs under torchrun, one process per GPU. Rank 0 prints one JSON line.
 `--impl reference` times go-tensor's CPU path (the oracle's restatement of
@@ -32,14 +48,79 @@ sys.path.insert(0, os.path.join(ROOT, "go-tensor_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "train samples/sec (fwd+bwd+step)"
-WORKLOAD = "wide_mlp_4096-4096-4096-1000_b8192_sgd"
-GLOBAL_BATCH = 8192
-IN, HID, OUT = 4096, 4096, 1000
-LR, MOM, WD = 0.01, 0.9, 1e-4
-# fwd + dW for every layer + dX for layers 2-3, per sample (2 flops per MAC)
-GEMM_FLOPS_PER_SAMPLE = 2 * (3 * IN * HID + 3 * HID * HID + 3 * HID * OUT - IN * HID)
-BWD_GEMM_FLOPS_PER_SAMPLE = 2 * (2 * IN * HID + 2 * HID * HID + 2 * HID * OUT - IN * HID)
-CPU_SAMPLE_ROWS = 256
+
+# Per-sample GEMM flops (forward, dW, and dX for every layer but the first;
+# convolutions as 2 N OH OW O C KH KW with padded taps counted), the
+# algorithmic work the GEMM roofline divides.
+WORKLOADS = {
+    "wide_mlp": {
+        "name": "wide_mlp_4096-4096-4096-1000_b8192_sgd", "batch": 8192, "sample": [4096], "classes": 1000,
+        "dtype": "f32", "x": "normal", "opt": "sgd", "gemm_flops": 192_348_160,
+        "layers": [("Linear", (4096, 4096)), ("ReLU", ()), ("Linear", (4096, 4096)), ("ReLU", ()),
+                   ("Linear", (4096, 1000))]},
+    "mlp": {
+        "name": "mlp_784-128-10_b64_adam", "batch": 64, "sample": [784], "classes": 10, "dtype": "f32",
+        "x": "uniform01", "opt": "adam", "gemm_flops": 409_088,
+        "layers": [("Linear", (784, 128)), ("ReLU", ()), ("Linear", (128, 10))]},
+    "cnn": {
+        "name": "cnn_28x28_c32-64_fc128_b256_adam", "batch": 256, "sample": [1, 28, 28], "classes": 10,
+        "dtype": "f32", "x": "uniform01", "opt": "adam", "gemm_flops": 24_995_328,
+        "layers": [("Conv2d", (1, 32, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)),
+                   ("Conv2d", (32, 64, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)), ("Flatten", ()),
+                   ("Linear", (3136, 128)), ("ReLU", ()), ("Dropout", (0.0,)), ("Linear", (128, 10))]},
+    "conv_stack": {
+        "name": "conv_stack_32x32_c64-128-256-512_b1024_adam", "batch": 1024, "sample": [3, 32, 32],
+        "classes": 10, "dtype": "f32", "x": "normal", "opt": "adam", "gemm_flops": 346_939_392,
+        "layers": [("Conv2d", (3, 64, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)),
+                   ("Conv2d", (64, 128, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)),
+                   ("Conv2d", (128, 256, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)),
+                   ("Conv2d", (256, 512, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)), ("Flatten", ()),
+                   ("Linear", (2048, 10))]},
+    "fp64_mlp": {
+        "name": "fp64_mlp_1024-1024-1024-10_b4096_adam", "batch": 4096, "sample": [1024], "classes": 10,
+        "dtype": "f64", "x": "uniform11", "opt": "adam", "gemm_flops": 10_547_200,
+        "layers": [("Linear", (1024, 1024)), ("Tanh", ()), ("Linear", (1024, 1024)), ("Sigmoid", ()),
+                   ("Linear", (1024, 10))]},
+}
+SGD_CFG = (0.01, 0.9, 1e-4)   # lr, momentum, weight decay
+ADAM_LR = 1e-3
+# Optimizer bytes per parameter: SGD with momentum and weight decay reads p,
+# g, v and writes p, v; Adam reads p, g, m, v and writes p, m, v.
+OPT_BYTES = {("sgd", "f32"): 20, ("adam", "f32"): 28, ("adam", "f64"): 56, ("sgd", "f64"): 40}
+# FP64 peak: the HGX B200 datasheet's FP64 / FP64 tensor-core figure (the
+# measured-peaks file has no float64 entry).
+FP64_PEAK_TFLOPS = 37.0
+CPU_SAMPLE_ROWS = {"wide_mlp": 256, "mlp": 64, "cnn": 64, "conv_stack": 32, "fp64_mlp": 512}
+
+
+def make_layers(gm, spec):
+    return [getattr(gm, kind)(*args) for kind, args in spec]
+
+
+def init_params(model, spec, seed=1):
+    """U(+-1/sqrt(fan_in)) for every weight and bias, fan_in of its layer."""
+    rng = np.random.default_rng(seed)
+    fans = []
+    for kind, args in spec:
+        if kind == "Linear":
+            fans += [args[0], args[0]]
+        elif kind == "Conv2d":
+            fans += [args[0] * args[2] * args[2]] * 2
+    sd = {}
+    for (name, shape, _), fan in zip(model.params, fans):
+        b = 1 / np.sqrt(fan)
+        sd[name] = rng.uniform(-b, b, shape).astype(model.np_dtype)
+    return sd
+
+
+def make_batch(wl, rows, seed):
+    rng = np.random.default_rng(seed)
+    shape = [rows] + wl["sample"]
+    n = int(np.prod(shape))
+    x = {"normal": lambda: rng.standard_normal(n), "uniform01": lambda: rng.random(n),
+         "uniform11": lambda: rng.uniform(-1, 1, n)}[wl["x"]]()
+    y = rng.integers(0, wl["classes"], rows).astype(np.int32)
+    return x.reshape(shape).astype(np.float64 if wl["dtype"] == "f64" else np.float32), y
 
 
 def peaks():
@@ -117,52 +198,83 @@ def clocks_summary(proc, path, windows):
 # ---------------------------------------------------------------------------
 # CPU leg: the oracle's restatement of go-tensor's CPU path
 
-def cpu_step_time(rows: int, steps: int, warmup: int, threads: int):
+def cpu_step_time(wl, rows: int, steps: int, warmup: int, threads: int):
+    """Times the oracle's training loop on `rows` samples of the workload:
+    per step, the forward + backward (loss, ZeroGrad, Backward) and, apart,
+    the optimizer update of all parameters. Returns two lists of seconds."""
     from oracle import gotensor_ref as T
     from oracle import nn_ref as nn
     from oracle import optim_ref as optim
-    T.SetDefaultDType(T.Float32)
+    T.SetDefaultDType(T.Float64 if wl["dtype"] == "f64" else T.Float32)
     T._factories[T.CPU_TYPE] = lambda index: T.CPUBackend(threads)
     T._backends.clear()
     T.ManualSeed(1)
-    model = nn.NewSequential(nn.NewLinear(IN, HID), nn.NewReLU(), nn.NewLinear(HID, HID), nn.NewReLU(),
-                             nn.NewLinear(HID, OUT))
-    opt = optim.NewSGD(model.Parameters(), optim.SGDConfig(LR=LR, Momentum=MOM, WeightDecay=WD))
-    rng = np.random.default_rng(1)
-    x = T.New(rng.standard_normal(rows * IN), rows, IN)
-    y = list(rng.integers(0, OUT, rows))
-    times = []
+    model = nn.NewSequential(*[getattr(nn, "New" + kind)(*args) for kind, args in wl["layers"]])
+    if wl["opt"] == "sgd":
+        opt = optim.NewSGD(model.Parameters(), optim.SGDConfig(LR=SGD_CFG[0], Momentum=SGD_CFG[1],
+                                                               WeightDecay=SGD_CFG[2]))
+    else:
+        opt = optim.NewAdam(model.Parameters(), optim.AdamConfig(LR=ADAM_LR))
+    xb, yb = make_batch(wl, rows, 1)
+    x = T.New(xb.astype(np.float64).reshape(-1), *xb.shape)
+    y = [int(v) for v in yb]
+    fb, st = [], []
     for i in range(warmup + steps):
-        t = time.perf_counter()
+        t0 = time.perf_counter()
         loss = nn.CrossEntropyLoss(model.Forward(x), y)
         opt.ZeroGrad()
         loss.Backward()
-        opt.Step()
         loss.Item()
+        t1 = time.perf_counter()
+        opt.Step()
+        model.Parameters()[0].Float64s()[:1]  # the update has landed
+        t2 = time.perf_counter()
         if i >= warmup:
-            times.append(time.perf_counter() - t)
-    return times
+            fb.append(t1 - t0)
+            st.append(t2 - t1)
+    return fb, st
+
+
+def cpu_baseline(wl_key, steps, warmup, threads):
+    """Samples/s of the CPU path at the workload's full global batch: the
+    forward + backward cost (linear in the rows, as the row-split MatMul of
+    internal/cpu/linalg.go:65-81 is) measured on a sample of rows and scaled
+    to the batch, plus the optimizer update, which does not depend on the
+    batch, measured at its full size. Returns (value, seconds per step,
+    description)."""
+    wl = WORKLOADS[wl_key]
+    rows = min(CPU_SAMPLE_ROWS[wl_key], wl["batch"])
+    fb, st = cpu_step_time(wl, rows, steps, warmup, threads)
+    t_fb, t_st = statistics.median(fb), statistics.median(st)
+    t_step = t_fb * wl["batch"] / rows + t_st
+    desc = (f"forward+backward timed on {rows} of the {wl['batch']} rows and scaled to the batch "
+            f"({t_fb * 1e3:.1f} ms x {wl['batch'] // rows}), plus the optimizer update of all parameters timed "
+            f"at full size ({t_st * 1e3:.1f} ms); median of {len(fb)} steps after {warmup} warm-up; oracle "
+            "restatement of go-tensor's CPU backend and tensor/nn/optim (Go is absent)")
+    if rows == wl["batch"]:
+        desc = (f"the full batch of {rows} rows, median of {len(fb)} steps after {warmup} warm-up; oracle "
+                "restatement of go-tensor's CPU backend and tensor/nn/optim (Go is absent)")
+    return wl["batch"] / t_step, t_step, desc
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    wl = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
-    # ~1.7 s per 256-row step on 16 threads: keep the whole arm near a minute
-    rows = CPU_SAMPLE_ROWS if args.steps + args.warmup <= 40 else 64
-    times = cpu_step_time(rows, args.steps, args.warmup, threads)
-    total = sum(times)
-    value = rows * len(times) / total
+    # keep the arm to a few minutes: the sampled steps of the large configs take seconds each
+    steps = max(1, min(args.steps, 5))
+    warmup = 1
+    value, t_step, desc = cpu_baseline(args.workload, steps, warmup, threads)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1) inputs, uniform labels)",
-        "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "sample_rows_per_step": rows},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": wl["dtype"],
+        "data": "synthetic (seeded inputs of the config's shape and distribution, uniform labels)",
+        "config": {"workload": wl["name"], "global_batch": wl["batch"]},
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} rows of the batch per step, {len(times)} steps, oracle "
-                                   "restatement of go-tensor's CPU backend and tensor/nn/optim (Go absent)"},
+                         "sample": desc + f"; {steps} timed steps (the arm caps them at 5)"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -198,23 +310,25 @@ def barrier(world):
 def run_ours(args):
     import torch
 
+    from gotensor import FLOAT32, FLOAT64
     from gotensor import model as gm
     from gotensor._lib import check, cuda_lib
+    wl = WORKLOADS[args.workload]
+    f64 = wl["dtype"] == "f64"
+    es = 8 if f64 else 4
     rank, world, local = init_dist(args.gpus)
     torch.cuda.set_device(local)
     from gotensor.dist import exchange_unique_id, shard
-    lo, hi = shard(GLOBAL_BATCH, rank, world)
+    lo, hi = shard(wl["batch"], rank, world)
     B = hi - lo
-    layers = [gm.Linear(IN, HID), gm.ReLU(), gm.Linear(HID, HID), gm.ReLU(), gm.Linear(HID, OUT)]
-    model = gm.Model(layers, [B, IN], device=local)
+    model = gm.Model(make_layers(gm, wl["layers"]), [B] + wl["sample"], dtype=FLOAT64 if f64 else FLOAT32,
+                     device=local)
     lib, ctx = cuda_lib(), model.ctx.ptr
-    rng = np.random.default_rng(1)  # same weights on every rank
-    sd = {}
-    for name, shape, _ in model.params:
-        fan_in = IN if name.startswith("0.") else HID
-        sd[name] = rng.uniform(-1 / np.sqrt(fan_in), 1 / np.sqrt(fan_in), shape).astype(np.float32)
-    model.load_state_dict(sd)
-    model.sgd(LR, MOM, WD)
+    model.load_state_dict(init_params(model, wl["layers"], 1))  # same weights on every rank
+    if wl["opt"] == "sgd":
+        model.sgd(*SGD_CFG)
+    else:
+        model.adam(lr=ADAM_LR)
     if world > 1:
         # rank 0's stdout carries exactly one JSON line: keep NCCL's version banner off it
         if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
@@ -223,13 +337,11 @@ def run_ours(args):
     model.enable_graph(not args.no_graph)
 
     # This rank's shard of the batch, in pinned host memory for the e2e leg.
-    drng = np.random.default_rng(100 + rank)
-    x_np = drng.standard_normal((B, IN)).astype(np.float32)
-    y_np = drng.integers(0, OUT, B).astype(np.int32)
+    x_np, y_np = make_batch(wl, B, 100 + rank)
     xh = torch.from_numpy(x_np).pin_memory()
     yh = torch.from_numpy(y_np).pin_memory()
-    loss_h = torch.zeros(1, dtype=torch.float32).pin_memory()
-    h2d = xh.numel() * 4 + yh.numel() * 4
+    loss_h = torch.zeros(1, dtype=torch.float64 if f64 else torch.float32).pin_memory()
+    h2d = xh.numel() * es + yh.numel() * 4
     model.set_batch(x_np, y_np)
 
     def steps_resident(k):
@@ -245,7 +357,7 @@ def run_ours(args):
             if i + 1 < k:
                 model.stage_batch(xh.data_ptr(), yh.data_ptr())
             model.train_step()
-            check(lib.gt_download_async(ctx, loss_h.data_ptr(), model.lib.gth_loss_device(model.ptr), 4))
+            check(lib.gt_download_async(ctx, loss_h.data_ptr(), model.lib.gth_loss_device(model.ptr), es))
 
     def timed(fn, k):
         """Device time of fn(k) (k steps) on the model's stream, max over ranks."""
@@ -274,7 +386,7 @@ def run_ours(args):
     launches = lib.gt_launch_count() - before
     if launches == 0:  # graph replays launch without passing through the library's counter
         launches = launches_per_step * args.steps
-    value = GLOBAL_BATCH * args.steps / (ms_total / 1e3)
+    value = wl["batch"] * args.steps / (ms_total / 1e3)
     loss = model.loss()
 
     steps_e2e(2)
@@ -282,37 +394,37 @@ def run_ours(args):
     ms_e2e = timed(steps_e2e, args.steps)
     windows.append((t0, time.time()))
     clocks = clocks_summary(proc, cpath, windows)
-    e2e = GLOBAL_BATCH * args.steps / (ms_e2e / 1e3)
+    e2e = wl["batch"] * args.steps / (ms_e2e / 1e3)
 
-    # Roofline of the dominant kernel, the float32 GEMM (tcgen05 3xTF32):
-    # K more steps of the same workload with every GEMM launch bracketed by
-    # CUDA events on the model's stream (graph replay off: events inside a
-    # replayed graph keep only the last replay's times).
-    roof = step_roofline(lib, model, args.steps)
+    # Roofline of the dominant kernel, the GEMM (tcgen05 3xTF32 for float32,
+    # the FP64 pipe for float64): K more steps of the same workload with every
+    # GEMM launch bracketed by CUDA events on the model's stream (graph replay
+    # off: events inside a replayed graph keep only the last replay's times).
+    roof = step_roofline(lib, model, args.steps, wl, args.workload)
     roof["roofline"]["step_ms_graph"] = ms_total / args.steps
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         threads = os.cpu_count() or 1
-        times = cpu_step_time(CPU_SAMPLE_ROWS, 3, 1, threads)
-        cpu = {"value": CPU_SAMPLE_ROWS * len(times) / sum(times), "unit": "samples/s", "cores": threads,
-               "kind": "port", "sample": f"{CPU_SAMPLE_ROWS} rows per step, {len(times)} timed steps after 1 "
-                                         "warm-up; oracle restatement of go-tensor's CPU path (Go absent)"}
+        cval, _, desc = cpu_baseline(args.workload, 2, 1, threads)
+        cpu = {"value": cval, "unit": "samples/s", "cores": threads, "kind": "port", "sample": desc}
 
     if rank == 0:
+        opt_desc = (f"sgd(lr={SGD_CFG[0]}, momentum={SGD_CFG[1]}, wd={SGD_CFG[2]})" if wl["opt"] == "sgd"
+                    else f"adam(lr={ADAM_LR})")
         line = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,1) inputs, uniform labels, PyTorch-style uniform init)",
-            "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "per_gpu_batch": B,
-                       "parallelism": f"dp{world}", "optimizer": "sgd(lr=0.01, momentum=0.9, wd=1e-4)",
-                       "graph": not args.no_graph,
-                       "l2": "per-step working set (weights, grads, momentum 452 MB + activations) exceeds L2",
-                       "gemm": "tcgen05 3xTF32" if roof.get("path") == "tc" else "SIMT fp32"},
+            "scaling": "strong", "vs_baseline": None, "dtype": wl["dtype"],
+            "data": "synthetic (seeded inputs of the config's shape and distribution, uniform labels, "
+                    "PyTorch-style uniform init)",
+            "config": {"workload": wl["name"], "global_batch": wl["batch"], "per_gpu_batch": B,
+                       "parallelism": f"dp{world}", "optimizer": opt_desc, "graph": not args.no_graph,
+                       "l2": l2_note(args.workload, model),
+                       "gemm": roof["path"]},
             "gemm_launches": roof["launches"],
             "loss_after": loss,
-            "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+            "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": es},
             "gpu_launches": int(launches),
             "roofline": roof["roofline"],
             "optimizer_roofline": roof["optimizer"],
@@ -328,16 +440,26 @@ def run_ours(args):
     return 0
 
 
+def l2_note(key, model):
+    """Why no L2 flush is needed between timed steps: the step's working set
+    (parameters, gradients, optimizer state, activations) against the 126 MB L2."""
+    es = model.np_dtype().itemsize
+    state = model.num_params * es * (3 if WORKLOADS[key]["opt"] == "sgd" else 4)
+    if key in ("wide_mlp", "conv_stack", "fp64_mlp", "cnn"):
+        return (f"per-step working set exceeds L2: parameters, gradients and optimizer state "
+                f"{state / 1e6:.0f} MB plus activations")
+    return (f"the whole working set ({state / 1e6:.1f} MB of parameters and state plus activations) fits in "
+            "L2: a small-batch, launch-latency-bound config, timed as it runs")
+
+
 # dram__bytes_read.sum + dram__bytes_write.sum of the GEMM launches of one
-# training step of this workload, from one ncu capture of
+# training step of the wide MLP, from one ncu capture of
 # `bench.py --steps 1 --warmup 3 --skip-cpu` (launches 19-37: the second
 # warm-up step, replayed from the CUDA graph).
-GEMM_TRAFFIC_BYTES_PER_STEP = 4_224_623_616
-GEMM_LAUNCHES_PER_STEP = 8
-# The SGD update: read p, g, v and write p, v (float32), and the DRAM traffic
-# of its launch in the same capture.
-SGD_BYTES_PER_PARAM = 20
-SGD_TRAFFIC_BYTES = 698_175_488
+GEMM_TRAFFIC_BYTES_PER_STEP = {"wide_mlp": 4_224_623_616}
+GEMM_LAUNCHES_PER_STEP = {"wide_mlp": 8}
+# The wide MLP's SGD update: DRAM traffic of its launch in the same capture.
+OPT_TRAFFIC_BYTES = {"wide_mlp": 698_175_488}
 
 
 def _peak_3xtf32():
@@ -355,15 +477,22 @@ def _peak_3xtf32_sustained():
         return None
 
 
-def step_roofline(lib, model, steps):
+def step_roofline(lib, model, steps, wl, key):
     """Runs `steps` training steps with the GEMM launch timer on; returns the
     flop rate of all GEMM launches (total algorithmic flops / total kernel
-    time) against the 3xTF32 peak, plus the per-shape breakdown."""
+    time) against the GEMM peak of the dtype, the optimizer kernel's bytes per
+    second against HBM, and the per-shape breakdown."""
     from gotensor._lib import check
     ctx = model.ctx.ptr
-    peak, note = _peak_3xtf32()
+    f64 = wl["dtype"] == "f64"
+    if f64:
+        peak, note, sustained = FP64_PEAK_TFLOPS, "FP64 peak = 37 TF/s (HGX B200 datasheet; nominal)", None
+    else:
+        peak, note = _peak_3xtf32()
+        note += " (of measured)"
+        sustained = _peak_3xtf32_sustained()
     model.enable_graph(False)
-    check(lib.gt_gemm_timer_start(ctx, steps * 32 + 64))
+    check(lib.gt_gemm_timer_start(ctx, steps * 64 + 64))
     pass_ms, opt_ms, t = ctypes.c_float(), 0.0, ctypes.c_float()
     check(lib.gt_mark(ctx, 4))
     for _ in range(steps):
@@ -379,13 +508,14 @@ def step_roofline(lib, model, steps):
     check(lib.gt_elapsed_ms(ctx, 4, 5, ctypes.byref(pass_ms)))
     hbm, _, hbm_kind = peaks()
     nparams = model.num_params
-    opt_gbs = SGD_BYTES_PER_PARAM * nparams / (opt_ms / steps / 1e3) / 1e9
-    optimizer = {"bound": "hbm", "kernel": "sgd_kernel (momentum + weight decay, one pass)",
-                 "achieved": opt_gbs, "peak": hbm, "unit": "GB/s", "frac": opt_gbs / hbm,
-                 "bytes_per_launch": SGD_BYTES_PER_PARAM * nparams, "ms_per_launch": opt_ms / steps,
-                 "traffic": SGD_TRAFFIC_BYTES,
-                 "note": f"{SGD_BYTES_PER_PARAM} B/param (read p, g, v; write p, v) x {nparams} params; "
-                         f"peak = {hbm_kind} copy bandwidth"}
+    bpp = OPT_BYTES[(wl["opt"], wl["dtype"])]
+    opt_gbs = bpp * nparams / (opt_ms / steps / 1e3) / 1e9
+    kern = ("sgd_kernel (momentum + weight decay, one pass)" if wl["opt"] == "sgd"
+            else "adam_kernel (one pass; bias corrections from a device step counter)")
+    optimizer = {"bound": "hbm", "kernel": kern, "achieved": opt_gbs, "peak": hbm, "unit": "GB/s",
+                 "frac": opt_gbs / hbm, "bytes_per_launch": bpp * nparams, "ms_per_launch": opt_ms / steps,
+                 "traffic": OPT_TRAFFIC_BYTES.get(key),
+                 "note": f"{bpp} B/param x {nparams} params; peak = {hbm_kind} copy bandwidth (of {hbm_kind})"}
     n, dropped = ctypes.c_int64(), ctypes.c_int64()
     check(lib.gt_gemm_timer_count(ctx, ctypes.byref(n), ctypes.byref(dropped)))
     if dropped.value:
@@ -393,42 +523,55 @@ def step_roofline(lib, model, steps):
     shapes = {}
     last_step = []  # (M x N x K, ms) of every GEMM of the pass's last step, in launch order
     total_ms = total_flops = 0.0
-    tc = True
+    paths = set()
     mnk = (ctypes.c_int64 * 3)()
     path = ctypes.c_int()
     ms = ctypes.c_float()
     for i in range(n.value):
         check(lib.gt_gemm_timer_read(ctx, i, mnk, ctypes.byref(path), ctypes.byref(ms)))
-        key = f"{mnk[0]}x{mnk[1]}x{mnk[2]}"
+        key_s = f"{mnk[0]}x{mnk[1]}x{mnk[2]}"
         if i >= n.value - n.value // steps:
-            last_step.append((key, round(ms.value, 4)))
+            last_step.append((key_s, round(ms.value, 4)))
         flops = 2.0 * mnk[0] * mnk[1] * mnk[2]
-        e = shapes.setdefault(key, {"launches": 0, "ms": 0.0, "flops": flops})
+        e = shapes.setdefault(key_s, {"launches": 0, "ms": 0.0, "flops": flops, "path": path.value})
         e["launches"] += 1
         e["ms"] += ms.value
         total_ms += ms.value
         total_flops += flops
-        tc = tc and path.value == 2
+        paths.add(path.value)
     check(lib.gt_gemm_timer_stop(ctx))
     per_step = n.value // steps
     achieved = total_flops / (total_ms / 1e3) / 1e12
     traffic = None
-    if GEMM_TRAFFIC_BYTES_PER_STEP and per_step == GEMM_LAUNCHES_PER_STEP:
-        traffic = GEMM_TRAFFIC_BYTES_PER_STEP / GEMM_LAUNCHES_PER_STEP
+    if GEMM_TRAFFIC_BYTES_PER_STEP.get(key) and per_step == GEMM_LAUNCHES_PER_STEP.get(key):
+        traffic = GEMM_TRAFFIC_BYTES_PER_STEP[key] / GEMM_LAUNCHES_PER_STEP[key]
+    names = {1: "SIMT (FFMA; float64 on DFMA or the FP64 tensor path, mma.sync f64)", 2: "tcgen05 3xTF32",
+             4: "tcgen05 3xTF32 implicit-GEMM convolution"}
     breakdown = {k: {"launches_per_step": v["launches"] // steps, "ms_per_launch": v["ms"] / v["launches"],
-                     "tflops": v["flops"] * v["launches"] / (v["ms"] / 1e3) / 1e12} for k, v in shapes.items()}
-    return {"path": "tc" if tc else "simt", "launches": per_step,
+                     "tflops": v["flops"] * v["launches"] / (v["ms"] / 1e3) / 1e12,
+                     "path": names.get(v["path"], str(v["path"]))} for k, v in shapes.items()}
+    step_ms = pass_ms.value / steps
+    alg = wl["gemm_flops"] * model.input_shape[0]
+    return {"path": " + ".join(sorted(names.get(p, str(p)) for p in paths)), "launches": per_step,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "gemm_tf32x3_pair (float32 GEMM, 3xTF32 on tcgen05): every GEMM launch of the "
-                                   "step (forward, dW, dX), M x N x K below",
-                         "flops_per_launch": total_flops / n.value, "ms_per_launch": total_ms / n.value,
-                         "gemm_share_of_step": total_ms / pass_ms.value, "step_ms_timed_pass": pass_ms.value / steps,
+                         "kernel": ("every GEMM launch of the step (forward, dW, dX), M x N x K below; float64 "
+                                    "on the FP64 pipe" if f64 else
+                                    "every GEMM launch of the step (forward, dW, dX; convolutions as GEMMs), "
+                                    "M x N x K below"),
+                         "flops_per_launch": total_flops / max(n.value, 1), "ms_per_launch": total_ms / max(n.value, 1),
+                         "algorithmic_gemm_flops_per_step": alg,
+                         "algorithmic_tflops_over_step": alg / (step_ms / 1e3) / 1e12,
+                         "gemm_share_of_step": total_ms / pass_ms.value, "step_ms_timed_pass": step_ms,
                          "by_shape": breakdown, "last_step_launches": last_step,
-                         "peak_note": note + " (of measured)",
-                         "peak_sustained": _peak_3xtf32_sustained(),
-                         "frac_of_sustained": (achieved / _peak_3xtf32_sustained()) if _peak_3xtf32_sustained() else None},
+                         "peak_note": note, "peak_sustained": sustained,
+                         "frac_of_sustained": (achieved / sustained) if sustained else None},
             "optimizer": optimizer}
+
+
+IN, HID, OUT = 4096, 4096, 1000  # the wide MLP's widths, for the isolated GEMM and eval modes
+GLOBAL_BATCH = 8192
+WORKLOAD = WORKLOADS["wide_mlp"]["name"]
 
 
 def gemm_isolated(lib, model, B, reps):
@@ -471,6 +614,7 @@ def gemm_isolated(lib, model, B, reps):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="wide_mlp")
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")

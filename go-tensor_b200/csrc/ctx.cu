@@ -130,6 +130,16 @@ char* gt_release(gt_ctx* ctx, void* ptr) {
   return nullptr;
 }
 
+char* gt_pool_usage(gt_ctx* ctx, uint64_t* used_bytes, uint64_t* reserved_bytes) {
+  GT_ENTER(ctx);
+  uint64_t used = 0, reserved = 0;
+  GT_CUDA(cudaMemPoolGetAttribute(ctx->pool, cudaMemPoolAttrUsedMemCurrent, &used));
+  GT_CUDA(cudaMemPoolGetAttribute(ctx->pool, cudaMemPoolAttrReservedMemCurrent, &reserved));
+  if (used_bytes) *used_bytes = used;
+  if (reserved_bytes) *reserved_bytes = reserved;
+  return nullptr;
+}
+
 char* gt_zero(gt_ctx* ctx, void* dst, size_t bytes) {
   GT_ENTER(ctx);
   if (bytes) GT_CUDA(cudaMemsetAsync(dst, 0, bytes, ctx->stream));

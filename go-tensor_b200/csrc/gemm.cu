@@ -114,6 +114,8 @@ char* gt_set_gemm_sm_reserve(gt_ctx* ctx, int sms) {
 
 void gt_debug_set_gemm_path(int path) { set_gemm_path(path); }
 void gt_debug_set_gemm_splits(int splits) { set_gemm_splits(splits < 0 ? 0 : splits); }
+void gt_debug_set_tc_wait_limit_us(int64_t us) { set_tc_wait_limit_us(us); }
+void gt_debug_tc_withhold_arrive(void) { tc_withhold_next_arrive(); }
 int gt_gemm_path_taken(void) { return g_gemm_taken; }
 
 char* gt_gemm_timer_start(gt_ctx* ctx, int64_t capacity) {

@@ -83,5 +83,7 @@ char* gemm(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>
 void set_gemm_path(int path);
 int gemm_path();
 void set_gemm_splits(int splits);  // tcgen05 path: 0 = automatic, else this many K-splits
+void set_tc_wait_limit_us(int64_t us);  // tcgen05 barrier-wait limit (0: the default 2 s)
+void tc_withhold_next_arrive();         // the next tcgen05 GEMM's first slice never reaches its MMA
 
 }  // namespace gt

@@ -78,7 +78,7 @@ constexpr uint32_t BUF_COLS = 256;  // one partial accumulator: 128 lanes x 256 
 // the split keeps the block's total: 256 * 64 + 256 * 192 = 256 * 128 * 2.
 constexpr int REGS_LOW = 64, REGS_HIGH = 192;
 static_assert(256 * REGS_LOW + 256 * REGS_HIGH <= THREADS * 128, "register split exceeds the launch's registers");
-constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s; a healthy wait takes microseconds
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // default limit, 2 s; a healthy wait takes microseconds
 
 static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -147,12 +147,12 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 
 // Waits for the phase of `bar` with the given parity; false (and the error
-// word set to `site`) once kTimeoutNs has passed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {
+// word set to `site`) once `limit_ns` has passed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kTimeoutNs) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicCAS(&g_tc_error, 0, site);
       return false;
     }
@@ -391,6 +391,11 @@ struct SplitPlan {
   int whole = 0;
   int splits = 1;
   float* ws = nullptr;  // [splits][tiles - whole][256 * 256]
+  uint64_t wait_limit_ns = kTimeoutNs;  // every barrier wait gives up after this long
+  // Test hook (gt_debug_tc_withhold_arrive): the leader CTA's splitter of ring
+  // slot 0 withholds its arrival for the first slice, so the MMA issuer's wait
+  // for that slice runs out and the kernel takes its error path.
+  int withhold_arrive = 0;
 };
 
 constexpr int64_t TILE_ELEMS = 2 * BM * BN;
@@ -481,7 +486,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const int b_row = nt * BN + (int)rank * BNH;
           for (int kt = kb; kt < ke; kt++, it++) {
             const int st = it % STAGES;
-            if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1)) {
+            if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1, sp.wait_limit_ns)) {
               *failed = 1;
               break;
             }
@@ -507,7 +512,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         if (*failed) {  // let copies in flight land before the CTA tears down
           for (int i = issued_to > STAGES ? issued_to - STAGES : 0; i < issued_to; i++)
-            mbar_wait(&sh->full[i % STAGES], (i / STAGES) & 1, 5);
+            mbar_wait(&sh->full[i % STAGES], (i / STAGES) & 1, 5, kTimeoutNs);  // copies land in microseconds
         }
       }
     } else if (warp == 1) {
@@ -522,14 +527,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const bool group_start = (kt - kb) % GROUP == 0;
             const uint32_t buf = (uint32_t)(group & 1);
             if (group_start) {  // the promoters must have read this buffer's previous partial
-              if (!mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2)) {
+              if (!mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2, sp.wait_limit_ns)) {
                 stop = true;
                 break;
               }
               tc_fence_after();
             }
             const int st = it % STAGES;
-            if (!mbar_wait(&sh->split[st], (it / STAGES) & 1, 3)) {
+            if (!mbar_wait(&sh->split[st], (it / STAGES) & 1, 3, sp.wait_limit_ns)) {
               stop = true;
               break;
             }
@@ -557,7 +562,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                          smem_u32(&sh->mma_done))
                      : "memory");
-        mbar_wait(&sh->mma_done, 0, 6);
+        mbar_wait(&sh->mma_done, 0, 6, kTimeoutNs);
       }
     } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + STAGES) {
       // ---- splitters (both CTAs): this warp owns ring slot st, i.e. every
@@ -571,7 +576,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
       for (int it = st; it < total; it += STAGES) {
         if (__shfl_sync(0xffffffffu, *failed, 0)) break;
-        if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4)) {
+        if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4, sp.wait_limit_ns)) {
           *failed = 1;
           break;
         }
@@ -579,7 +584,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
         split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + B_BYTES), B_BYTES / 16, lane);
         fence_async_shared();  // generic-proxy writes -> visible to the tensor core
-        mbar_arrive_rank(&sh->split[st], 0);
+        if (!(sp.withhold_arrive && it == 0 && st == 0 && leader)) mbar_arrive_rank(&sh->split[st], 0);
       }
     }
   } else {
@@ -608,7 +613,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int g = 0; g < groups; g++, group++) {
         const uint32_t buf = (uint32_t)(group & 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&sh->pfull[buf], (group >> 1) & 1, 7))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&sh->pfull[buf], (group >> 1) & 1, 7, sp.wait_limit_ns))) {
           *failed = 1;
           ok = false;
           break;
@@ -804,6 +809,8 @@ __global__ void splitk_reduce_bits_kernel(const float* __restrict__ ws, SplitPla
 // no split; every tile split S ways (too few tiles for the SM pairs); or only
 // the tiles of a mostly empty last round split S ways (wave quantisation).
 static int g_force_splits = 0;
+static uint64_t g_wait_limit_ns = kTimeoutNs;  // gt_debug_set_tc_wait_limit_us
+static int g_withhold_next = 0;               // gt_debug_tc_withhold_arrive
 
 static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k) {
   SplitPlan best;
@@ -852,6 +859,8 @@ static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k) {
 }  // namespace tc
 
 void set_gemm_splits(int splits) { tc::g_force_splits = splits; }
+void set_tc_wait_limit_us(int64_t us) { tc::g_wait_limit_ns = us > 0 ? (uint64_t)us * 1000ull : tc::kTimeoutNs; }
+void tc_withhold_next_arrive() { tc::g_withhold_next = 1; }
 
 // Reports (and clears) a timed-out pipeline wait of an earlier tcgen05 GEMM.
 char* tc_check_errors() {
@@ -878,6 +887,9 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
   const int64_t tiles = ceil_div(s.M, 2 * tc::BM) * ceil_div(s.N, tc::BN);
   const int64_t n_tiles = ceil_div(s.N, tc::BN);
   tc::SplitPlan sp = tc::choose_plan(tiles, tc::pairs_available(ctx), ceil_div(s.K, tc::BK));
+  sp.wait_limit_ns = tc::g_wait_limit_ns;
+  sp.withhold_arrive = tc::g_withhold_next;
+  tc::g_withhold_next = 0;
   char* err;
   if (sp.splits > 1) {
     const int64_t rest = tiles - sp.whole;

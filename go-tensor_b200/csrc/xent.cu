@@ -71,6 +71,96 @@ __global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restr
   }
 }
 
+// The same for rows of at most 32 * NPL classes, with one float64 exp per
+// element: lane l holds elements l, l + 32, ... of its row in registers (NPL
+// values, a compile-time count so the array never leaves registers), loaded
+// once. e = T(exp(double(x - m))) replaces x in place, is summed, and gives
+// the gradient q * e from the same rounded value the streaming kernel
+// recomputes, so both kernels produce identical bits. A log-probability
+// x_j - m - L is non-finite exactly when x_j - m or L is (x - m <= 0 and
+// 0 <= L <= log C), so the Pick's NaN rule needs no third pass either.
+template <typename T, int NPL>
+__global__ void xent_rows_reg_kernel(const T* __restrict__ x, const int32_t* __restrict__ labels, int64_t B, int C,
+                                     T c, T* __restrict__ row_terms, T* __restrict__ dx, int32_t* bad_label) {
+  const int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t i = warp; i < B; i += nwarps) {
+    const T* xr = x + i * C;
+    const int32_t y = labels[i];
+    const bool bad = y < 0 || y >= C;
+    if (bad && lane == 0 && bad_label) *bad_label = 1;
+    T v[NPL];
+#pragma unroll
+    for (int t = 0; t < NPL; t++) {
+      const int j = lane + 32 * t;
+      v[t] = j < C ? __ldg(xr + j) : (T)(-INFINITY);
+    }
+    T m = (T)(-INFINITY);
+#pragma unroll
+    for (int t = 0; t < NPL; t++)
+      if (lane + 32 * t < C) m = go_max(m, v[t]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = go_max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    T S = (T)0, s_y = (T)0;
+    bool nonfinite = false;
+#pragma unroll
+    for (int t = 0; t < NPL; t++) {
+      const int j = lane + 32 * t;
+      if (j < C) {
+        const T s = sub_rn(v[t], m);
+        if (j == y) s_y = s;
+        else if (!isfinite(s)) nonfinite = true;
+        v[t] = (T)exp((double)s);
+        S = add_rn(S, v[t]);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) S = add_rn(S, __shfl_xor_sync(0xffffffffu, S, off));
+    const T Lse = (T)log((double)S);
+    if (dx) {
+      const T q = div_rn(c, S);
+      T* dr = dx + i * C;
+#pragma unroll
+      for (int t = 0; t < NPL; t++) {
+        const int j = lane + 32 * t;
+        if (j < C) {
+          const T g = mul_rn(q, v[t]);
+          dr[j] = j == y ? add_rn(-c, g) : g;
+        }
+      }
+    }
+    // picked: the label's log-probability, summed over the warp like the
+    // streaming kernel's picked terms (one lane non-zero)
+    T picked = (lane == (y & 31) && !bad) ? sub_rn(s_y, Lse) : (T)0;
+    if (!isfinite(Lse) && C > 1) nonfinite = true;  // every off-label log-probability is non-finite
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      picked = add_rn(picked, __shfl_xor_sync(0xffffffffu, picked, off));
+      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, off) != 0;
+    }
+    if (lane == 0) row_terms[i] = (nonfinite || bad) ? (T)NAN : picked;
+  }
+}
+
+// Launches the row kernel that fits C: register rows up to 1024 classes,
+// else the streaming kernel.
+template <typename T>
+static void xent_rows_launch(gt_ctx* ctx, const T* x, const int32_t* labels, int64_t B, int64_t C, T c, T* terms,
+                             T* dx, int32_t* bad) {
+  const int grid = grid_for(ctx, B * 32, 256);
+  if (C <= 32)
+    xent_rows_reg_kernel<T, 1><<<grid, 256, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad);
+  else if (C <= 128)
+    xent_rows_reg_kernel<T, 4><<<grid, 256, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad);
+  else if (C <= 512)
+    xent_rows_reg_kernel<T, 16><<<grid, 256, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad);
+  else if (C <= 1024)
+    xent_rows_reg_kernel<T, 32><<<grid, 256, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad);
+  else
+    xent_rows_kernel<T><<<grid, 256, 0, ctx->stream>>>(x, labels, B, C, c, terms, dx, bad);
+}
+
 // loss = -(sum_i row_terms[i] * c), one block, fixed reduction order.
 template <typename T>
 __global__ void xent_sum_kernel(const T* __restrict__ row_terms, int64_t B, T c, T* __restrict__ loss) {
@@ -131,8 +221,7 @@ extern "C" char* gt_xent_fwd_bwd_noalloc(gt_ctx* ctx, int dtype, const void* log
   GT_TRY(xent_rows_buffer(ctx, &terms));
   GT_DISPATCH(dtype, {
     T c = (T)(1.0 / (double)B);
-    xent_rows_kernel<T><<<grid_for(ctx, B * 32, 256), 256, 0, ctx->stream>>>(
-        (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
+    xent_rows_launch<T>(ctx, (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
     xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
   });
   count_launch(2);
@@ -151,8 +240,7 @@ extern "C" char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, con
   GT_TRY(scratch(ctx, B * es, &terms));
   GT_DISPATCH(dtype, {
     T c = (T)(1.0 / (double)B);  // MulScalar(1/float64(N)) rounds the scalar to T
-    xent_rows_kernel<T><<<grid_for(ctx, B * 32, 256), 256, 0, ctx->stream>>>(
-        (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
+    xent_rows_launch<T>(ctx, (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label);
     xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
   });
   count_launch(2);

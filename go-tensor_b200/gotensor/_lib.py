@@ -66,6 +66,7 @@ CUDA_API = {
     "gt_alloc": ("err", [_P, ctypes.c_size_t, ctypes.POINTER(_P)]),
     "gt_release": ("err", [_P, _P]),
     "gt_zero": ("err", [_P, _P, ctypes.c_size_t]),
+    "gt_pool_usage": ("err", [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
     "gt_upload": ("err", [_P, _P, _P, ctypes.c_size_t]),
     "gt_download": ("err", [_P, _P, _P, ctypes.c_size_t]),
     "gt_upload_async": ("err", [_P, _P, _P, ctypes.c_size_t]),
@@ -133,6 +134,8 @@ CUDA_API = {
     "gt_set_gemm_sm_reserve": ("err", [_P, _INT]),
     "gt_debug_set_gemm_path": (None, [_INT]),
     "gt_debug_set_gemm_splits": (None, [_INT]),
+    "gt_debug_set_tc_wait_limit_us": (None, [_I64]),
+    "gt_debug_tc_withhold_arrive": (None, []),
     "gt_gemm_path_taken": (_INT, []),
 }
 
@@ -175,6 +178,8 @@ HOST_API = {
     "gth_count_correct": ("err", [_P, ctypes.POINTER(_I64)]),
     "gth_dp_init": ("err", [_P, _INT, _INT, ctypes.c_char_p, _INT, _I64]),
     "gth_bucket_plan": (_INT, [ctypes.POINTER(_I64), _INT, _I64, ctypes.POINTER(_I64), _INT]),
+    "gth_row_chunk_plan": (_INT, [ctypes.POINTER(_I64), _INT, _I64, _I64, _I64, _INT, ctypes.POINTER(_I64), _INT,
+                                  ctypes.POINTER(_I64), _INT, ctypes.POINTER(_INT)]),
 }
 
 _cuda = None

@@ -239,6 +239,22 @@ def bucket_plan(sizes, bucket_elems):
     return [(bounds[2 * i], bounds[2 * i + 1]) for i in range(cnt)]
 
 
+def row_chunk_plan(buckets, w_off, N, K, chunks):
+    """The runtime's row-chunk split of the first Linear's weight bucket (host
+    only): (row boundaries, new bucket list), or ([], buckets) unchanged."""
+    lib = _lib.host_lib()
+    nb = len(buckets)
+    flat = (ctypes.c_int64 * max(2 * nb, 1))(*[v for b in buckets for v in b])
+    cap = N // 32 + 3
+    rows = (ctypes.c_int64 * cap)()
+    out = (ctypes.c_int64 * (2 * (nb + cap)))()
+    out_nb = ctypes.c_int()
+    nr = lib.gth_row_chunk_plan(flat, nb, w_off, N, K, chunks, rows, cap, out, nb + cap, ctypes.byref(out_nb))
+    if nr == 0:
+        return [], list(buckets)
+    return list(rows[:nr]), [(out[2 * i], out[2 * i + 1]) for i in range(out_nb.value)]
+
+
 def unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     check(_lib.cuda_lib().gt_comm_unique_id(buf))

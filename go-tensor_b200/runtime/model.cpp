@@ -625,26 +625,16 @@ void Model::dp_init(int rank, int world, const unsigned char id[128], int timeou
   if (const char* c = getenv("GT_DP_LAST_CHUNKS")) chunks = std::max(1, atoi(c));
   if (world > 1 && chunks > 1 && first_param_op_ >= 0 && ops_[first_param_op_].kind == Op::LINEAR) {
     const Op& op = ops_[first_param_op_];
-    int64_t per = (op.N + chunks - 1) / chunks;
-    per = per >= 256 ? per / 256 * 256 : per / 32 * 32;  // whole tiles where they fit
-    for (size_t b = 0; per > 0 && b < buckets_.size(); b++) {
-      if (buckets_[b].first != op.w_off) continue;
-      for (int64_t r = 0; r < op.N; r += per) first_rows_.push_back(r);
-      first_rows_.push_back(op.N);
-      if (first_rows_.size() < 3) {
-        first_rows_.clear();
-        break;
-      }
-      // sub-buckets in the list's order (highest offsets first); the last
-      // one keeps the rest of the bucket (the bias and anything after it)
-      std::vector<std::pair<int64_t, int64_t>> sub;
-      const int64_t end = buckets_[b].second;
-      for (size_t j = first_rows_.size() - 1; j-- > 0;)
-        sub.emplace_back(op.w_off + first_rows_[j] * op.K,
-                         j + 2 == first_rows_.size() ? end : op.w_off + first_rows_[j + 1] * op.K);
-      buckets_.erase(buckets_.begin() + (long)b);
-      buckets_.insert(buckets_.begin() + (long)b, sub.begin(), sub.end());
-      break;
+    const int64_t cap = op.N / 32 + 3;  // chunks are at least 32 rows
+    std::vector<int64_t> flat, rows(cap), out(2 * (nb + cap));
+    for (auto& b : buckets_) flat.push_back(b.first), flat.push_back(b.second);
+    int out_nb = 0;
+    const int nr = gth_row_chunk_plan(flat.data(), nb, op.w_off, op.N, op.K, chunks, rows.data(), (int)rows.size(),
+                                      out.data(), (int)out.size() / 2, &out_nb);
+    if (nr > 0) {
+      first_rows_.assign(rows.begin(), rows.begin() + nr);
+      buckets_.clear();
+      for (int b = 0; b < out_nb; b++) buckets_.emplace_back(out[2 * b], out[2 * b + 1]);
     }
   }
   nb = (int)buckets_.size();
@@ -676,4 +666,43 @@ extern "C" int gth_bucket_plan(const int64_t* sizes, int n, int64_t bucket_elems
     }
   }
   return count;
+}
+
+// The first layer's weight gradient is the backward's last GEMM, so the
+// all-reduce of its bucket cannot overlap anything. The bucket that starts at
+// that weight (w_off, N rows of K) is split at row chunks: rows per chunk a
+// multiple of 256 (whole GEMM tiles) or, for small layers, of 32. Sub-buckets
+// are listed highest offsets first, the order the backward computes the
+// chunks; the last one keeps the rest of the original bucket (the bias and
+// anything after it).
+extern "C" int gth_row_chunk_plan(const int64_t* bounds, int nb, int64_t w_off, int64_t N, int64_t K, int chunks,
+                                  int64_t* rows, int rows_cap, int64_t* out_bounds, int out_cap, int* out_nb) {
+  if (out_nb) *out_nb = 0;
+  if (!bounds || !rows || !out_bounds || !out_nb || nb < 0 || N <= 0 || K <= 0 || chunks < 2) return 0;
+  int64_t per = (N + chunks - 1) / chunks;
+  per = per >= 256 ? per / 256 * 256 : per / 32 * 32;
+  if (per <= 0) return 0;
+  int b = 0;
+  while (b < nb && bounds[2 * b] != w_off) b++;
+  if (b == nb) return 0;
+  int nr = 0;
+  for (int64_t r = 0; r < N; r += per) {
+    if (nr >= rows_cap) return 0;
+    rows[nr++] = r;
+  }
+  if (nr >= rows_cap) return 0;
+  rows[nr++] = N;
+  if (nr < 3) return 0;  // one chunk: nothing to split
+  const int total = nb - 1 + (nr - 1);
+  if (total > out_cap) return 0;
+  int k = 0;
+  for (int i = 0; i < b; i++, k++) out_bounds[2 * k] = bounds[2 * i], out_bounds[2 * k + 1] = bounds[2 * i + 1];
+  const int64_t end = bounds[2 * b + 1];
+  for (int j = nr - 2; j >= 0; j--, k++) {
+    out_bounds[2 * k] = w_off + rows[j] * K;
+    out_bounds[2 * k + 1] = j == nr - 2 ? end : w_off + rows[j + 1] * K;
+  }
+  for (int i = b + 1; i < nb; i++, k++) out_bounds[2 * k] = bounds[2 * i], out_bounds[2 * k + 1] = bounds[2 * i + 1];
+  *out_nb = k;
+  return nr;
 }

@@ -72,8 +72,9 @@ typedef struct {
 /* ---- context and errors -------------------------------------------------- */
 
 /* Opens device `device`: stream, memory pool, kernel attributes. Replaces
- * mps_init (internal/mps/mps.h:20-21) and the per-device factory registered
- * through tensor/device.go:166-195. */
+ * mps_init (internal/mps/mps.h:20-21) and the per-device factory that
+ * tensor/device.go registers (registerBackend, 68-72) and instantiates lazily
+ * (backendFor, 74-95). */
 GT_API char* gt_init(int device, gt_ctx** out);
 /* Frees every resource of the context (communicator, stream). */
 GT_API char* gt_destroy(gt_ctx* ctx);
@@ -98,6 +99,11 @@ GT_API char* gt_alloc(gt_ctx* ctx, size_t bytes, void** out);
 /* Returns a buffer to the pool, ordered after the work already queued;
  * mps_release (internal/mps/mps.h:28). */
 GT_API char* gt_release(gt_ctx* ctx, void* ptr);
+/* Bytes of the context's memory pool in use by live allocations and bytes the
+ * pool holds from the device (in use plus cached), as of the work queued so
+ * far; a diagnostic for callers that budget device memory. No counterpart in
+ * the reference. */
+GT_API char* gt_pool_usage(gt_ctx* ctx, uint64_t* used_bytes, uint64_t* reserved_bytes);
 /* mps_zero (internal/mps/mps.h:27); Backend.Zeros = gt_alloc + gt_zero. */
 GT_API char* gt_zero(gt_ctx* ctx, void* dst, size_t bytes);
 /* Host -> device copy; Backend.FromHost (mps_alloc_copy, mps.h:26). The host
@@ -276,7 +282,10 @@ GT_API char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, const i
  * which every GPU that loads the library keeps until the process exits.
  * Batches larger than GT_XENT_NOALLOC_MAX_ROWS are rejected with an error.
  * The first call on each device looks up that buffer's device address, so
- * make it before capturing the stream into a graph. All calls share the one
+ * make it before capturing the stream into a graph. The address is kept until
+ * the process exits; after a device reset (cudaDeviceReset, which reloads the
+ * library's device code) it is stale, so do not call this entry point again
+ * after resetting a device it was used on. All calls share the one
  * buffer: two calls that run on the GPU at the same time (different streams
  * or contexts on one device) race and corrupt each other's loss. */
 GT_API char* gt_xent_fwd_bwd_noalloc(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
@@ -399,6 +408,17 @@ GT_API void gt_debug_set_gemm_path(int path);
  * with S > 1 splits computes S partial products over consecutive K ranges and
  * sums them in order with its epilogue. Process-wide; for tests. */
 GT_API void gt_debug_set_gemm_splits(int splits);
+/* Every mbarrier wait of the tcgen05 GEMM gives up after this many
+ * microseconds (0: the default, 2 s), records the waiting site in an error
+ * word that the next gt_sync reports, and the kernel returns. Process-wide;
+ * for tests of that error path. */
+GT_API void gt_debug_set_tc_wait_limit_us(int64_t us);
+/* Arms a one-shot fault for the next tcgen05 GEMM launch: one splitter warp
+ * of each SM pair withholds its arrival for the first K-slice, so the MMA
+ * issuer's wait for that slice runs out. Every other wait then runs out too,
+ * the kernel frees its tensor memory and returns, and gt_sync reports the
+ * timed-out site; the context stays usable. For tests of the error path. */
+GT_API void gt_debug_tc_withhold_arrive(void);
 /* The path the most recent float32 GEMM took: 1 SIMT, 2 tcgen05 (0: none yet). */
 GT_API int gt_gemm_path_taken(void);
 

@@ -155,6 +155,20 @@ GT_API char* gth_dp_init(gth_model* m, int rank, int world, const unsigned char 
  * first; returns the bucket count, or -1 if cap is too small. Host only. */
 GT_API int gth_bucket_plan(const int64_t* sizes, int n, int64_t bucket_elems, int64_t* bounds, int cap);
 
+/* The row-chunk split of the bucket that starts at the first Linear's weight
+ * (element offset w_off, N rows of K elements), for a data-parallel step that
+ * computes that weight gradient in row chunks and averages each chunk while
+ * the next is computed (GT_DP_LAST_CHUNKS). bounds: nb (lo, hi) pairs from
+ * gth_bucket_plan. Writes the chunk row boundaries (0, ..., N; chunks of a
+ * multiple of 256 rows, or of 32 for small layers) to rows and the new bucket
+ * list to out_bounds (*out_nb pairs): the chunk buckets replace that bucket,
+ * highest rows first, and the first of them also holds the rest of the
+ * original bucket after the weight (the bias). Returns the number of row
+ * boundaries, or 0 when nothing is split (no such bucket, one chunk, or a
+ * capacity too small). No counterpart in the reference. Host only. */
+GT_API int gth_row_chunk_plan(const int64_t* bounds, int nb, int64_t w_off, int64_t N, int64_t K, int chunks,
+                              int64_t* rows, int rows_cap, int64_t* out_bounds, int out_cap, int* out_nb);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,7 +13,7 @@ The CNN is Conv2d(1,2,3,pad 1) -> ReLU -> MaxPool2d(2) -> Flatten ->
 Linear(32,3) on an input of shape [2,1,8,8]; parameter names follow the
 reference's Sequential naming (0.weight, 0.bias, 4.weight, 4.bias).
 
-Usage: python tests/golden/make_golden.py [reference_root]
+Usage: python tests/golden/make_golden.py <go-tensor checkout>
 """
 import json
 import os
@@ -58,4 +58,6 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <go-tensor checkout>")
+    main(sys.argv[1])

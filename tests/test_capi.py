@@ -6,7 +6,7 @@ import re
 import pytest
 
 from gotensor import _lib
-from gotensor.model import bucket_plan
+from gotensor.model import bucket_plan, row_chunk_plan
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -51,3 +51,41 @@ def test_bucket_plan_single_bucket_and_tiny_sizes():
     assert bucket_plan([10, 20, 30], 1 << 30) == [(0, 60)]
     assert bucket_plan([10, 20, 30], 1) == [(30, 60), (10, 30), (0, 10)]
     assert bucket_plan([], 5) == []
+
+
+def test_row_chunk_plan_splits_the_first_weight_bucket():
+    """GT_DP_LAST_CHUNKS: the bucket that starts at the first Linear's weight is
+    cut at row chunks; the chunk buckets tile it exactly, highest rows first,
+    and the first of them keeps the bias that follows the weight."""
+    # the data-parallel test model: Linear(256,512), Linear(512,512), Linear(512,100)
+    # (each tensor padded to 64 elements, as the runtime lays them out)
+    sizes = [512 * 256, 512, 512 * 512, 512, 100 * 512, 128]
+    buckets = bucket_plan(sizes, (256 << 10) // 4)
+    w_off, N, K = 0, 512, 256
+    rows, plan = row_chunk_plan(buckets, w_off, N, K, 4)
+    assert rows == [0, 128, 256, 384, 512]
+    first = [b for b in buckets if b[0] == w_off][0]
+    chunk_buckets = plan[len(buckets) - 1:]
+    assert plan[:len(buckets) - 1] == [b for b in buckets if b[0] != w_off]
+    assert chunk_buckets == [(w_off + 384 * K, first[1]), (w_off + 256 * K, w_off + 384 * K),
+                             (w_off + 128 * K, w_off + 256 * K), (w_off, w_off + 128 * K)]
+    assert first[1] > w_off + N * K  # the bias sits in the first chunk bucket issued
+    # contiguous and covering the buffer
+    assert plan[0][1] == sum(sizes) and plan[-1][0] == 0
+    for (lo, hi), (lo2, hi2) in zip(plan, plan[1:]):
+        assert hi2 == lo and lo < hi
+
+
+@pytest.mark.parametrize("N,chunks,want", [(4096, 4, [0, 1024, 2048, 3072, 4096]),
+                                           (4096, 3, [0, 1280, 2560, 3840, 4096]),
+                                           (100, 2, [0, 32, 64, 96, 100])])
+def test_row_chunk_plan_rounds_rows_to_tiles(N, chunks, want):
+    rows, plan = row_chunk_plan([(0, N * 8 + 64)], 0, N, 8, chunks)
+    assert rows == want
+    assert plan[0] == (want[-2] * 8, N * 8 + 64) and plan[-1] == (0, want[1] * 8)
+
+
+def test_row_chunk_plan_leaves_other_plans_alone():
+    assert row_chunk_plan([(0, 100)], 0, 64, 1, 1) == ([], [(0, 100)])      # one chunk
+    assert row_chunk_plan([(10, 100)], 0, 64, 1, 4) == ([], [(10, 100)])    # no bucket starts at the weight
+    assert row_chunk_plan([(0, 1000)], 0, 16, 8, 4) == ([], [(0, 1000)])   # fewer rows than one chunk

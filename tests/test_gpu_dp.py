@@ -61,10 +61,14 @@ def _wait(procs, timeout=240):
 
 
 @pytest.mark.skipif("_gpus() < 2", reason="needs two GPUs")
-def test_two_gpu_dp_matches_one_gpu(tmp_path):
+@pytest.mark.parametrize("extra_env", [{}, {"GT_DP_LAST_CHUNKS": "4"}], ids=["one_dw_gemm", "dw_in_row_chunks"])
+def test_two_gpu_dp_matches_one_gpu(tmp_path, extra_env):
+    """With GT_DP_LAST_CHUNKS=4 the first Linear's weight gradient (N = 512
+    rows) is computed in 4 chunks of 128 rows, each averaged while the next is
+    computed, and its bias rides in the first chunk's bucket."""
     _wait([_spawn("step", tmp_path, 0, 1, _free_port())])
     port = _free_port()
-    _wait([_spawn("step", tmp_path, r, 2, port) for r in range(2)])
+    _wait([_spawn("step", tmp_path, r, 2, port, extra_env) for r in range(2)])
     one = np.load(tmp_path / "rank0_of1.npz")
     r0, r1 = np.load(tmp_path / "rank0_of2.npz"), np.load(tmp_path / "rank1_of2.npz")
     # every rank holds the same averaged gradient and, after the steps, the same weights

@@ -197,3 +197,38 @@ def test_sm_reserve_leaves_results_unchanged():
             check(lib.gt_set_gemm_sm_reserve(be.ctx.ptr, 10_000))
     finally:
         check(lib.gt_set_gemm_sm_reserve(be.ctx.ptr, 0))
+
+
+def test_timed_out_wait_returns_an_error_and_the_context_recovers():
+    """The error path of the tcgen05 GEMM's bounded barrier waits. With the
+    wait limit lowered to 20 ms, one splitter warp per SM pair withholds its
+    arrival for the first K-slice (a barrier that nothing completes): the MMA
+    issuer's wait runs out, every other wait follows, the kernel frees its
+    tensor memory and returns. gt_sync reports the timed-out site, and the
+    next GEMM on the same context is correct. Nothing traps or hangs."""
+    import time
+
+    from gotensor._lib import GTError
+    lib = _lib.cuda_lib()
+    be = cuda_backend()
+    be.Sync()
+    rng = np.random.default_rng(9)
+    m = k = n = 512
+    a = rng.standard_normal(m * k).astype(np.float32)
+    b = rng.standard_normal(k * n).astype(np.float32)
+    ga, gb = be.FromHost(a), be.FromHost(b)
+    lib.gt_debug_set_tc_wait_limit_us(20000)
+    try:
+        lib.gt_debug_tc_withhold_arrive()
+        t0 = time.time()
+        be.MatMul(ga, gb, m, k, n, False, False)
+        with pytest.raises(GTError, match=r"pipeline wait timed out \(site \d\)"):
+            be.Sync()
+        assert time.time() - t0 < 10
+        be.Sync()  # the error was reported once and cleared
+    finally:
+        lib.gt_debug_set_tc_wait_limit_us(0)
+    got = be.ToHost(be.MatMul(ga, gb, m, k, n, False, False))
+    assert lib.gt_gemm_path_taken() == 2
+    want = cpu_backend().MatMul(T.CPUStorage(a), T.CPUStorage(b), m, k, n, False, False).data
+    assert_close(got, want, 1e-4, "GEMM after the timed-out one")

@@ -43,6 +43,15 @@ CONV_STACK_SMALL = [("Conv2d", (3, 16, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2
                     ("Flatten", ()), ("Linear", (512, 10))]
 FP64_MLP_SMALL = [("Linear", (256, 256)), ("Tanh", ()), ("Linear", (256, 256)), ("Sigmoid", ()),
                   ("Linear", (256, 10))]
+# The benchmark configs at their own layer widths.
+WIDE_C2_SPEC = [("Linear", (4096, 4096)), ("ReLU", ()), ("Linear", (4096, 4096)), ("ReLU", ()),
+                ("Linear", (4096, 1000))]
+CONV_STACK_C4 = [("Conv2d", (3, 64, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)), ("Conv2d", (64, 128, 3, 1, 1)),
+                 ("ReLU", ()), ("MaxPool2d", (2, 0)), ("Conv2d", (128, 256, 3, 1, 1)), ("ReLU", ()),
+                 ("MaxPool2d", (2, 0)), ("Conv2d", (256, 512, 3, 1, 1)), ("ReLU", ()), ("MaxPool2d", (2, 0)),
+                 ("Flatten", ()), ("Linear", (2048, 10))]
+FP64_MLP_C5 = [("Linear", (1024, 1024)), ("Tanh", ()), ("Linear", (1024, 1024)), ("Sigmoid", ()),
+               ("Linear", (1024, 10))]
 
 CASES = {
     # name: (spec, input shape, classes, dtype, optimizer, x distribution)
@@ -52,6 +61,17 @@ CASES = {
     "conv_stack32_b8_adam": (CONV_STACK_SMALL, [8, 3, 32, 32], 10, T.Float32, "adam", "normal"),
     "fp64_mlp_small_adam": (FP64_MLP_SMALL, [128, 256], 10, T.Float64, "adam", "uniform11"),
 }
+# Full size: the small CNN and the float64 MLP exactly as benchmarked; the
+# wide MLP and the conv stack at full widths with the batch each of 8
+# data-parallel ranks computes (1024 rows; 128 images, so every conv's weight
+# gradient runs over K = 128 * OH * OW positions, 131,072 for the first).
+FULL_CASES = {
+    "cnn28_b256_adam": (CNN_C3, [256, 1, 28, 28], 10, T.Float32, "adam", "uniform01"),
+    "fp64_mlp1024_b4096_adam": (FP64_MLP_C5, [4096, 1024], 10, T.Float64, "adam", "uniform11"),
+    "wide_mlp4096_b1024_sgd": (WIDE_C2_SPEC, [1024, 4096], 1000, T.Float32, "sgd", "normal"),
+    "conv_stack_c64_512_b128_adam": (CONV_STACK_C4, [128, 3, 32, 32], 10, T.Float32, "adam", "normal"),
+}
+CASES.update(FULL_CASES)
 
 
 def make_case(name, seed):
@@ -99,19 +119,31 @@ def test_step_loss_grads_and_update(name):
         assert_close(g[k].reshape(-1), want, tol, f"grad {k}")
     # the update: with the same gradients the optimizer is bit-exact (see
     # test_gpu_fused); here the gradients differ by rounding, so compare at
-    # the tolerance, exempting Adam's first-step sign flips of gradients that
-    # are zero up to rounding (|g| below the float32 noise of its GEMM).
+    # the tolerance
     ropt.Step()
     model.optimizer_step()
     after = model.state_dict()
     for k, p in nn.NamedParameters(ref):
-        want = p.Float64s()
-        got = after[k].reshape(-1).astype(np.float64)
-        ok = np.abs(got - want) <= tol * np.maximum(1, np.abs(want))
-        if isinstance(ropt, optim.Adam):
-            noise = np.abs(ref_grads[k]) <= 1e-6 * max(1.0, np.abs(ref_grads[k]).max())
-            ok |= noise & (np.abs(got - want) <= 2.0 * ropt.cfg.LR + tol)
-        assert ok.all(), f"param {k}: {int((~ok).sum())} of {ok.size} differ"
+        check_update(k, after[k].reshape(-1).astype(np.float64), p.Float64s(), g[k].reshape(-1), ref_grads[k],
+                     ropt, tol)
+
+
+def check_update(name, got, want, g_dev, g_ref, ropt, tol):
+    """Post-step weights within tol, except where Adam's first step cannot be
+    reproduced from gradients that agree only to rounding: Adam's first update
+    is lr * g / (|g| + eps), nearly lr * sign(g), so a gradient that is zero up
+    to the rounding of its GEMM (the device's and the reference's values then
+    differ by more than 1 % of |g| + eps, although both pass the gradient
+    check) can move a weight by anything up to 2 lr. Only such elements are
+    exempt, at most 2 lr + tol apart, and they must be rare."""
+    ok = np.abs(got - want) <= tol * np.maximum(1, np.abs(want))
+    if isinstance(ropt, optim.Adam):
+        g_dev = np.asarray(g_dev, np.float64)
+        noise = np.abs(g_dev - g_ref) > 0.01 * (np.abs(g_ref) + ropt.cfg.Eps)
+        exempt = ~ok & noise & (np.abs(got - want) <= 2.0 * ropt.cfg.LR + tol)
+        assert exempt.sum() <= max(2, 1e-3 * ok.size), f"param {name}: {int(exempt.sum())} noise-level gradients"
+        ok |= exempt
+    assert ok.all(), f"param {name}: {int((~ok).sum())} of {ok.size} differ"
 
 
 @pytest.mark.parametrize("name", ["cnn28_b32_adam", "mlp784_b64_adam"])

@@ -17,10 +17,16 @@ from gotensor.backend import CudaBackend
 pytestmark = pytest.mark.gpu
 
 
-def _run(be, fn, x_dev, labels_dev, B, C, dt):
-    loss = be.Zeros(dt, 1)
-    dl = be.Zeros(dt, B * C)
+def _pool_usage(be):
+    used, reserved = ctypes.c_uint64(), ctypes.c_uint64()
+    be.Sync()
+    check(_lib.cuda_lib().gt_pool_usage(be.ctx.ptr, ctypes.byref(used), ctypes.byref(reserved)))
+    return used.value, reserved.value
+
+
+def _run(be, fn, x_dev, labels_dev, B, C, dt, loss, dl):
     check(fn(be.ctx.ptr, dt, x_dev.ptr, labels_dev, B, C, loss.ptr, dl.ptr, None))
+    be.Sync()
     return be.ToHost(loss), be.ToHost(dl)
 
 
@@ -36,12 +42,18 @@ def test_noalloc_matches_pool_variant_on_consecutive_calls(dt, npdt):
         y = rng.integers(0, C, B).astype(np.int32)
         labels = be.ctx.alloc(4 * B)
         check(lib.gt_upload(be.ctx.ptr, labels, y.ctypes.data, 4 * B))
-        want_loss, want_dl = _run(be, lib.gt_xent_fwd_bwd, x, labels, B, C, dt)
-        got_loss, got_dl = _run(be, lib.gt_xent_fwd_bwd_noalloc, x, labels, B, C, dt)
-        tol = 1e-4 if dt == FLOAT32 else 1e-10
-        assert np.all(np.abs(got_loss - want_loss) <= tol * np.maximum(1, np.abs(want_loss)))
-        assert np.all(np.abs(got_dl - want_dl) <= tol * np.maximum(1, np.abs(want_dl)))
-        be.Sync()
+        loss, dl = be.Zeros(dt, 1), be.Zeros(dt, B * C)
+        want_loss, want_dl = _run(be, lib.gt_xent_fwd_bwd, x, labels, B, C, dt, loss, dl)
+        # the same two kernels on the same inputs: identical bits, and the
+        # pool neither hands out nor grows by a byte during the call
+        es = 4 if dt == FLOAT32 else 8
+        check(lib.gt_zero(be.ctx.ptr, loss.ptr, es))  # so a call that wrote nothing cannot pass
+        check(lib.gt_zero(be.ctx.ptr, dl.ptr, es * B * C))
+        before = _pool_usage(be)
+        got_loss, got_dl = _run(be, lib.gt_xent_fwd_bwd_noalloc, x, labels, B, C, dt, loss, dl)
+        assert _pool_usage(be) == before
+        assert got_loss.tobytes() == want_loss.tobytes()
+        assert got_dl.tobytes() == want_dl.tobytes()
         be.ctx.release(labels)
 
 
