@@ -201,6 +201,37 @@ __global__ void maxpool2_bwd_idx_kernel(const T* __restrict__ grad, const uint8_
   }
 }
 
+// The weight operand of an implicit-GEMM convolution, split into its tf32
+// planes once per call (the splitter warps would otherwise split the same
+// weight slice again for every tile): ws rows [0, rows) = tf32(v) and rows
+// [rows_pad, rows_pad + rows) = tf32(v - tf32(v)), rows of `pitch` elements
+// (a multiple of 4, for the TMA copy), zero elsewhere. v is row r, column j
+// of the GEMM's B operand:
+//   forward (flip = 0): w viewed as (O, C*KH*KW), rows = O, cols = C*KH*KW;
+//   input gradient (flip = 1): the weight of the forward convolution of dy
+//     that gives dx (stride 1): row c, column (o, kh, kw) =
+//     w[o][c][KH-1-kh][KW-1-kw], rows = C, cols = O*KH*KW.
+__global__ void split_weight_kernel(const float* __restrict__ w, float* __restrict__ ws, int rows, int cols,
+                                    int pitch, int rows_pad, int flip, int O, int C, int KH, int KW) {
+  const int KHW = KH * KW;
+  const int64_t plane = (int64_t)rows_pad * pitch;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < plane; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / pitch), j = (int)(i - (int64_t)r * pitch);
+    float v = 0.0f;
+    if (r < rows && j < cols) {
+      if (flip) {
+        const int o = j / KHW, rem = j - o * KHW, kh = rem / KW, kw = rem - kh * KW;
+        v = w[((int64_t)(o * C + r) * KH + (KH - 1 - kh)) * KW + (KW - 1 - kw)];
+      } else {
+        v = w[(int64_t)r * cols + j];
+      }
+    }
+    const float h = tf32_round(v);
+    ws[i] = h;
+    ws[plane + i] = tf32_round(__fsub_rn(v, h));
+  }
+}
+
 static bool pool2_tiles(const gt_geom* g) {
   return g->KH == 2 && g->KW == 2 && g->stride == 2 && g->pad == 0 && g->H == 2 * g->OH && g->W == 2 * g->OW;
 }
@@ -396,8 +427,50 @@ char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t
   return nullptr;
 }
 
-// Conv2d forward: cols = im2col(x) (scratch), then C (O, N*L) = W (O, CKK) @
-// cols^T stored straight into NCHW with the bias and activation fused.
+// The implicit-GEMM forward (float32, tcgen05): no columns in memory. The
+// weight is first split into its tf32 planes (split_weight_kernel). *done is
+// false if the geometry does not qualify.
+static char* conv_implicit(gt_ctx* ctx, const float* x, const float* w, int flip, int64_t rows, int64_t cols,
+                           const float* bias, float* y, const gt_geom& g, int act, int64_t O_w, int64_t C_w,
+                           bool* done) {
+  *done = false;
+  if ((act != GT_ACT_NONE && act != GT_ACT_RELU) || g.stride != 1) return nullptr;
+  const int64_t pitch = (cols + 3) / 4 * 4, rows_pad = conv_weight_rows(rows);
+  if (2 * rows_pad * pitch >= INT32_MAX / 2) return nullptr;
+  void* ws = nullptr;
+  GT_TRY(scratch(ctx, (size_t)(2 * rows_pad * pitch) * sizeof(float), &ws));
+  split_weight_kernel<<<grid_for(ctx, rows_pad * pitch, 256), 256, 0, ctx->stream>>>(
+      w, (float*)ws, (int)rows, (int)cols, (int)pitch, (int)rows_pad, flip, (int)O_w, (int)C_w, (int)g.KH,
+      (int)g.KW);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  char* err = e != cudaSuccess ? cuda_error(e, "split_weight_kernel launch", __FILE__, __LINE__)
+                               : conv_fwd_gemm(ctx, x, (const float*)ws, pitch, bias, y, g, rows, act, done);
+  release(ctx, ws);
+  return err;
+}
+
+static char* conv_fwd_implicit(gt_ctx* ctx, const float* x, const float* w, const float* bias, float* y,
+                               const gt_geom& g, int64_t O, int act, bool* done) {
+  return conv_implicit(ctx, x, w, 0, O, g.C * g.KH * g.KW, bias, y, g, act, O, g.C, done);
+}
+
+// The implicit-GEMM input gradient of a stride-1 convolution with a square
+// window: dx = conv2d(dy, flip(w)^T) with padding KH-1-pad (dy plays the
+// input, C the output channels).
+static char* conv_dgrad_implicit(gt_ctx* ctx, const float* dy, const float* w, float* dx, const gt_geom& g,
+                                 int64_t O, bool* done) {
+  *done = false;
+  if (g.stride != 1 || g.KH != g.KW || g.pad > g.KH - 1) return nullptr;
+  gt_geom gd = g;
+  gd.C = O, gd.H = g.OH, gd.W = g.OW, gd.OH = g.H, gd.OW = g.W, gd.pad = g.KH - 1 - g.pad;
+  return conv_implicit(ctx, dy, w, 1, g.C, O * g.KH * g.KW, nullptr, dx, gd, GT_ACT_NONE, O, g.C, done);
+}
+
+// Conv2d forward. float32 runs as an implicit GEMM on the tensor cores
+// (conv_fwd_implicit); otherwise cols = im2col(x) (scratch), then C (O, N*L)
+// = W (O, CKK) @ cols^T stored straight into NCHW with the bias and
+// activation fused.
 char* gt_conv_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* y, const gt_geom* g,
                   int64_t O, int act) {
   GT_ENTER(ctx);
@@ -406,6 +479,11 @@ char* gt_conv_fwd(gt_ctx* ctx, int dtype, const void* x, const void* w, const vo
   if (O <= 0) return errorf("gt_conv_fwd: out_channels must be positive");
   const int64_t L = g->OH * g->OW, NL = g->N * L, CKK = g->C * g->KH * g->KW;
   if (NL == 0) return nullptr;
+  if (dtype == GT_FLOAT32) {
+    bool done = false;
+    GT_TRY(conv_fwd_implicit(ctx, (const float*)x, (const float*)w, (const float*)bias, (float*)y, *g, O, act, &done));
+    if (done) return nullptr;
+  }
   const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
   void* cols = nullptr;
   GT_TRY(scratch(ctx, (size_t)(NL * CKK) * es, &cols));
@@ -463,6 +541,11 @@ char* gt_conv_bwd_weight(gt_ctx* ctx, int dtype, const void* x, const void* dy, 
     if (db) GT_CUDA(cudaMemsetAsync(db, 0, O * es, ctx->stream));
     return nullptr;
   }
+  if (dtype == GT_FLOAT32) {  // implicit GEMM: no columns, dy read in place, db as one more row
+    bool done = false;
+    GT_TRY(conv_wgrad_gemm(ctx, (const float*)x, (const float*)dy, (float*)dw, (float*)db, *g, O, &done));
+    if (done) return nullptr;
+  }
   void *cols = nullptr, *dyp = nullptr;
   GT_TRY(scratch(ctx, (size_t)(NL * CKK) * es, &cols));
   char* err = scratch(ctx, (size_t)(O * NL) * es, &dyp);
@@ -491,7 +574,15 @@ char* gt_conv_bwd_data(gt_ctx* ctx, int dtype, const void* dy, const void* w, vo
   if (O <= 0) return errorf("gt_conv_bwd_data: out_channels must be positive");
   const int64_t L = g->OH * g->OW, NL = g->N * L, CKK = g->C * g->KH * g->KW;
   const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
-  if (NL == 0) return nullptr;
+  if (NL == 0) {  // no output positions: nothing reaches the input
+    GT_CUDA(cudaMemsetAsync(dx, 0, g->N * g->C * g->H * g->W * es, ctx->stream));
+    return nullptr;
+  }
+  if (dtype == GT_FLOAT32) {  // implicit GEMM: no dcols, no col2im
+    bool done = false;
+    GT_TRY(conv_dgrad_implicit(ctx, (const float*)dy, (const float*)w, (float*)dx, *g, O, &done));
+    if (done) return nullptr;
+  }
   void *dcols = nullptr, *dyp = nullptr;
   GT_TRY(scratch(ctx, (size_t)(NL * CKK) * es, &dcols));
   char* err = scratch(ctx, (size_t)(O * NL) * es, &dyp);

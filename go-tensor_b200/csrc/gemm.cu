@@ -30,15 +30,18 @@ namespace gt {
 
 // Brackets one GEMM with the context's timer events (when a timer is on and
 // the stream is not being captured into a graph).
+// With `done`, a call that ends with *done false launched nothing and leaves
+// no record.
 template <typename F>
-static char* timed_gemm(gt_ctx* ctx, const GemmShape& s, F&& run) {
+static char* timed_gemm(gt_ctx* ctx, const GemmShape& s, F&& run, const bool* done = nullptr) {
   gt_gemm_timer* t = ctx->gemm_timer;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (t) GT_CUDA(cudaStreamIsCapturing(ctx->stream, &cap));
   if (!t || cap != cudaStreamCaptureStatusNone) return run();
   if (t->used >= (int64_t)t->launches.size()) {
-    t->dropped++;
-    return run();
+    char* err = run();
+    if (!done || *done) t->dropped++;
+    return err;
   }
   auto& l = t->launches[t->used++];
   l.m = s.M, l.n = s.N, l.k = s.K;
@@ -46,10 +49,44 @@ static char* timed_gemm(gt_ctx* ctx, const GemmShape& s, F&& run) {
   char* err = run();
   l.path = g_gemm_taken;
   GT_CUDA(cudaEventRecord(l.end, ctx->stream));
+  if (done && !*done) t->used--;
   return err;
 }
 
 static char* gemm_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi);
+
+// The implicit-GEMM convolutions, timed like any GEMM (path 4). The timer
+// records the convolution's own GEMM shape (M = positions or patch entries
+// without the bias-gradient row), so its flops are the algorithmic ones.
+char* conv_fwd_gemm(gt_ctx* ctx, const float* x, const float* w, int64_t w_pitch, const float* bias, float* y,
+                    const gt_geom& g, int64_t O, int act, bool* done) {
+  *done = false;
+  if (g_gemm_path == 1) return nullptr;  // SIMT pinned: the explicit path
+  GemmShape ts{g.N * g.OH * g.OW, O, g.C * g.KH * g.KW, false, true, 0, 0};
+  return timed_gemm(
+      ctx, ts,
+      [&] {
+        char* e = conv_fwd_tc(ctx, x, w, w_pitch, bias, y, g, O, act, done);
+        if (*done) g_gemm_taken = 4;
+        return e;
+      },
+      done);
+}
+
+char* conv_wgrad_gemm(gt_ctx* ctx, const float* x, const float* dy, float* dw, float* db, const gt_geom& g,
+                      int64_t O, bool* done) {
+  *done = false;
+  if (g_gemm_path == 1) return nullptr;
+  GemmShape ts{O, g.C * g.KH * g.KW, g.N * g.OH * g.OW, true, false, 0, 0};
+  return timed_gemm(
+      ctx, ts,
+      [&] {
+        char* e = conv_wgrad_tc(ctx, x, dy, dw, db, g, O, done);
+        if (*done) g_gemm_taken = 4;
+        return e;
+      },
+      done);
+}
 
 template <>
 char* gemm<double>(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {

@@ -35,6 +35,17 @@ struct Epi {
   uint32_t* bits_out = nullptr;
   const uint32_t* dbits = nullptr;
   int64_t ldw = 0;
+  // pos_major (with nchw_L > 0) swaps the roles in the NCHW store: m is the
+  // position (image m / L, offset m % L) and n the channel, nchw_M channels:
+  // out[((m / L) * nchw_M + n) * L + m % L] (an implicit-GEMM convolution,
+  // positions on M).
+  bool pos_major = false;
+  // col_major stores C transposed, out[n * ldc + m]; row rowsum_m of C goes to
+  // rowsum_out[n] instead (a weight gradient whose extra row of ones in A
+  // makes that row the bias gradient).
+  bool col_major = false;
+  T* rowsum_out = nullptr;
+  int64_t rowsum_m = -1;
 
   // The finished value of C(m, n): bias, activation, activation derivative.
   __device__ __forceinline__ T finish(int64_t m, int64_t n, T acc) const {
@@ -48,9 +59,18 @@ struct Epi {
 
   __device__ __forceinline__ void store(int64_t m, int64_t n, T acc) const { put(m, n, finish(m, n, acc)); }
 
-  // Writes the finished value of C(m, n) (row-major or the NCHW order).
+  // Writes the finished value of C(m, n) (row-major, transposed or an NCHW order).
   __device__ __forceinline__ void put(int64_t m, int64_t n, T v) const {
-    if (nchw_L > 0) {
+    if (col_major) {
+      if (m == rowsum_m) {
+        if (rowsum_out) rowsum_out[n] = v;
+      } else {
+        out[n * ldc + m] = v;
+      }
+    } else if (nchw_L > 0 && pos_major) {
+      int64_t img = m / nchw_L;
+      out[(img * nchw_M + n) * nchw_L + (m - img * nchw_L)] = v;
+    } else if (nchw_L > 0) {
       int64_t img = n / nchw_L;
       out[(img * nchw_M + m) * nchw_L + (n - img * nchw_L)] = v;
     } else {
@@ -58,6 +78,24 @@ struct Epi {
     }
   }
 };
+
+// Rounds to the nearest tf32 value (ties away from zero) on the integer ALU:
+// add half a tf32 ulp to the magnitude bits, clear the 13 dropped bits. The
+// 3xTF32 operands are x = hi + lo with hi = tf32(x), lo = tf32(x - hi).
+// Infinities stay infinities; a NaN stays NaN or becomes an infinity whose lo
+// part is NaN, so a product with it is NaN either way.
+__device__ __forceinline__ float tf32_round(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// Output-channel tile width of an implicit-GEMM convolution with `cols`
+// output channels (the narrowest of 64, 128, 256 that holds them), and the
+// row count its pre-split weight planes are padded to.
+inline int64_t conv_tile_width(int64_t cols) { return cols <= 64 ? 64 : cols <= 128 ? 128 : 256; }
+inline int64_t conv_weight_rows(int64_t cols) {
+  const int64_t t = conv_tile_width(cols);
+  return (cols + t - 1) / t * t;
+}
 
 struct GemmShape {
   int64_t M, N, K;
@@ -73,6 +111,28 @@ char* gemm_simt(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const E
 // when the shape or alignment does not qualify (the caller falls back).
 char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,
                   bool* done);
+
+// Implicit-GEMM convolutions on the tcgen05 path (float32), with no im2col
+// columns in memory. Both return nullptr with *done = false when the geometry
+// does not qualify (the caller then uses the explicit path).
+//   conv_fwd_tc: y (N, O, OH, OW) = act(conv2d(x, w) + bias) (stride 1); the
+//     weight comes pre-split into tf32 planes: ws rows [0, O) = tf32(w) and
+//     rows [wrows, wrows + O) = tf32(w - tf32(w)), wrows =
+//     conv_weight_rows(O), every row of w_pitch elements (a multiple of 4,
+//     16-byte aligned base), padding rows and columns zero; act is none or
+//     ReLU.
+//   conv_wgrad_tc: dw (O, C*KH*KW) and db (O, or NULL) from x and dy
+//     (N, O, OH, OW); needs OH * OW % 16 == 0.
+char* conv_fwd_tc(gt_ctx* ctx, const float* x, const float* ws, int64_t w_pitch, const float* bias, float* y,
+                  const gt_geom& g, int64_t O, int act, bool* done);
+char* conv_wgrad_tc(gt_ctx* ctx, const float* x, const float* dy, float* dw, float* db, const gt_geom& g, int64_t O,
+                    bool* done);
+
+// The same through the GEMM launch timer (gemm.cu); the conv entry points call these.
+char* conv_fwd_gemm(gt_ctx* ctx, const float* x, const float* w, int64_t w_pitch, const float* bias, float* y,
+                    const gt_geom& g, int64_t O, int act, bool* done);
+char* conv_wgrad_gemm(gt_ctx* ctx, const float* x, const float* dy, float* dw, float* db, const gt_geom& g,
+                      int64_t O, bool* done);
 
 // Dispatches to the fastest qualifying path.
 template <typename T>

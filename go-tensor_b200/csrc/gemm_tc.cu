@@ -35,6 +35,19 @@
 // the next tile's first two groups. The register split (setmaxnreg) gives
 // warps 0-7 64 registers each and the promoters 192.
 //
+// Implicit-GEMM convolution. The same pipeline runs a convolution without
+// materialising its im2col columns: the splitter warps, which rewrite every
+// staged tile anyway, instead read the im2col values of the A operand
+// straight from the NCHW tensor (x, or dy for the input gradient) and write
+// them, split, into the swizzled shared-memory layout the MMA reads. Two
+// orientations: positions on M with the input channels' patches on K (the
+// forward pass, and the input gradient as the forward convolution of dy with
+// the flipped, transposed weight), and patches on M with positions on K (the
+// weight gradient, whose B operand, dy itself, comes by a 3-D TMA copy over
+// (positions, channels, images), and whose A operand has an extra row of
+// ones so that the bias gradient is one more row of the product). The tile
+// width BN (64, 128 or 256 columns) fits the channel count on N.
+//
 // Every barrier wait is bounded in time; on expiry the kernel records the
 // waiting site in an error word (reported by gt_sync), stops its loops,
 // waits (bounded) for its copies and MMAs in flight, frees its tensor memory
@@ -54,25 +67,46 @@ __device__ int g_tc_error = 0;
 namespace tc {
 
 constexpr int BM = 128;    // A rows per CTA (a pair covers 256)
-constexpr int BN = 256;    // C columns per tile
-constexpr int BNH = 128;   // B rows per CTA
 constexpr int BK = 16;     // K elements per slice
 constexpr int STAGES = 6;
+constexpr int MAX_STAGES = 6;
+// One splitter warp per ring slot: splitter w takes slices w, w + 6, ...,
+// all of which land in slot w, so its waits on that slot's barrier come in
+// phase order. (A barrier's parity wait cannot tell a phase from the one two
+// phases later, so two warps sharing a slot could wake on stale data.)
+constexpr int SPLITTERS = STAGES;
 constexpr int GROUP = 16;  // K slices per promotion group
 constexpr int THREADS = 512;
-constexpr int SPLIT_WARP0 = 2;  // warps 2..2+STAGES-1 split; warp 2+j owns slot j
+constexpr int SPLIT_WARP0 = 2;  // warps 2..2+SPLITTERS-1 split
 constexpr int PROMOTERS = 256;
 constexpr uint32_t A_BYTES = BM * BK * 4;
-constexpr uint32_t B_BYTES = BNH * BK * 4;
-constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // A hi, A lo, B hi, B lo
-constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
 constexpr int PROMOTER_WARPS = PROMOTERS / 32;
 constexpr int EPI_LD = 33;  // padded row of the per-warp 32 x 32 transpose (conflict-free both ways)
-constexpr uint32_t EPI_OFFSET = BAR_OFFSET + 512;
 constexpr uint32_t EPI_BYTES = PROMOTER_WARPS * 32 * EPI_LD * 4;
-constexpr uint32_t SMEM_BYTES = EPI_OFFSET + EPI_BYTES + 1024;  // + slack for 1024-byte alignment
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t BUF_COLS = 256;  // one partial accumulator: 128 lanes x 256 fp32 columns
+
+// Layout of one instantiation for a tile of 256 x BN outputs (C columns BN;
+// each CTA holds BN / 2 rows of B per stage and 128 lanes x BN columns of
+// each of the two tensor-memory accumulators).
+template <int BN>
+struct Tile {
+  static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
+  static constexpr int BNH = BN / 2;  // B rows per CTA
+  static constexpr uint32_t B_BYTES = BNH * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // A hi, A lo, B hi, B lo
+  static constexpr int STAGES = tc::STAGES;
+  static constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr uint32_t EPI_OFFSET = BAR_OFFSET + 512;
+  static constexpr uint32_t SMEM_BYTES = EPI_OFFSET + EPI_BYTES + 1024;  // + slack for 1024-byte alignment
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two partial accumulators of BN columns
+  static constexpr int HC = BN / 2;               // columns per promoter warp
+  static constexpr int64_t TILE_ELEMS = 2 * BM * BN;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(STAGES <= MAX_STAGES && STAGES == SPLITTERS, "one splitter warp per slot");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+constexpr int BN = 256;  // the plain GEMMs' tile width
+constexpr int BNH = Tile<BN>::BNH;
+constexpr uint32_t BUF_COLS = 256;
 // Registers per thread after the split: warps 0-7 (TMA, MMA, splitters) and
 // warps 8-15 (promoters). The launch gives every thread 65536 / 512 = 128;
 // the split keeps the block's total: 256 * 64 + 256 * 192 = 256 * 128 * 2.
@@ -80,8 +114,46 @@ constexpr int REGS_LOW = 64, REGS_HIGH = 192;
 static_assert(256 * REGS_LOW + 256 * REGS_HIGH <= THREADS * 128, "register split exceeds the launch's registers");
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // default limit, 2 s; a healthy wait takes microseconds
 
-static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+// Where an operand comes from. A: TMA, or gathered by the splitter warps as
+// im2col values with positions on the rows (A_IM2COL_POS) or patch entries
+// on the rows (A_IM2COL_CK). B: a 2-D TMA copy, a 3-D one over (positions
+// per image, channels, images) whose K index is image * L + position, or two
+// 2-D copies of an operand already split into tf32 planes (B_SPLIT2: hi rows
+// from 0, lo rows from Gather::b_lo_row), which the splitters leave alone.
+enum ASrc : int { A_TMA = 0, A_IM2COL_POS = 1, A_IM2COL_CK = 2 };
+enum BSrc : int { B_TMA2 = 0, B_TMA3 = 1, B_SPLIT2 = 2 };
+
+// The im2col geometry of a gathered operand (stride 1): src (N, C, H, W) read
+// through KH x KW windows with the padding, L = OH * OW positions per image.
+// Column k of the patch matrix is (c, kh, kw) = (k / KHW, k % KHW / KW,
+// k % KW), as internal/cpu/linalg.go:122-146 lays it out. ones_row (the
+// A_IM2COL_CK orientation) is a row of ones (-1: none).
+//
+// Per K-slice the producer copies, with one 4-D TMA load over src's
+// (W, H, C, N) dimensions, the "halo" the slice needs into the stage's lo
+// plane: box_w columns from x0 (rounded down to a 16-byte boundary, so the
+// TMA's innermost coordinate stays aligned), box_h rows, box_c channels,
+// box_n images, zero outside the tensor (the convolution's padding). The
+// splitter warps build the slice's im2col tile from it in shared memory.
+//   A_IM2COL_POS: a CTA's 128 rows are 128 consecutive positions forming a
+//     rectangle: rows_pi (= bh * OW) positions of each of box_n images, bh
+//     output rows each. The halo holds the channels of the slice's 16 patch
+//     entries.
+//   A_IM2COL_CK: a slice's 16 positions form a rectangle of one image (r16
+//     rows of min(OW, 16) columns); the halo holds the channels of the CTA's
+//     128 patch-entry rows.
+// rp is the padding rounded up to a multiple of 4: the halo's column 0 is
+// input column (first output column) - rp. Every index fits 32 bits (the
+// host checks).
+struct Gather {
+  int C = 0, H = 0, W = 0, KH = 1, KW = 1, OW = 1, pad = 0;
+  int L = 1, KHW = 1, CKK = 0, ones_row = -1;
+  int rp = 0, box_w = 0, box_h = 0, box_c = 0, box_n = 1;
+  int bh = 1, rows_pi = 1;  // A_IM2COL_POS
+  int r16 = 1, w16 = 16;    // A_IM2COL_CK
+  uint32_t halo_bytes = 0;  // box_w * box_h * box_c * box_n * 4
+  int b_lo_row = 0;         // B_SPLIT2: first row of the lo plane
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -168,6 +240,23 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -198,8 +287,8 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
             : smem_desc(base + kk * 32, 16, 512, kLayoutSw64);
 }
 
-// Instruction descriptor for kind::tf32, fp32 accumulate, M = 256 (pair), N = 256.
-template <bool A_MN, bool B_MN>
+// Instruction descriptor for kind::tf32, fp32 accumulate, M = 256 (pair), N = TBN.
+template <bool A_MN, bool B_MN, int TBN>
 __device__ __forceinline__ uint32_t instr_desc() {
   uint32_t d = 0;
   d |= 1u << 4;                 // D format: F32
@@ -207,7 +296,7 @@ __device__ __forceinline__ uint32_t instr_desc() {
   d |= 2u << 10;                // B format: TF32
   d |= (A_MN ? 1u : 0u) << 15;  // A major
   d |= (B_MN ? 1u : 0u) << 16;  // B major
-  d |= (uint32_t)(BN >> 3) << 17;
+  d |= (uint32_t)(TBN >> 3) << 17;
   d |= (uint32_t)((2 * BM) >> 4) << 24;
   return d;
 }
@@ -261,16 +350,6 @@ __device__ __forceinline__ void tmem_store32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
-// Rounds to the nearest tf32 value (ties away from zero) on the integer ALU:
-// add half a tf32 ulp to the magnitude bits, clear the 13 dropped bits. (The
-// cvt instruction for this runs on the narrow XU pipe, which capped the
-// splitters at a third of the tensor rate.) Infinities stay infinities; a
-// NaN stays NaN or becomes an infinity whose lo part is NaN, so the product
-// is NaN either way.
-__device__ __forceinline__ float tf32_round(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-
 // One warp splits n16 float4s of a staged slice in place: x -> hi = tf32(x)
 // over x, lo = tf32(x - hi) into the lo plane. The tensor core reads an fp32
 // operand of kind::tf32 by dropping its low 13 bits (truncation), so both
@@ -288,6 +367,114 @@ __device__ __forceinline__ void split_tf32(float4* x, float4* lo, int n16, int l
   }
 }
 
+// Byte offset of element (r, k) of a K-major stage operand (128 rows of 16
+// fp32, 64-byte rows, the 64-byte swizzle the TMA writes and the MMA's
+// descriptor reads: the 16-byte chunk index XORed with address bits 7-8).
+__device__ __forceinline__ uint32_t kmajor_offset(int r, int chunk) {
+  return (uint32_t)r * 64u + ((uint32_t)(chunk ^ ((r >> 1) & 3)) << 4);
+}
+
+__device__ __forceinline__ void split_store4(uint8_t* hi, uint8_t* lo, uint32_t off, float a, float b, float c,
+                                             float d) {
+  float4 h, l;
+  h.x = tf32_round(a), h.y = tf32_round(b), h.z = tf32_round(c), h.w = tf32_round(d);
+  l.x = tf32_round(__fsub_rn(a, h.x)), l.y = tf32_round(__fsub_rn(b, h.y));
+  l.z = tf32_round(__fsub_rn(c, h.z)), l.w = tf32_round(__fsub_rn(d, h.w));
+  *(float4*)(hi + off) = h;
+  *(float4*)(lo + off) = l;
+}
+
+// A_IM2COL_POS: rows 0..rows-1 of this CTA's A block are output positions
+// (the block starts at a rectangle of the output), columns k0 .. k0+15 patch
+// entries (c, kh, kw). Lane l fills rows l, l+32, l+64, l+96, whose halo
+// offsets hb[] pos_rows() computes once per kernel (the block's layout in the
+// halo is the same for every tile). Each chunk of four entries of a row goes
+// to the hi plane as one 16-byte store of raw values (conflict-free under the
+// swizzle); the warp's halo reads are 32 consecutive positions. Entries past
+// C*KH*KW are zero; taps in the padding read the halo's zero fill
+// (internal/cpu/linalg.go:130-139).
+__device__ __forceinline__ void pos_rows(const Gather& g, int lane, int (&hb)[4]) {
+  const int plane = g.box_w * g.box_h;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int r = lane + 32 * i;
+    const int n = r / g.rows_pi, rem = r - n * g.rows_pi;
+    const int oh = rem / g.OW, ow = rem - oh * g.OW;
+    hb[i] = n * g.box_c * plane + oh * g.box_w + ow + g.rp - g.pad;
+  }
+}
+
+__device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, const float* halo, int rows, int k0,
+                                           int lane, const int (&hb)[4]) {
+  const int plane = g.box_w * g.box_h;
+  const int c_lo = k0 / g.KHW;
+  int c = 0;
+  const int rem = k0 - c_lo * g.KHW;
+  int kh = rem / g.KW, kw = rem - kh * g.KW;
+#pragma unroll 1
+  for (int c4 = 0; c4 < 4; c4++) {
+    float v[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const bool kin = k0 + 4 * c4 + kk < g.CKK;
+      const int koff = c * plane + kh * g.box_w + kw;
+#pragma unroll
+      for (int i = 0; i < 4; i++) v[i][kk] = kin ? halo[hb[i] + koff] : 0.0f;
+      if (++kw == g.KW) {
+        kw = 0;
+        if (++kh == g.KH) kh = 0, ++c;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int r = lane + 32 * i;
+      if (r < rows) *(float4*)(hi + kmajor_offset(r, c4)) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+    }
+  }
+}
+
+// A_IM2COL_CK: rows 0..rows-1 of this CTA's A block are patch entries
+// row0 + r = (c, kh, kw), columns the slice's 16 positions. Lane l fills rows
+// l, l+32, l+64, l+96: ck_rows() gives, once per tile, each row's offset in
+// the halo (channel relative to the block's first) and its kind (gathered,
+// zero past C*KH*KW, or the row of ones that makes that row of the product
+// the bias gradient). A row's 16 positions go out as four 16-byte stores.
+__device__ __forceinline__ void ck_rows(const Gather& g, int row0, int lane, int (&koff)[4], int (&kind)[4]) {
+  const int plane = g.box_w * g.box_h, c_lo = row0 / g.KHW;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int ck = row0 + lane + 32 * i;
+    const int c = ck / g.KHW, rem = ck - c * g.KHW, kh = rem / g.KW, kw = rem - kh * g.KW;
+    koff[i] = (c - c_lo) * plane + kh * g.box_w + kw + g.rp - g.pad;
+    kind[i] = ck < g.CKK ? 1 : ck == g.ones_row ? 2 : 0;
+  }
+}
+
+__device__ __forceinline__ void gather_ck(const Gather& g, uint8_t* hi, const float* halo, int rows, int lane,
+                                          const int (&koff)[4], const int (&kind)[4]) {
+#pragma unroll 1
+  for (int i = 0; i < 4; i++) {
+    const int r = lane + 32 * i;
+    if (r >= rows) break;
+    float v[16];
+    if (kind[i] == 1) {
+      int oh = 0, ow = 0;
+#pragma unroll
+      for (int p = 0; p < 16; p++) {
+        v[p] = halo[koff[i] + oh * g.box_w + ow];
+        if (++ow == g.w16) ow = 0, ++oh;
+      }
+    } else {
+      const float f = kind[i] == 2 ? 1.0f : 0.0f;
+#pragma unroll
+      for (int p = 0; p < 16; p++) v[p] = f;
+    }
+#pragma unroll
+    for (int c4 = 0; c4 < 4; c4++)
+      *(float4*)(hi + kmajor_offset(r, c4)) = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+  }
+}
+
 // Epilogue kinds: each kernel instantiation carries only the code of its
 // kind. The promoters' code shares the SM's instruction cache with the MMA
 // issuer and the splitters, and large unrolled epilogues measurably slowed
@@ -299,9 +486,18 @@ enum EpiKind : int {
   EK_CONV = 3,       // + bias[m] (optional), then ReLU (optional), stored in NCHW order: Conv2d forward
   EK_GENERIC = 4,    // anything else (tanh / sigmoid forward)
   EK_MASKBITS = 5,   // * Step from a ReLU bit mask: the dX of a Linear after a ReLU
+  EK_NCHW_POS = 6,   // + bias[n] (optional), ReLU (optional), m = position, n = channel, stored NCHW:
+                     // an implicit-GEMM convolution's forward pass or input gradient
+  EK_COLMAJOR = 7,   // stored transposed, with the bias-gradient row: a convolution's weight gradient
 };
 
 inline int epi_kind(const Epi<float>& e, int64_t n_cols) {
+  if (e.col_major) return !e.bias && e.act == GT_ACT_NONE && !e.dmask && !e.dbits && !e.bits_out ? EK_COLMAJOR : -2;
+  if (e.pos_major)
+    return e.nchw_L > 0 && !e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask &&
+                   !e.dbits && !e.bits_out
+               ? EK_NCHW_POS
+               : -2;
   const bool rowmajor = e.nchw_L == 0;
   if (e.bits_out)  // only this kind writes the bit mask
     return !e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask && !e.dbits && rowmajor
@@ -417,9 +613,9 @@ __device__ __forceinline__ int unit_of(int u, int tiles, const SplitPlan& sp, in
 }
 
 struct Shared {
-  uint64_t full[STAGES];   // TMA -> splitters (local)
-  uint64_t split[STAGES];  // splitters of both CTAs -> leader's MMA
-  uint64_t empty[STAGES];  // MMA -> producers of both CTAs
+  uint64_t full[MAX_STAGES];   // TMA -> splitters (local)
+  uint64_t split[MAX_STAGES];  // splitters of both CTAs -> leader's MMA
+  uint64_t empty[MAX_STAGES];  // MMA -> producers of both CTAs
   uint64_t pfull[2];       // MMA -> promoters of both CTAs: partial buffer b is complete
   uint64_t pempty[2];      // promoter warps of both CTAs -> leader's MMA: buffer b was read
   uint64_t mma_done;       // leader: every MMA issued has completed
@@ -427,13 +623,27 @@ struct Shared {
   int failed;
 };
 
-template <bool A_MN, bool B_MN, int EK>
+// Moves the promoters' 32-column chunk J of the running total into the warp's
+// transpose buffer (lane = row): the switch below keeps register indices
+// static in a loop that is not unrolled, so the block's code exists once.
+template <int J, int N>
+__device__ __forceinline__ void xpose_chunk(float* xpose, const float (&tot)[N], int lane) {
+  if constexpr (32 * J < N) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) xpose[lane * EPI_LD + i] = tot[32 * J + i];
+  }
+}
+
+template <bool A_MN, bool B_MN, int EK, int TBN, int AS, int BS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            GemmShape s, Epi<float> epi, SplitPlan sp) {
+                            GemmShape s, Epi<float> epi, SplitPlan sp, Gather ga) {
+  using TL = Tile<TBN>;
+  constexpr int HC = TL::HC;
+  constexpr int STAGES = TL::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  Shared* sh = (Shared*)(smem + BAR_OFFSET);
+  Shared* sh = (Shared*)(smem + TL::BAR_OFFSET);
   volatile int* failed = &sh->failed;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -441,7 +651,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const bool leader = rank == 0;
   const int num_k = (int)((s.K + BK - 1) / BK);
   const int m_tiles = (int)((s.M + 2 * BM - 1) / (2 * BM));
-  const int n_tiles = (int)((s.N + BN - 1) / BN);
+  const int n_tiles = (int)((s.N + TBN - 1) / TBN);
   const int tiles = m_tiles * n_tiles;
   const int units = sp.whole + (tiles - sp.whole) * sp.splits;
   const int pair = (int)cluster_id(), pairs = (int)num_clusters();
@@ -462,7 +672,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   }
   if (warp == 1) {  // both CTAs of the pair allocate together
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh->tmem_base)),
-                 "r"(TMEM_COLS));
+                 "r"(TL::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
   }
   tc_fence_before();
@@ -483,26 +693,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           unit_of(u, tiles, sp, num_k, t, kb, ke);
           const int mt = t / n_tiles, nt = t % n_tiles;
           const int a_row = mt * 2 * BM + (int)rank * BM;
-          const int b_row = nt * BN + (int)rank * BNH;
+          const int b_row = nt * TBN + (int)rank * TL::BNH;
           for (int kt = kb; kt < ke; kt++, it++) {
             const int st = it % STAGES;
             if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1, sp.wait_limit_ns)) {
               *failed = 1;
               break;
             }
-            uint8_t* a_hi = smem + st * STAGE_BYTES;
+            uint8_t* a_hi = smem + st * TL::STAGE_BYTES;
             uint8_t* b_hi = a_hi + 2 * A_BYTES;
-            mbar_expect_tx(&sh->full[st], A_BYTES + B_BYTES);
+            mbar_expect_tx(&sh->full[st],
+                           (AS == A_TMA ? A_BYTES : ga.halo_bytes) + (BS == B_SPLIT2 ? 2u : 1u) * TL::B_BYTES);
             const int k0 = kt * BK;
-            if (A_MN) {
-  #pragma unroll
-              for (int j = 0; j < BM / 32; j++) tma_load_2d(a_hi + j * kLboMN, &tmA, &sh->full[st], a_row + 32 * j, k0);
-            } else {
-              tma_load_2d(a_hi, &tmA, &sh->full[st], k0, a_row);
+            if constexpr (AS == A_IM2COL_POS) {  // the halo of this block's positions, the slice's channels
+              const int n0 = a_row / ga.L, oh0 = (a_row - n0 * ga.L) / ga.OW;
+              tma_load_4d(a_hi + A_BYTES, &tmA, &sh->full[st], -ga.rp, oh0 - ga.pad, k0 / ga.KHW, n0);
+            } else if constexpr (AS == A_IM2COL_CK) {  // the halo of the slice's positions, this block's channels
+              const int n = k0 / ga.L, l0 = k0 - n * ga.L, oh0 = l0 / ga.OW, ow0 = l0 - oh0 * ga.OW;
+              tma_load_4d(a_hi + A_BYTES, &tmA, &sh->full[st], ow0 - ga.rp, oh0 - ga.pad, a_row / ga.KHW, n);
             }
-            if (B_MN) {
-  #pragma unroll
-              for (int j = 0; j < BNH / 32; j++)
+            if constexpr (AS == A_TMA) {
+              if (A_MN) {
+#pragma unroll
+                for (int j = 0; j < BM / 32; j++)
+                  tma_load_2d(a_hi + j * kLboMN, &tmA, &sh->full[st], a_row + 32 * j, k0);
+              } else {
+                tma_load_2d(a_hi, &tmA, &sh->full[st], k0, a_row);
+              }
+            }
+            if constexpr (BS == B_TMA3) {  // K index = image * L + position
+              const int img = k0 / ga.L;
+              tma_load_3d(b_hi, &tmB, &sh->full[st], k0 - img * ga.L, b_row, img);
+            } else if constexpr (BS == B_SPLIT2) {  // both planes, already split
+              tma_load_2d(b_hi, &tmB, &sh->full[st], k0, b_row);
+              tma_load_2d(b_hi + TL::B_BYTES, &tmB, &sh->full[st], k0, ga.b_lo_row + b_row);
+            } else if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < TL::BNH / 32; j++)
                 tma_load_2d(b_hi + j * kLboMN, &tmB, &sh->full[st], b_row + 32 * j, k0);
             } else {
               tma_load_2d(b_hi, &tmB, &sh->full[st], k0, b_row);
@@ -517,7 +744,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
     } else if (warp == 1) {
       if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
-        const uint32_t idesc = instr_desc<A_MN, B_MN>();
+        const uint32_t idesc = instr_desc<A_MN, B_MN, TBN>();
         int it = 0, group = 0;
         bool stop = false;
         for (int u = pair; u < units && !stop; u += pairs) {
@@ -539,13 +766,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t a_hi = smem_u32(smem + st * STAGE_BYTES), a_lo = a_hi + A_BYTES;
-            const uint32_t b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
-  #pragma unroll
+            const uint32_t a_hi = smem_u32(smem + st * TL::STAGE_BYTES), a_lo = a_hi + A_BYTES;
+            const uint32_t b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + TL::B_BYTES;
+#pragma unroll
             for (int kk = 0; kk < BK / 8; kk++) {
               const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
               const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
-              const uint32_t d = tmem + buf * BUF_COLS;
+              const uint32_t d = tmem + buf * TBN;
               mma_tf32_pair(d, dal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
               mma_tf32_pair(d, dah, dbl, idesc, 1u);
               mma_tf32_pair(d, dah, dbh, idesc, 1u);
@@ -564,52 +791,81 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                      : "memory");
         mbar_wait(&sh->mma_done, 0, 6, kTimeoutNs);
       }
-    } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + STAGES) {
-      // ---- splitters (both CTAs): this warp owns ring slot st, i.e. every
-      // STAGES-th slice, starting with slice st.
-      const int st = warp - SPLIT_WARP0;
-      int total = 0;  // slices this pair streams
-      for (int u = pair; u < units; u += pairs) {
+    } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + SPLITTERS) {
+      // ---- splitters (both CTAs): splitter w takes every SPLITTERS-th slice,
+      // starting with slice w, whichever ring slot it lands in; a gathered A
+      // operand is built here from its halo.
+      const int sw = warp - SPLIT_WARP0;
+      int it = 0;
+      bool stop = false;
+      int rows4[4] = {0, 0, 0, 0}, kind4[4] = {0, 0, 0, 0};
+      if constexpr (AS == A_IM2COL_POS) pos_rows(ga, lane, rows4);
+      for (int u = pair; u < units && !stop; u += pairs) {
         int t, kb, ke;
         unit_of(u, tiles, sp, num_k, t, kb, ke);
-        total += ke - kb;
-      }
-      for (int it = st; it < total; it += STAGES) {
-        if (__shfl_sync(0xffffffffu, *failed, 0)) break;
-        if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4, sp.wait_limit_ns)) {
-          *failed = 1;
-          break;
+        const int a_row = (t / n_tiles) * 2 * BM + (int)rank * BM;
+        if constexpr (AS == A_IM2COL_CK) ck_rows(ga, a_row, lane, rows4, kind4);
+        for (int kt = kb; kt < ke; kt++, it++) {
+          if (it % SPLITTERS != sw) continue;
+          const int st = it % STAGES;
+          if (__shfl_sync(0xffffffffu, *failed, 0)) {
+            stop = true;
+            break;
+          }
+          uint8_t* stage = smem + st * TL::STAGE_BYTES;
+          // rows of this CTA's A block that the output uses
+          const int a_rows = (int)(s.M - a_row < BM ? (s.M - a_row > 0 ? s.M - a_row : 0) : BM);
+          if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4, sp.wait_limit_ns)) {
+            *failed = 1;
+            stop = true;
+            break;
+          }
+          if constexpr (AS == A_TMA) {
+            split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
+          } else {
+            // im2col tile from the halo in the lo plane into the hi plane,
+            // then split in place (the lo plane is overwritten only after
+            // every lane has read the halo). Rows past M are left as they
+            // are: they only reach rows of C that are never stored.
+            const float* halo = (const float*)(stage + A_BYTES);
+            if constexpr (AS == A_IM2COL_POS)
+              gather_pos(ga, stage, halo, a_rows, kt * BK, lane, rows4);
+            else
+              gather_ck(ga, stage, halo, a_rows, lane, rows4, kind4);
+            __syncwarp();
+            split_tf32((float4*)stage, (float4*)(stage + A_BYTES), a_rows * 64 / 16, lane);
+          }
+          if constexpr (BS != B_SPLIT2)
+            split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + TL::B_BYTES),
+                       TL::B_BYTES / 16, lane);
+          fence_async_shared();  // generic-proxy writes -> visible to the tensor core
+          if (!(sp.withhold_arrive && it == 0 && leader)) mbar_arrive_rank(&sh->split[st], 0);
         }
-        uint8_t* stage = smem + st * STAGE_BYTES;
-        split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
-        split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + B_BYTES), B_BYTES / 16, lane);
-        fence_async_shared();  // generic-proxy writes -> visible to the tensor core
-        if (!(sp.withhold_arrive && it == 0 && st == 0 && leader)) mbar_arrive_rank(&sh->split[st], 0);
       }
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_HIGH));
     // ---- promoters and epilogue (both CTAs): TMEM lanes 32*(warp%4)..+31 are
-    // this warp's rows, columns [128*h, 128*h + 128) its half of the tile.
+    // this warp's rows, columns [HC*h, HC*h + HC) its half of the tile.
     // Every decision below is warp-uniform: tcgen05.ld is .sync.aligned.
     const int q = warp & 3, h = (warp - 8) >> 2;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + 128 * h;
-    float* xpose = (float*)(smem + EPI_OFFSET) + (warp - 8) * 32 * EPI_LD;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + HC * h;
+    float* xpose = (float*)(smem + TL::EPI_OFFSET) + (warp - 8) * 32 * EPI_LD;
     int group = 0;
     for (int u = pair; u < units && !__shfl_sync(0xffffffffu, *failed, 0); u += pairs) {
       int t, kb, ke;
       const int sidx = unit_of(u, tiles, sp, num_k, t, kb, ke);
-      // a split unit's partial tile in the workspace (row-major 256 x 256)
+      // a split unit's partial tile in the workspace (row-major 256 x TBN)
       float* part = sidx < 0 ? nullptr
-                             : sp.ws + ((int64_t)sidx * (tiles - sp.whole) + (t - sp.whole)) * TILE_ELEMS +
-                                   (int64_t)(rank * BM + 32 * q) * BN + 128 * h + lane;
+                             : sp.ws + ((int64_t)sidx * (tiles - sp.whole) + (t - sp.whole)) * TL::TILE_ELEMS +
+                                   (int64_t)(rank * BM + 32 * q) * TBN + HC * h + lane;
       const int groups = (ke - kb + GROUP - 1) / GROUP;
       const int mt = t / n_tiles, nt = t % n_tiles;
       // The running total starts at +0 and every partial is added with
       // round-to-nearest, like the reference's c = 0; c += a*b.
-      float tot[128];
+      float tot[HC];
 #pragma unroll
-      for (int i = 0; i < 128; i++) tot[i] = 0.0f;
+      for (int i = 0; i < HC; i++) tot[i] = 0.0f;
       bool ok = true;
       for (int g = 0; g < groups; g++, group++) {
         const uint32_t buf = (uint32_t)(group & 1);
@@ -620,9 +876,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
+        for (int j = 0; j < HC / 32; j++) {
           float p[32];
-          tmem_load32(lane_base + buf * BUF_COLS + 32 * j, p);
+          tmem_load32(lane_base + buf * TBN + 32 * j, p);
 #pragma unroll
           for (int i = 0; i < 32; i++) tot[32 * j + i] = __fadd_rn(tot[32 * j + i], p[i]);
         }
@@ -631,29 +887,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (lane == 0) mbar_arrive_rank(&sh->pempty[buf], 0);  // the buffer may be overwritten
       }
       if (!ok) break;
-      // Epilogue: four 32 x 32 blocks through the transpose buffer (the
-      // switch keeps the register indices static in a loop that is not
-      // unrolled, so the block's code exists once).
       const int64_t m0 = (int64_t)mt * 2 * BM + rank * BM + 32 * q;
+      const int64_t n0 = (int64_t)nt * TBN + HC * h;
+      // The implicit-convolution layouts store each lane's own row (lane =
+      // row m): for a column, the warp writes 32 consecutive rows, which are
+      // 32 consecutive positions of a channel plane (NCHW) or of a transposed
+      // weight-gradient row.
+      const int64_t m_own = m0 + lane;
+      float* nchw_base = nullptr;
+      if constexpr (EK == EK_NCHW_POS) {
+        if (!part && m_own < s.M) {
+          const int64_t L = epi.nchw_L, img = m_own / L;
+          nchw_base = epi.out + img * epi.nchw_M * L + (m_own - img * L);
+        }
+      }
+      // Epilogue: 32 x 32 blocks through the per-warp buffer (the switch keeps
+      // the register indices static in a loop that is not unrolled).
 #pragma unroll 1
-      for (int j = 0; j < 4; j++) {
+      for (int j = 0; j < HC / 32; j++) {
         switch (j) {
-#define GT_XPOSE_CASE(J)                                                          \
-  case J:                                                                         \
-    _Pragma("unroll") for (int i = 0; i < 32; i++) xpose[lane * EPI_LD + i] = tot[32 * J + i]; \
-    break;
-          GT_XPOSE_CASE(0)
-          GT_XPOSE_CASE(1)
-          GT_XPOSE_CASE(2)
-          GT_XPOSE_CASE(3)
-#undef GT_XPOSE_CASE
+          case 0: xpose_chunk<0>(xpose, tot, lane); break;
+          case 1: xpose_chunk<1>(xpose, tot, lane); break;
+          case 2: xpose_chunk<2>(xpose, tot, lane); break;
+          case 3: xpose_chunk<3>(xpose, tot, lane); break;
         }
         __syncwarp();
-        if (!part) {
-          epilogue_block<EK>(epi, s, xpose, lane, m0, (int64_t)nt * BN + 128 * h + 32 * j + lane);
-        } else {
+        if (part) {
 #pragma unroll 4
-          for (int r = 0; r < 32; r++) part[r * BN + 32 * j] = xpose[r * EPI_LD + lane];
+          for (int r = 0; r < 32; r++) part[r * TBN + 32 * j] = xpose[r * EPI_LD + lane];
+        } else if constexpr (EK == EK_NCHW_POS) {
+          if (nchw_base) {
+            const int64_t L = epi.nchw_L;
+            const bool relu = epi.act == GT_ACT_RELU;
+#pragma unroll 4
+            for (int i = 0; i < 32; i++) {
+              const int64_t n = n0 + 32 * j + i;
+              if (n < s.N) {
+                float v = xpose[lane * EPI_LD + i];
+                if (epi.bias) v = __fadd_rn(v, __ldg(epi.bias + n));
+                if (relu) v = go_max(v, 0.0f);
+                nchw_base[n * L] = v;
+              }
+            }
+          }
+        } else if constexpr (EK == EK_COLMAJOR) {
+          if (m_own < s.M) {
+#pragma unroll 4
+            for (int i = 0; i < 32; i++) {
+              const int64_t n = n0 + 32 * j + i;
+              if (n < s.N) {
+                const float v = xpose[lane * EPI_LD + i];
+                if (m_own == epi.rowsum_m) {
+                  if (epi.rowsum_out) epi.rowsum_out[n] = v;
+                } else {
+                  epi.out[n * epi.ldc + m_own] = v;
+                }
+              }
+            }
+          }
+        } else {
+          epilogue_block<EK>(epi, s, xpose, lane, m0, n0 + 32 * j + lane);
         }
         __syncwarp();
       }
@@ -665,7 +958,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   __syncthreads();
   cluster_sync();  // no TMEM access remains anywhere in the pair
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TL::TMEM_COLS));
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -673,16 +967,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 // 2-D fp32 tensor map over `outer` rows of `inner` contiguous elements with a
-// pitch of `ld` elements; zero fill outside. K-major operands: box 16 x 128
-// with the 64-byte swizzle; M/N-major: box 32 x 16 with the 128-byte swizzle
-// of 32-byte atoms.
+// pitch of `ld` elements; zero fill outside. K-major operands: box 16 x
+// box_rows with the 64-byte swizzle; M/N-major: box 32 x 16 with the
+// 128-byte swizzle of 32-byte atoms.
 static char* make_map(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t inner, int64_t outer, int64_t ld,
-                      bool mn_major) {
+                      bool mn_major, int box_rows = BM) {
   auto encode = (EncodeTiledFn)ctx->encode_tiled;
   if (!encode) return errorf("gemm_tc: cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {mn_major ? 32u : (cuuint32_t)BK, mn_major ? (cuuint32_t)BK : (cuuint32_t)BM};
+  cuuint32_t box[2] = {mn_major ? 32u : (cuuint32_t)BK, mn_major ? (cuuint32_t)BK : (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -692,11 +986,70 @@ static char* make_map(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t 
   return nullptr;
 }
 
+// 3-D fp32 tensor map over an (images, channels, L) tensor (dy of a
+// convolution, NCHW with the plane flattened): dims {L, channels, images},
+// box {16 positions, box_rows channels, 1 image}, the K-major 64-byte swizzle.
+// A K-slice of 16 positions is one box when L % 16 == 0.
+static char* make_map3(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t L, int64_t chans, int64_t images,
+                       int box_rows) {
+  auto encode = (EncodeTiledFn)ctx->encode_tiled;
+  if (!encode) return errorf("gemm_tc: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)L, (cuuint64_t)chans, (cuuint64_t)images};
+  cuuint64_t strides[2] = {(cuuint64_t)L * 4, (cuuint64_t)(L * chans) * 4};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return errorf("gemm_tc: cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return nullptr;
+}
+
+// 4-D fp32 tensor map over an NCHW tensor, dims {W, H, C, N}, with the halo
+// box of a gathered operand (no swizzle: the splitters index it directly);
+// zero fill outside the tensor is the convolution's padding.
+static char* make_halo_map(gt_ctx* ctx, CUtensorMap* map, const float* base, const gt_geom& g, const Gather& ga) {
+  auto encode = (EncodeTiledFn)ctx->encode_tiled;
+  if (!encode) return errorf("gemm_tc: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[4] = {(cuuint64_t)g.W, (cuuint64_t)g.H, (cuuint64_t)g.C, (cuuint64_t)g.N};
+  cuuint64_t strides[3] = {(cuuint64_t)g.W * 4, (cuuint64_t)(g.H * g.W) * 4, (cuuint64_t)(g.C * g.H * g.W) * 4};
+  cuuint32_t box[4] = {(cuuint32_t)ga.box_w, (cuuint32_t)ga.box_h, (cuuint32_t)ga.box_c, (cuuint32_t)ga.box_n};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return errorf("gemm_tc: cuTensorMapEncodeTiled (halo) failed (%d)", (int)r);
+  return nullptr;
+}
+
 // SM pairs a GEMM may occupy: all of them, less the SMs reserved for kernels
 // that run beside it (a collective on another stream).
 static int64_t pairs_available(const gt_ctx* ctx) {
   const int64_t free_sms = (int64_t)ctx->sm_count - ctx->gemm_sm_reserve;
   return free_sms >= 2 ? free_sms / 2 : 1;
+}
+
+template <bool A_MN, bool B_MN, int EK, int TBN = BN, int AS = A_TMA, int BS = B_TMA2>
+static char* launch_kernel(gt_ctx* ctx, const GemmShape& s, const CUtensorMap& ta, const CUtensorMap& tb,
+                           const Epi<float>& epi, const SplitPlan& sp, const Gather& ga) {
+  auto kern = gemm_tf32x3_pair_kernel<A_MN, B_MN, EK, TBN, AS, BS>;
+  static bool configured[64] = {};
+  if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
+    GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<TBN>::SMEM_BYTES));
+    if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
+  }
+  const int64_t tiles = ceil_div(s.M, 2 * BM) * ceil_div(s.N, TBN);
+  const int64_t units = sp.whole + (tiles - sp.whole) * sp.splits;
+  const int64_t avail = pairs_available(ctx);
+  const int64_t pairs = units < avail ? units : avail;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Tile<TBN>::SMEM_BYTES;
+  cfg.stream = ctx->stream;
+  GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi, sp, ga));
+  GT_LAUNCH_CHECK();
+  return nullptr;
 }
 
 template <bool A_MN, bool B_MN, int EK>
@@ -711,24 +1064,7 @@ static char* launch(gt_ctx* ctx, const GemmShape& s, const float* A, const float
     GT_TRY(make_map(ctx, &tb, B, s.N, s.K, s.ldb, true));
   else
     GT_TRY(make_map(ctx, &tb, B, s.K, s.N, s.ldb, false));
-  auto kern = gemm_tf32x3_pair_kernel<A_MN, B_MN, EK>;
-  static bool configured[64] = {};
-  if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
-    GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
-  }
-  const int64_t tiles = ceil_div(s.M, 2 * BM) * ceil_div(s.N, BN);
-  const int64_t units = sp.whole + (tiles - sp.whole) * sp.splits;
-  const int64_t avail = pairs_available(ctx);
-  const int64_t pairs = units < avail ? units : avail;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
-  cfg.stream = ctx->stream;
-  GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi, sp));
-  GT_LAUNCH_CHECK();
-  return nullptr;
+  return launch_kernel<A_MN, B_MN, EK>(ctx, s, ta, tb, epi, sp, Gather{});
 }
 
 template <int EK>
@@ -749,26 +1085,31 @@ static char* launch_kind(gt_ctx* ctx, const GemmShape& s, const float* A, const 
                          bool a_mn, bool b_mn, const SplitPlan& sp) {
   switch (epi_kind(epi, s.N)) {
     case -1: return errorf("gemm_tc: a ReLU bit mask needs a row-major bias / ReLU epilogue");
+    case -2: return errorf("gemm_tc: a convolution layout with an unsupported epilogue");
     case EK_MASKBITS: return launch_layout<EK_MASKBITS>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_PLAIN: return launch_layout<EK_PLAIN>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_BIAS_RELU: return launch_layout<EK_BIAS_RELU>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_MASK: return launch_layout<EK_MASK>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_CONV: return launch_layout<EK_CONV>(ctx, s, A, B, epi, a_mn, b_mn, sp);
+    case EK_NCHW_POS:
+    case EK_COLMAJOR: return errorf("gemm_tc: the implicit convolution layouts have their own launchers");
     default: return launch_layout<EK_GENERIC>(ctx, s, A, B, epi, a_mn, b_mn, sp);
   }
 }
 
 // C of the split tiles = epilogue(sum of their partials), the partials added
 // in split order, so the result does not depend on which unit finished first.
+template <int TBN>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, SplitPlan sp, int tiles, int n_tiles, int64_t M,
                                      int64_t N, Epi<float> epi) {
+  constexpr int64_t TE = Tile<TBN>::TILE_ELEMS;
   const int rest = tiles - sp.whole;
-  const int64_t total = (int64_t)rest * TILE_ELEMS;
+  const int64_t total = (int64_t)rest * TE;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int r = (int)(i / TILE_ELEMS);
-    const int64_t e = i - (int64_t)r * TILE_ELEMS;
+    const int r = (int)(i / TE);
+    const int64_t e = i - (int64_t)r * TE;
     const int t = sp.whole + r;
-    const int64_t m = (int64_t)(t / n_tiles) * 2 * BM + e / BN, n = (int64_t)(t % n_tiles) * BN + e % BN;
+    const int64_t m = (int64_t)(t / n_tiles) * 2 * BM + e / TBN, n = (int64_t)(t % n_tiles) * TBN + e % TBN;
     if (m >= M || n >= N) continue;
     float acc = ws[i];
     for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
@@ -812,7 +1153,7 @@ static int g_force_splits = 0;
 static uint64_t g_wait_limit_ns = kTimeoutNs;  // gt_debug_set_tc_wait_limit_us
 static int g_withhold_next = 0;               // gt_debug_tc_withhold_arrive
 
-static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k) {
+static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k, int64_t tile_elems = TILE_ELEMS) {
   SplitPlan best;
   best.whole = (int)tiles;
   if (g_force_splits > 1) {
@@ -822,13 +1163,14 @@ static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k) {
   }
   constexpr double kUnitOverhead = 40.0;
   auto reduce_cost = [&](int64_t split_tiles, int S) {
+    // a slice's MMA time scales with the tile width; so does the partials' traffic
     return (S + 1) * (double)split_tiles * TILE_ELEMS * 4.0 / 5e6 / 0.54;
   };
   const double base = std::ceil((double)tiles / pairs) * (num_k + kUnitOverhead);
   double best_cost = base;
   for (int S = 2; S <= 64 && num_k / S >= 2 * GROUP; S++) {
     // every tile split (the workspace holds S partial tiles per tile: at most 1 GB)
-    double c = (double)S * tiles * TILE_ELEMS * 4 > (double)(1ull << 30)
+    double c = (double)S * tiles * tile_elems * 4 > (double)(1ull << 30)
                    ? INFINITY
                    : std::ceil((double)(tiles * S) / pairs) * (std::ceil((double)num_k / S) + kUnitOverhead) +
                          reduce_cost(tiles, S);
@@ -854,6 +1196,126 @@ static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k) {
     best.splits = 1;
   }
   return best;
+}
+
+// Runs a tcgen05 GEMM of `tiles` tiles (`n_tiles` per row of tiles) with the
+// split plan its shape calls for: fire(plan) launches the main kernel; split
+// units leave partial tiles in a pool workspace that a second kernel sums in
+// split order and finishes with the epilogue.
+template <int TBN, typename Fire>
+static char* run_planned(gt_ctx* ctx, const GemmShape& s, const Epi<float>& epi, int64_t tiles, int64_t n_tiles,
+                         Fire&& fire) {
+  constexpr int64_t TE = Tile<TBN>::TILE_ELEMS;
+  SplitPlan sp = choose_plan(tiles, pairs_available(ctx), ceil_div(s.K, BK), TE);
+  sp.wait_limit_ns = g_wait_limit_ns;
+  sp.withhold_arrive = g_withhold_next;
+  g_withhold_next = 0;
+  if (sp.splits <= 1) return fire(sp);
+  const int64_t rest = tiles - sp.whole;
+  void* ws = nullptr;
+  GT_TRY(scratch(ctx, (size_t)sp.splits * rest * TE * sizeof(float), &ws));
+  sp.ws = (float*)ws;
+  char* err = fire(sp);
+  if (!err) {
+    if (epi.bits_out)
+      splitk_reduce_bits_kernel<<<grid_for(ctx, rest * TE / 32, 256), 256, 0, ctx->stream>>>(
+          sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
+    else
+      splitk_reduce_kernel<TBN><<<grid_for(ctx, rest * TE, 256), 256, 0, ctx->stream>>>(sp.ws, sp, (int)tiles,
+                                                                                        (int)n_tiles, s.M, s.N, epi);
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) err = cuda_error(e, "splitk_reduce_kernel launch", __FILE__, __LINE__);
+  }
+  release(ctx, ws);
+  return err;
+}
+
+template <int TBN>
+static char* conv_fwd_launch(gt_ctx* ctx, const GemmShape& s, const CUtensorMap& ta, const CUtensorMap& tb,
+                             const Epi<float>& e, const Gather& ga) {
+  const int64_t n_tiles = ceil_div(s.N, TBN), tiles = ceil_div(s.M, 2 * BM) * n_tiles;
+  return run_planned<TBN>(ctx, s, e, tiles, n_tiles, [&](const SplitPlan& sp) {
+    return launch_kernel<false, false, EK_NCHW_POS, TBN, A_IM2COL_POS, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga);
+  });
+}
+
+template <int TBN>
+static char* conv_wgrad_launch(gt_ctx* ctx, const GemmShape& s, const CUtensorMap& ta, const CUtensorMap& tb,
+                               const Epi<float>& e, const Gather& ga) {
+  const int64_t n_tiles = ceil_div(s.N, TBN), tiles = ceil_div(s.M, 2 * BM) * n_tiles;
+  return run_planned<TBN>(ctx, s, e, tiles, n_tiles, [&](const SplitPlan& sp) {
+    return launch_kernel<false, false, EK_COLMAJOR, TBN, A_IM2COL_CK, B_TMA3>(ctx, s, ta, tb, e, sp, ga);
+  });
+}
+
+// The halo geometry shared by both orientations (stride 1 only); false if
+// the geometry does not fit the implicit path.
+static bool halo_common(const gt_geom& g, Gather& ga) {
+  if (g.stride != 1 || g.pad < 0 || g.pad > 64 || g.W % 4 || g.KH > 64 || g.KW > 64) return false;
+  ga.C = (int)g.C, ga.H = (int)g.H, ga.W = (int)g.W, ga.KH = (int)g.KH, ga.KW = (int)g.KW, ga.OW = (int)g.OW;
+  ga.pad = (int)g.pad, ga.L = (int)(g.OH * g.OW), ga.KHW = (int)(g.KH * g.KW), ga.CKK = (int)(g.C * g.KH * g.KW);
+  ga.rp = (ga.pad + 3) / 4 * 4;
+  return true;
+}
+
+// Most channels that `span` consecutive patch entries starting at a multiple
+// of `span` touch (the pattern repeats every lcm(span, KHW) entries).
+static int channels_spanned(int span, int khw, int C) {
+  int most = 1;
+  for (int k0 = 0; k0 < span * khw; k0 += span) most = std::max(most, (k0 + span - 1) / khw - k0 / khw + 1);
+  return std::min(most, C);
+}
+
+static bool halo_fits(Gather& ga) {
+  const int64_t floats = (int64_t)ga.box_w * ga.box_h * ga.box_c * ga.box_n;
+  if (ga.box_w > 256 || ga.box_h > 256 || ga.box_c > 256 || ga.box_n > 256 || floats * 4 > A_BYTES) return false;
+  ga.halo_bytes = (uint32_t)(floats * 4);
+  return true;
+}
+
+// A_IM2COL_POS: a CTA's 128 positions must form whole output rows of one
+// image (L % 128 == 0 and 128 % OW == 0) or whole images (128 % L == 0).
+static bool halo_pos(const gt_geom& g, Gather& ga) {
+  if (!halo_common(g, ga)) return false;
+  const int64_t L = g.OH * g.OW;
+  if (L % 128 == 0 && 128 % g.OW == 0) {
+    ga.bh = (int)(128 / g.OW), ga.box_n = 1;
+  } else if (L < 128 && 128 % L == 0) {
+    ga.bh = (int)g.OH, ga.box_n = (int)(128 / L);
+  } else {
+    return false;
+  }
+  ga.rows_pi = ga.bh * ga.OW;
+  ga.box_w = (int)((g.OW + g.KW - 1 + ga.rp - g.pad + 3) / 4 * 4);
+  ga.box_h = ga.bh + ga.KH - 1;
+  ga.box_c = channels_spanned(BK, ga.KHW, ga.C);
+  return halo_fits(ga);
+}
+
+// A_IM2COL_CK: a slice's 16 positions must form whole rows of 16 columns
+// (OW % 16 == 0) or whole rows of one image (16 % OW == 0, L % 16 == 0).
+static bool halo_ck(const gt_geom& g, Gather& ga) {
+  if (!halo_common(g, ga)) return false;
+  if (g.OW % 16 == 0) {
+    ga.w16 = 16, ga.r16 = 1;
+  } else if (16 % g.OW == 0 && (g.OH * g.OW) % 16 == 0) {
+    ga.w16 = (int)g.OW, ga.r16 = (int)(16 / g.OW);
+  } else {
+    return false;
+  }
+  ga.box_w = (ga.w16 + ga.KW - 1 + ga.rp - ga.pad + 3) / 4 * 4;
+  ga.box_h = ga.r16 + ga.KH - 1;
+  ga.box_c = channels_spanned(BM, ga.KHW, ga.C);
+  ga.box_n = 1;
+  return halo_fits(ga);
+}
+
+static bool fits32(const gt_geom& g, int64_t chans_out) {
+  const int64_t lim = INT32_MAX / 2;
+  return g.N * g.C * g.H * g.W < lim && g.N * g.OH * g.OW < lim && g.C * g.KH * g.KW < lim &&
+         g.N * chans_out * g.OH * g.OW < lim && g.H < lim / 4 && g.W < lim / 4 && g.stride < 65536 &&
+         g.pad < 65536 && g.KH < 65536 && g.KW < 65536;
 }
 
 }  // namespace tc
@@ -883,38 +1345,72 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
     return nullptr;
   if (ctx->sm_count < 2) return nullptr;
   if (gemm_path() != 2 && s.M * s.N * s.K < (int64_t)1 << 21) return nullptr;
+  if (epi.pos_major || epi.col_major) return nullptr;  // the implicit-convolution layouts have their own launchers
   const bool a_mn = s.trans_a, b_mn = !s.trans_b;
-  const int64_t tiles = ceil_div(s.M, 2 * tc::BM) * ceil_div(s.N, tc::BN);
-  const int64_t n_tiles = ceil_div(s.N, tc::BN);
-  tc::SplitPlan sp = tc::choose_plan(tiles, tc::pairs_available(ctx), ceil_div(s.K, tc::BK));
-  sp.wait_limit_ns = tc::g_wait_limit_ns;
-  sp.withhold_arrive = tc::g_withhold_next;
-  tc::g_withhold_next = 0;
-  char* err;
-  if (sp.splits > 1) {
-    const int64_t rest = tiles - sp.whole;
-    void* ws = nullptr;
-    GT_TRY(scratch(ctx, (size_t)sp.splits * rest * tc::TILE_ELEMS * sizeof(float), &ws));
-    sp.ws = (float*)ws;
-    // Whole tiles finish with their own epilogue; the split tiles' partials
-    // go to the workspace and are summed, in order, by the second kernel.
-    err = tc::launch_kind(ctx, s, A, B, epi, a_mn, b_mn, sp);
-    if (!err) {
-      if (epi.bits_out)
-        tc::splitk_reduce_bits_kernel<<<grid_for(ctx, rest * tc::TILE_ELEMS / 32, 256), 256, 0, ctx->stream>>>(
-            sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
-      else
-        tc::splitk_reduce_kernel<<<grid_for(ctx, rest * tc::TILE_ELEMS, 256), 256, 0, ctx->stream>>>(
-            sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
-      count_launch();
-      cudaError_t e = cudaGetLastError();
-      if (e != cudaSuccess) err = cuda_error(e, "splitk_reduce_kernel launch", __FILE__, __LINE__);
-    }
-    release(ctx, ws);
-    if (!err) *done = true;
-    return err;
-  }
-  err = tc::launch_kind(ctx, s, A, B, epi, a_mn, b_mn, sp);
+  const int64_t n_tiles = ceil_div(s.N, tc::BN), tiles = ceil_div(s.M, 2 * tc::BM) * n_tiles;
+  char* err = tc::run_planned<tc::BN>(ctx, s, epi, tiles, n_tiles, [&](const tc::SplitPlan& sp) {
+    return tc::launch_kind(ctx, s, A, B, epi, a_mn, b_mn, sp);
+  });
+  if (!err) *done = true;
+  return err;
+}
+
+char* conv_fwd_tc(gt_ctx* ctx, const float* x, const float* ws, int64_t w_pitch, const float* bias, float* y,
+                  const gt_geom& g, int64_t O, int act, bool* done) {
+  *done = false;
+  const int64_t L = g.OH * g.OW, P = g.N * L, CKK = g.C * g.KH * g.KW;
+  if (P < 1 || O < 1 || CKK < 1 || ctx->sm_count < 2 || !tc::fits32(g, O)) return nullptr;
+  if (((uintptr_t)ws & 15) || (w_pitch & 3) || w_pitch < CKK || (act != GT_ACT_NONE && act != GT_ACT_RELU))
+    return nullptr;
+  // C (P, O) = cols (P, CKK) @ w (O, CKK)^T: A gathered, B(k, n) = w[n * w_pitch + k].
+  GemmShape s{P, O, CKK, false, true, 0, w_pitch};
+  tc::Gather ga;
+  if (!tc::halo_pos(g, ga) || ((uintptr_t)x & 15)) return nullptr;
+  ga.b_lo_row = (int)conv_weight_rows(O);
+  Epi<float> e;
+  e.out = y;
+  e.bias = bias;
+  e.act = act;
+  e.nchw_L = L;
+  e.nchw_M = O;
+  e.pos_major = true;
+  const int tbn = (int)conv_tile_width(O);
+  CUtensorMap ta, tb;
+  GT_TRY(tc::make_halo_map(ctx, &ta, x, g, ga));
+  GT_TRY(tc::make_map(ctx, &tb, ws, CKK, 2 * ga.b_lo_row, w_pitch, false, tbn / 2));
+  char* err = tbn == 64    ? tc::conv_fwd_launch<64>(ctx, s, ta, tb, e, ga)
+              : tbn == 128 ? tc::conv_fwd_launch<128>(ctx, s, ta, tb, e, ga)
+                           : tc::conv_fwd_launch<256>(ctx, s, ta, tb, e, ga);
+  if (!err) *done = true;
+  return err;
+}
+
+char* conv_wgrad_tc(gt_ctx* ctx, const float* x, const float* dy, float* dw, float* db, const gt_geom& g, int64_t O,
+                    bool* done) {
+  *done = false;
+  const int64_t L = g.OH * g.OW, P = g.N * L, CKK = g.C * g.KH * g.KW;
+  if (P < 1 || O < 1 || CKK < 1 || ctx->sm_count < 2 || !tc::fits32(g, O)) return nullptr;
+  // A K-slice of 16 positions must lie in one image and start 16-byte aligned.
+  if (L % 16 || ((uintptr_t)dy & 15)) return nullptr;
+  // C (CKK [+1], O) = cols^T (CKK, P) @ dy (P, O); the extra row of ones in
+  // A makes row CKK of C the bias gradient.
+  GemmShape s{CKK + (db ? 1 : 0), O, P, true, false, 0, 0};
+  tc::Gather ga;
+  if (!tc::halo_ck(g, ga) || ((uintptr_t)x & 15)) return nullptr;
+  ga.ones_row = db ? (int)CKK : -1;
+  Epi<float> e;
+  e.out = dw;
+  e.ldc = CKK;
+  e.col_major = true;
+  e.rowsum_out = db;
+  e.rowsum_m = db ? CKK : -1;
+  const int tbn = (int)conv_tile_width(O);
+  CUtensorMap ta, tb;
+  GT_TRY(tc::make_halo_map(ctx, &ta, x, g, ga));
+  GT_TRY(tc::make_map3(ctx, &tb, dy, L, O, g.N, tbn / 2));
+  char* err = tbn == 64    ? tc::conv_wgrad_launch<64>(ctx, s, ta, tb, e, ga)
+              : tbn == 128 ? tc::conv_wgrad_launch<128>(ctx, s, ta, tb, e, ga)
+                           : tc::conv_wgrad_launch<256>(ctx, s, ta, tb, e, ga);
   if (!err) *done = true;
   return err;
 }

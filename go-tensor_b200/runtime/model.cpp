@@ -273,9 +273,10 @@ void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t
       bits_.emplace_back(ctx_, (size_t)((src.M + 31) / 32) * (size_t)src.N * sizeof(uint32_t));
       src.bits = (uint32_t*)bits_.back().get();
     }
-  // Every conv keeps its forward's im2col columns for its backward.
+  // A float64 conv keeps its forward's im2col columns for its backward; the
+  // float32 convs are implicit GEMMs and keep none.
   for (auto& op : ops_) {
-    if (op.kind != Op::CONV) continue;
+    if (op.kind != Op::CONV || dtype_ != GT_FLOAT64) continue;
     const int64_t rows = op.g.N * op.g.OH * op.g.OW, ckk = op.g.C * op.g.KH * op.g.KW;
     if (rows * ckk == 0) continue;
     cols_.emplace_back(ctx_, (size_t)(rows * ckk) * es_);
@@ -438,7 +439,7 @@ void Model::backward(bool join) {
         break;
       }
       case Op::CONV:
-        if (!op.cols) {  // no output positions: the gradients are zero
+        if (!op.cols) {  // float32 (implicit GEMMs from x and dy), or no output positions
           check(gt_conv_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, &op.g, op.O));
           if (world_ > 1) issue_ready_buckets(op.w_off);
           if (op.needs_dx) {

@@ -45,21 +45,34 @@ def new(n, dt=T.Float32):
 
 
 def test_wide_mlp_first_layer_weight_gradient_full_shape():
+    """dY carries the mean loss's 1/B factor, as every gradient of the step
+    does. Unscaled N(0,1) operands would make the partial sums reach ~90, and
+    the oracle's own sequential fp32 rounding (~K eps |partial sum|) would then
+    exceed the 1e-4 floor by itself; the float64 check below holds the device
+    to fp32-class error whatever the scale."""
     M, K, N = 8192, 4096, 4096  # batch, in, out
     rng = np.random.default_rng(21)
     x = rng.standard_normal((M, K)).astype(np.float32)
-    dy = rng.standard_normal((M, N)).astype(np.float32)
+    dy = (rng.standard_normal((M, N)) / M).astype(np.float32)
     be = cuda_backend()
     dw, db = new(N * K), new(N)
     check(be.lib.gt_linear_bwd_weight(be.ctx.ptr, 0, dev(x).ptr, dev(dy).ptr, dw.ptr, db.ptr, M, K, N))
-    got_w, got_b = be.ToHost(dw), be.ToHost(db)
+    got_w, got_b = be.ToHost(dw).reshape(N, K), be.ToHost(db)
     cpu = T.backend_for(T.CPU)
     # dW' (K, N) = X^T (K, M) @ dY (M, N), as the MatMul closure computes it
     # (tensor/ops.go:324-326); the Linear weight gradient is its transpose.
     want = cpu.ToHost(cpu.MatMul(cpu.FromHost(x.reshape(-1)), cpu.FromHost(dy.reshape(-1)), K, M, N, True, False))
-    assert_close(got_w.reshape(N, K), want.reshape(K, N).T, 1e-4, "dW 4096x4096 over 8192 rows")
+    assert_close(got_w, want.reshape(K, N).T, 1e-4, "dW 4096x4096 over 8192 rows")
     want_b = cpu.ToHost(cpu.Reduce(0, cpu.FromHost(dy.reshape(-1)), 1, M, N))
     assert_close(got_b, want_b, 1e-4, "db over 8192 rows")
+    # against the exact product: error relative to sum |dy||x| at fp32 level,
+    # no worse than the oracle's own fp32 accumulation
+    rows = rng.choice(N, 64, replace=False)  # 64 output rows (262,144 values) in float64
+    exact = dy[:, rows].T.astype(np.float64) @ x.astype(np.float64)
+    scale = np.abs(dy[:, rows]).T.astype(np.float64) @ np.abs(x).astype(np.float64)
+    err = np.abs(got_w[rows] - exact) / scale
+    err_oracle = np.abs(want.reshape(K, N).T[rows] - exact) / scale
+    assert err.max() <= max(err_oracle.max(), 2.0 ** -20), (err.max(), err_oracle.max())
 
 
 def test_conv_stack_first_conv_weight_gradient_full_batch():

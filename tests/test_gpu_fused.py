@@ -218,17 +218,25 @@ def test_fused_losses_empty(fn):
     assert np.isnan(host(loss)[0])
 
 
+# (N, C, H, W, O, k, stride, pad). The float32 implicit-GEMM paths (stride 1,
+# position tiles that are rectangles of the output) cover tile widths 64 /
+# 128 / 256 and two column tiles (O = 512), weights whose C*k*k is not a
+# multiple of 4 (padded copies) and a 1x1 window; the other shapes (stride
+# 2, 5x5 with 144 positions, 28 x 28 and 14 x 14 planes, ragged O) take the
+# explicit im2col path.
 CONVS = [(2, 3, 5, 5, 4, 3, 1, 0), (2, 2, 5, 4, 3, 3, 2, 1), (8, 1, 28, 28, 32, 3, 1, 1), (4, 32, 14, 14, 64, 3, 1, 1),
-         (2, 3, 32, 32, 64, 3, 1, 1)]
+         (2, 3, 32, 32, 64, 3, 1, 1), (16, 64, 16, 16, 128, 3, 1, 1), (8, 128, 8, 8, 256, 3, 1, 1),
+         (8, 256, 4, 4, 512, 3, 1, 1), (2, 5, 8, 6, 70, 3, 1, 1), (2, 4, 12, 12, 20, 5, 1, 2), (4, 16, 8, 8, 32, 1, 1, 0)]
 
 
 @pytest.mark.parametrize("dt,npdt,tol", DT)
-@pytest.mark.parametrize("cs", CONVS + [(16, 64, 16, 16, 128, 3, 1, 1)])
+@pytest.mark.parametrize("cs", CONVS[:6])
 def test_conv_cols_entry_points(dt, npdt, tol, cs):
-    """gt_conv_fwd_cols stores what gt_conv_fwd stores and keeps the columns
-    gt_im2col builds; gt_conv_bwd from those columns gives what
-    gt_conv_bwd_weight and gt_conv_bwd_data give, bit for bit, with and
-    without dx."""
+    """gt_conv_fwd_cols keeps the columns gt_im2col builds (bit for bit) and
+    stores the convolution; gt_conv_bwd from those columns gives the weight,
+    bias and input gradients, the same bits with and without dx. These are the
+    explicit-column algorithm (im2col, GEMM, col2im), so they are held to the
+    oracle like the implicit-GEMM entry points, not to those bit for bit."""
     N, C, H, W, O, k, s, p = cs
     rng = np.random.default_rng(3 * sum(cs))
     x = rng.standard_normal((N, C, H, W)).astype(npdt)
@@ -238,23 +246,28 @@ def test_conv_cols_entry_points(dt, npdt, tol, cs):
     gg = ctypes.byref(_lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_]))
     L, CKK = g.OH * g.OW, C * k * k
     xd, wd, bd = dev(x), dev(w), dev(b)
-    y1, y2, cols, cols_ref = new(N * O * L, dt), new(N * O * L, dt), new(N * L * CKK, dt), new(N * L * CKK, dt)
-    check(lib().gt_conv_fwd(ctx(), dt, xd.ptr, wd.ptr, bd.ptr, y1.ptr, gg, O, 1))
+    y2, cols, cols_ref = new(N * O * L, dt), new(N * L * CKK, dt), new(N * L * CKK, dt)
     check(lib().gt_conv_fwd_cols(ctx(), dt, xd.ptr, wd.ptr, bd.ptr, y2.ptr, cols.ptr, gg, O, 1))
     check(lib().gt_im2col(ctx(), dt, xd.ptr, cols_ref.ptr, gg))
-    assert_bits(host(y2), host(y1), "conv fwd")
     assert_bits(host(cols), host(cols_ref), "cols")
-    dyd = dev(rng.standard_normal((N, O, g.OH, g.OW)).astype(npdt))
-    dx1, dw1, db1 = new(N * C * H * W, dt), new(O * CKK, dt), new(O, dt)
-    check(lib().gt_conv_bwd_weight(ctx(), dt, xd.ptr, dyd.ptr, dw1.ptr, db1.ptr, gg, O))
-    check(lib().gt_conv_bwd_data(ctx(), dt, dyd.ptr, wd.ptr, dx1.ptr, gg, O))
+    with T.no_grad():
+        want = T.Conv2d(ref(x, N, C, H, W), ref(w, O, C, k, k), ref(b, O), s, p).ReLU().Float64s()
+    assert_close(host(y2), want, tol, "conv fwd from columns")
+    # dy at the scale a mean loss gives it (1/N per image): unscaled N(0,1)
+    # gradients summed over N*OH*OW positions reach partial sums where the
+    # oracle's own sequential rounding is ~1e-4 by itself
+    dy = (rng.standard_normal((N, O, g.OH, g.OW)) / N).astype(npdt)
+    dyd = dev(dy)
     dx2, dw2, db2, dw3 = new(N * C * H * W, dt), new(O * CKK, dt), new(O, dt), new(O * CKK, dt)
     check(lib().gt_conv_bwd(ctx(), dt, cols.ptr, dyd.ptr, wd.ptr, dx2.ptr, dw2.ptr, db2.ptr, gg, O))
     check(lib().gt_conv_bwd(ctx(), dt, cols.ptr, dyd.ptr, wd.ptr, None, dw3.ptr, None, gg, O))
-    assert_bits(host(dx2), host(dx1), "dx")
-    assert_bits(host(dw2), host(dw1), "dw")
-    assert_bits(host(db2), host(db1), "db")
-    assert_bits(host(dw3), host(dw1), "dw without dx")
+    assert_bits(host(dw3), host(dw2), "dw without dx")
+    xs, ws, bs = ref(x, N, C, H, W).SetRequiresGrad(True), ref(w, O, C, k, k).SetRequiresGrad(True), \
+        ref(b, O).SetRequiresGrad(True)
+    T.Conv2d(xs, ws, bs, s, p).Backward(ref(dy, N, O, g.OH, g.OW))
+    assert_close(host(dx2), xs.Grad().Float64s(), tol, "conv dx from columns")
+    assert_close(host(dw2), ws.Grad().Float64s(), tol, "conv dw from columns")
+    assert_close(host(db2), bs.Grad().Float64s(), tol, "conv db from columns")
 
 
 @pytest.mark.parametrize("dt,npdt,tol", DT)
@@ -274,7 +287,7 @@ def test_conv_fwd_bwd(dt, npdt, tol, cs):
         with T.no_grad():
             want = apply_act(T.Conv2d(ref(x, N, C, H, W), ref(w, O, C, k, k), ref(b, O), s, p), act).Float64s()
         assert_close(host(y), want, tol, f"conv fwd act={act}")
-    dy = rng.standard_normal((N, O, g.OH, g.OW)).astype(npdt)
+    dy = (rng.standard_normal((N, O, g.OH, g.OW)) / N).astype(npdt)  # the mean loss's scale, as above
     dx, dw, db = new(N * C * H * W, dt), new(O * C * k * k, dt), new(O, dt)
     check(lib().gt_conv_bwd_data(ctx(), dt, dev(dy).ptr, dev(w).ptr, dx.ptr, ctypes.byref(gg), O))
     check(lib().gt_conv_bwd_weight(ctx(), dt, dev(x).ptr, dev(dy).ptr, dw.ptr, db.ptr, ctypes.byref(gg), O))
@@ -284,6 +297,54 @@ def test_conv_fwd_bwd(dt, npdt, tol, cs):
     assert_close(host(dx), xs.Grad().Float64s(), tol, "conv dx")
     assert_close(host(dw), ws.Grad().Float64s(), tol, "conv dw")
     assert_close(host(db), bs.Grad().Float64s(), tol, "conv db")
+
+
+@pytest.mark.parametrize("cs", [(2, 3, 32, 32, 64, 3, 1, 1), (4, 64, 16, 16, 128, 3, 1, 1), (4, 128, 8, 8, 256, 3, 1, 1),
+                                (8, 256, 4, 4, 512, 3, 1, 1), (4, 16, 8, 8, 32, 1, 1, 0), (2, 8, 16, 16, 16, 5, 1, 2)])
+def test_conv_implicit_against_float64(cs):
+    """The float32 implicit-GEMM convolutions (forward, input and weight
+    gradients, bias gradient) at the conv stack's layer shapes and a 1x1 and
+    a 5x5 window,
+    on unscaled N(0,1) data, against the exact (float64) results: the error,
+    relative to the same sums over absolute values, stays at the level of a
+    float32 dot product (the oracle's own float32 error is shown beside it)."""
+    N, C, H, W, O, k, s, p = cs
+    rng = np.random.default_rng(sum(cs) + 1)
+    x = rng.standard_normal((N, C, H, W)).astype(np.float32)
+    w = rng.standard_normal((O, C, k, k)).astype(np.float32)
+    b = rng.standard_normal(O).astype(np.float32)
+    g = T.conv_geom("Conv2d", [N, C, H, W], k, k, s, p)
+    gg = ctypes.byref(_lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_]))
+    dy = rng.standard_normal((N, O, g.OH, g.OW)).astype(np.float32)
+    y, dx, dw, db = new(N * O * g.OH * g.OW, T.Float32), new(N * C * H * W, T.Float32), new(O * C * k * k, T.Float32), \
+        new(O, T.Float32)
+    check(lib().gt_conv_fwd(ctx(), 0, dev(x).ptr, dev(w).ptr, dev(b).ptr, y.ptr, gg, O, 0))
+    assert lib().gt_gemm_path_taken() == 4
+    check(lib().gt_conv_bwd_data(ctx(), 0, dev(dy).ptr, dev(w).ptr, dx.ptr, gg, O))
+    assert lib().gt_gemm_path_taken() == 4
+    check(lib().gt_conv_bwd_weight(ctx(), 0, dev(x).ptr, dev(dy).ptr, dw.ptr, db.ptr, gg, O))
+    assert lib().gt_gemm_path_taken() == 4
+
+    def run(dt, absolute=False):
+        def t(a, *shape):
+            a = np.abs(a) if absolute else a
+            return T.FromFloat64(a.astype(np.float64).reshape(-1), *shape).ToDType(dt).SetRequiresGrad(True)
+        xs, ws, bs = t(x, N, C, H, W), t(w, O, C, k, k), t(b, O)
+        out = T.Conv2d(xs, ws, bs, s, p)
+        out.Backward(t(dy, N, O, g.OH, g.OW))
+        return [out.Float64s(), xs.Grad().Float64s(), ws.Grad().Float64s(), bs.Grad().Float64s()]
+
+    T.SetDefaultDType(T.Float64)
+    try:
+        exact, scale = run(T.Float64), run(T.Float64, absolute=True)
+    finally:
+        T.SetDefaultDType(T.Float32)
+    oracle32 = run(T.Float32)
+    for name, got, ex, sc, o32 in zip(("y", "dx", "dw", "db"), (host(y), host(dx), host(dw), host(db)), exact, scale,
+                                      oracle32):
+        err = np.abs(got.astype(np.float64) - ex) / np.maximum(sc, 1e-30)
+        err32 = np.abs(o32 - ex) / np.maximum(sc, 1e-30)
+        assert err.max() <= max(4 * err32.max(), 2.0 ** -20), (name, cs, float(err.max()), float(err32.max()))
 
 
 @pytest.mark.parametrize("dt,npdt,tol", DT)
