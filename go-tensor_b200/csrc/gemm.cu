@@ -138,9 +138,85 @@ __global__ void relu_bits_kernel(const T* __restrict__ y, uint32_t* __restrict__
   }
 }
 
+// db[n] = sum over the 32-row blocks of ws[b * N + n], blocks in order.
+__global__ void colsum_finish_kernel(const float* __restrict__ ws, int64_t blocks, int64_t N, float* __restrict__ db) {
+  for (int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
+    float acc = ws[n];
+    for (int64_t b = 1; b < blocks; b++) acc = __fadd_rn(acc, ws[b * N + n]);
+    db[n] = acc;
+  }
+}
+
+// dx = the GEMM of s with epilogue e (a Linear's input gradient, M x K), and
+// db_prev (K) = its column sums: the bias gradient of the Linear that
+// produced this layer's input (sumTo over the batch, tensor/ops.go:418-433).
+// On the float32 tcgen05 path the epilogue adds each 32-row block's columns
+// while it stores them, and one small kernel adds the blocks; elsewhere a
+// reduction over dx follows the GEMM.
+static char* bwd_data_with_db(gt_ctx* ctx, int dtype, const GemmShape& s, const void* dy, const void* w, void* dx,
+                              void* db_prev, const Epi<float>& ef, const Epi<double>& ed, int64_t M, int64_t K) {
+  if (dtype == GT_FLOAT32 && tc_writes_colsums(ef, K)) {
+    const int64_t blocks = ceil_div(M, 32);
+    void* ws = nullptr;
+    GT_TRY(scratch(ctx, (size_t)(blocks * K) * sizeof(float), &ws));
+    Epi<float> e = ef;
+    e.colsum_ws = (float*)ws;
+    e.ldcs = K;
+    char* err = gemm<float>(ctx, s, (const float*)dy, (const float*)w, e);
+    const bool fused = !err && g_gemm_taken == 2;
+    if (fused) {
+      colsum_finish_kernel<<<grid_for(ctx, K, 256), 256, 0, ctx->stream>>>((const float*)ws, blocks, K,
+                                                                          (float*)db_prev);
+      count_launch();
+      cudaError_t ce = cudaGetLastError();
+      if (ce != cudaSuccess) err = cuda_error(ce, "colsum_finish_kernel launch", __FILE__, __LINE__);
+    }
+    release(ctx, ws);
+    if (err || fused) return err;
+  } else if (dtype == GT_FLOAT32) {
+    GT_TRY(gemm<float>(ctx, s, (const float*)dy, (const float*)w, ef));
+  } else {
+    GT_TRY(gemm<double>(ctx, s, (const double*)dy, (const double*)w, ed));
+  }
+  return gt_reduce(ctx, dtype, GT_SUM, dx, db_prev, 1, M, K);
+}
+
 }  // namespace gt
 
 extern "C" {
+
+char* gt_linear_bwd_data_db(gt_ctx* ctx, int dtype, const void* dy, const void* w, const void* y_prev, int act_prev,
+                            void* dx, void* db_prev, int64_t M, int64_t K, int64_t N) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M <= 0 || K <= 0 || N <= 0 || !db_prev) return errorf("gt_linear_bwd_data_db: bad arguments");
+  GemmShape s{M, K, N, false, false, N, K};
+  Epi<float> ef;
+  Epi<double> ed;
+  ef.out = (float*)dx, ed.out = (double*)dx;
+  ef.ldc = ed.ldc = K;
+  if (y_prev && act_prev != GT_ACT_NONE) {
+    ef.dmask = (const float*)y_prev, ed.dmask = (const double*)y_prev;
+    ef.dact = ed.dact = act_prev;
+    ef.ldm = ed.ldm = K;
+  }
+  return bwd_data_with_db(ctx, dtype, s, dy, w, dx, db_prev, ef, ed, M, K);
+}
+
+char* gt_linear_bwd_data_bits_db(gt_ctx* ctx, int dtype, const void* dy, const void* w, const uint32_t* bits,
+                                 void* dx, void* db_prev, int64_t M, int64_t K, int64_t N) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (M <= 0 || K <= 0 || N <= 0 || !bits || !db_prev) return errorf("gt_linear_bwd_data_bits_db: bad arguments");
+  GemmShape s{M, K, N, false, false, N, K};
+  Epi<float> ef;
+  Epi<double> ed;
+  ef.out = (float*)dx, ed.out = (double*)dx;
+  ef.ldc = ed.ldc = K;
+  ef.dbits = ed.dbits = bits;
+  ef.ldw = ed.ldw = K;
+  return bwd_data_with_db(ctx, dtype, s, dy, w, dx, db_prev, ef, ed, M, K);
+}
 
 char* gt_set_gemm_sm_reserve(gt_ctx* ctx, int sms) {
   GT_ENTER(ctx);

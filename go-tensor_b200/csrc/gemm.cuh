@@ -46,6 +46,12 @@ struct Epi {
   bool col_major = false;
   T* rowsum_out = nullptr;
   int64_t rowsum_m = -1;
+  // Column partial sums of the stored values (tcgen05 plain, mask and bit-mask
+  // epilogues): colsum_ws[(m / 32) * ldcs + n] = sum over the 32-row block
+  // of C(m, n), rows in order; a second kernel adds the blocks. With dX of a
+  // Linear as C, the column sums are the bias gradient of the layer before.
+  T* colsum_ws = nullptr;
+  int64_t ldcs = 0;
 
   // The finished value of C(m, n): bias, activation, activation derivative.
   __device__ __forceinline__ T finish(int64_t m, int64_t n, T acc) const {
@@ -133,6 +139,10 @@ char* conv_fwd_gemm(gt_ctx* ctx, const float* x, const float* w, int64_t w_pitch
                     const gt_geom& g, int64_t O, int act, bool* done);
 char* conv_wgrad_gemm(gt_ctx* ctx, const float* x, const float* dy, float* dw, float* db, const gt_geom& g,
                       int64_t O, bool* done);
+
+// Whether a float32 GEMM with this epilogue, if it runs on the tcgen05 path,
+// writes its column partial sums (Epi::colsum_ws).
+bool tc_writes_colsums(const Epi<float>& epi, int64_t n_cols);
 
 // Dispatches to the fastest qualifying path.
 template <typename T>

@@ -87,12 +87,15 @@ constexpr uint32_t EPI_BYTES = PROMOTER_WARPS * 32 * EPI_LD * 4;
 // Layout of one instantiation for a tile of 256 x BN outputs (C columns BN;
 // each CTA holds BN / 2 rows of B per stage and 128 lanes x BN columns of
 // each of the two tensor-memory accumulators).
-template <int BN>
+template <int BN, bool HALO = false>
 struct Tile {
   static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
   static constexpr int BNH = BN / 2;  // B rows per CTA
   static constexpr uint32_t B_BYTES = BNH * BK * 4;
-  static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // A hi, A lo, B hi, B lo
+  // A hi, A lo, B hi, B lo, and (HALO) a region of A_BYTES for a gathered
+  // operand's halo, so the gather writes both split planes in one pass.
+  static constexpr uint32_t HALO_OFFSET = 2 * (A_BYTES + B_BYTES);
+  static constexpr uint32_t STAGE_BYTES = HALO_OFFSET + (HALO ? A_BYTES : 0u);
   static constexpr int STAGES = tc::STAGES;
   static constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
   static constexpr uint32_t EPI_OFFSET = BAR_OFFSET + 512;
@@ -404,8 +407,18 @@ __device__ __forceinline__ void pos_rows(const Gather& g, int lane, int (&hb)[4]
   }
 }
 
-__device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, const float* halo, int rows, int k0,
-                                           int lane, const int (&hb)[4]) {
+__device__ __forceinline__ void store_row4(uint8_t* hi, uint8_t* lo, uint32_t off, float a, float b, float c,
+                                           float d) {
+  if (lo)
+    split_store4(hi, lo, off, a, b, c, d);
+  else
+    *(float4*)(hi + off) = make_float4(a, b, c, d);
+}
+
+// lo NULL: raw values into the hi plane (split in place afterwards); else the
+// split planes directly.
+__device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, uint8_t* lo, const float* halo, int rows,
+                                           int k0, int lane, const int (&hb)[4]) {
   const int plane = g.box_w * g.box_h;
   const int c_lo = k0 / g.KHW;
   int c = 0;
@@ -428,7 +441,7 @@ __device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, const f
 #pragma unroll
     for (int i = 0; i < 4; i++) {
       const int r = lane + 32 * i;
-      if (r < rows) *(float4*)(hi + kmajor_offset(r, c4)) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+      if (r < rows) store_row4(hi, lo, kmajor_offset(r, c4), v[i][0], v[i][1], v[i][2], v[i][3]);
     }
   }
 }
@@ -450,8 +463,8 @@ __device__ __forceinline__ void ck_rows(const Gather& g, int row0, int lane, int
   }
 }
 
-__device__ __forceinline__ void gather_ck(const Gather& g, uint8_t* hi, const float* halo, int rows, int lane,
-                                          const int (&koff)[4], const int (&kind)[4]) {
+__device__ __forceinline__ void gather_ck(const Gather& g, uint8_t* hi, uint8_t* lo, const float* halo, int rows,
+                                          int lane, const int (&koff)[4], const int (&kind)[4]) {
 #pragma unroll 1
   for (int i = 0; i < 4; i++) {
     const int r = lane + 32 * i;
@@ -471,7 +484,7 @@ __device__ __forceinline__ void gather_ck(const Gather& g, uint8_t* hi, const fl
     }
 #pragma unroll
     for (int c4 = 0; c4 < 4; c4++)
-      *(float4*)(hi + kmajor_offset(r, c4)) = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+      store_row4(hi, lo, kmajor_offset(r, c4), v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
   }
 }
 
@@ -522,9 +535,14 @@ __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const Gemm
   const int rows = (int)(s.M - m0 < 32 ? s.M - m0 : 32);
   float* op = epi.out + m0 * epi.ldc + n;
   if (n >= s.N) return;
+  float cs = 0.0f;  // column partial sum of the stored values (Epi::colsum_ws)
   if (EK == EK_PLAIN) {
 #pragma unroll 4
-    for (int r = 0; r < rows; r++) op[r * epi.ldc] = xpose[r * EPI_LD + lane];
+    for (int r = 0; r < rows; r++) {
+      const float v = xpose[r * EPI_LD + lane];
+      op[r * epi.ldc] = v;
+      cs = __fadd_rn(cs, v);
+    }
   } else if (EK == EK_BIAS_RELU) {
     // With a bit mask, this lane's column of the block (m0 is a multiple of
     // 32) becomes one word: bit r = (row r's value > 0).
@@ -545,7 +563,11 @@ __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const Gemm
     // bytes per lane instead of 128 bytes of activations.
     const uint32_t w = rows > 0 ? __ldg(epi.dbits + (m0 >> 5) * epi.ldw + n) : 0u;
 #pragma unroll 4
-    for (int r = 0; r < rows; r++) op[r * epi.ldc] = __fmul_rn(xpose[r * EPI_LD + lane], ((w >> r) & 1u) ? 1.0f : 0.0f);
+    for (int r = 0; r < rows; r++) {
+      const float v = __fmul_rn(xpose[r * EPI_LD + lane], ((w >> r) & 1u) ? 1.0f : 0.0f);
+      op[r * epi.ldc] = v;
+      cs = __fadd_rn(cs, v);
+    }
   } else if (EK == EK_MASK) {
     // The mask values of 8 rows are requested before any is used.
     const float* mp = epi.dmask + m0 * epi.ldm + n;
@@ -556,7 +578,11 @@ __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const Gemm
       for (int r = 0; r < 8; r++) mask[r] = r0 + r < rows ? __ldg(mp + (r0 + r) * epi.ldm) : 0.0f;
 #pragma unroll
       for (int r = 0; r < 8; r++)
-        if (r0 + r < rows) op[(r0 + r) * epi.ldc] = act_bwd(epi.dact, xpose[(r0 + r) * EPI_LD + lane], mask[r]);
+        if (r0 + r < rows) {
+          const float v = act_bwd(epi.dact, xpose[(r0 + r) * EPI_LD + lane], mask[r]);
+          op[(r0 + r) * epi.ldc] = v;
+          cs = __fadd_rn(cs, v);
+        }
     }
   } else if (EK == EK_CONV) {
     // C(m, n) -> out[((n / L) * M + m) * L + n % L]: a warp's row is 32
@@ -577,6 +603,8 @@ __device__ __forceinline__ void epilogue_block(const Epi<float>& epi, const Gemm
 #pragma unroll 1
     for (int r = 0; r < rows; r++) epi.store(m0 + r, n, xpose[r * EPI_LD + lane]);
   }
+  if (EK == EK_PLAIN || EK == EK_MASK || EK == EK_MASKBITS)
+    if (epi.colsum_ws && rows > 0) epi.colsum_ws[(m0 >> 5) * epi.ldcs + n] = cs;
 }
 
 // How a launch covers its tiles: tiles [0, whole) as single units over all
@@ -634,11 +662,20 @@ __device__ __forceinline__ void xpose_chunk(float* xpose, const float (&tot)[N],
   }
 }
 
+// A gathered operand has its own halo region when the stage still fits six
+// times in shared memory (tile widths up to 128); at 256 the halo lands in the
+// A lo plane and the gather's raw values are split in place afterwards.
+template <int TBN, int AS>
+constexpr bool halo_region() {
+  return AS != A_TMA && TBN <= 128;
+}
+
 template <bool A_MN, bool B_MN, int EK, int TBN, int AS, int BS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             GemmShape s, Epi<float> epi, SplitPlan sp, Gather ga) {
-  using TL = Tile<TBN>;
+  constexpr bool HSEP = halo_region<TBN, AS>();
+  using TL = Tile<TBN, HSEP>;
   constexpr int HC = TL::HC;
   constexpr int STAGES = TL::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -707,10 +744,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const int k0 = kt * BK;
             if constexpr (AS == A_IM2COL_POS) {  // the halo of this block's positions, the slice's channels
               const int n0 = a_row / ga.L, oh0 = (a_row - n0 * ga.L) / ga.OW;
-              tma_load_4d(a_hi + A_BYTES, &tmA, &sh->full[st], -ga.rp, oh0 - ga.pad, k0 / ga.KHW, n0);
+              tma_load_4d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], -ga.rp, oh0 - ga.pad,
+                          k0 / ga.KHW, n0);
             } else if constexpr (AS == A_IM2COL_CK) {  // the halo of the slice's positions, this block's channels
               const int n = k0 / ga.L, l0 = k0 - n * ga.L, oh0 = l0 / ga.OW, ow0 = l0 - oh0 * ga.OW;
-              tma_load_4d(a_hi + A_BYTES, &tmA, &sh->full[st], ow0 - ga.rp, oh0 - ga.pad, a_row / ga.KHW, n);
+              tma_load_4d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], ow0 - ga.rp, oh0 - ga.pad,
+                          a_row / ga.KHW, n);
             }
             if constexpr (AS == A_TMA) {
               if (A_MN) {
@@ -827,13 +866,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             // then split in place (the lo plane is overwritten only after
             // every lane has read the halo). Rows past M are left as they
             // are: they only reach rows of C that are never stored.
-            const float* halo = (const float*)(stage + A_BYTES);
+            const float* halo = (const float*)(stage + (HSEP ? TL::HALO_OFFSET : A_BYTES));
+            uint8_t* lo = HSEP ? stage + A_BYTES : nullptr;  // with its own halo region: split while gathering
             if constexpr (AS == A_IM2COL_POS)
-              gather_pos(ga, stage, halo, a_rows, kt * BK, lane, rows4);
+              gather_pos(ga, stage, lo, halo, a_rows, kt * BK, lane, rows4);
             else
-              gather_ck(ga, stage, halo, a_rows, lane, rows4, kind4);
-            __syncwarp();
-            split_tf32((float4*)stage, (float4*)(stage + A_BYTES), a_rows * 64 / 16, lane);
+              gather_ck(ga, stage, lo, halo, a_rows, lane, rows4, kind4);
+            if constexpr (!HSEP) {
+              __syncwarp();
+              split_tf32((float4*)stage, (float4*)(stage + A_BYTES), a_rows * 64 / 16, lane);
+            }
           }
           if constexpr (BS != B_SPLIT2)
             split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + TL::B_BYTES),
@@ -916,18 +958,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll 4
           for (int r = 0; r < 32; r++) part[r * TBN + 32 * j] = xpose[r * EPI_LD + lane];
         } else if constexpr (EK == EK_NCHW_POS) {
-          if (nchw_base) {
-            const int64_t L = epi.nchw_L;
-            const bool relu = epi.act == GT_ACT_RELU;
-#pragma unroll 4
-            for (int i = 0; i < 32; i++) {
-              const int64_t n = n0 + 32 * j + i;
-              if (n < s.N) {
-                float v = xpose[lane * EPI_LD + i];
-                if (epi.bias) v = __fadd_rn(v, __ldg(epi.bias + n));
-                if (relu) v = go_max(v, 0.0f);
-                nchw_base[n * L] = v;
-              }
+          // the block's 32 biases, one per lane, broadcast by shuffles (a
+          // load per column would wait on memory before every store)
+          const int64_t nl = n0 + 32 * j + lane;
+          const float my_bias = epi.bias && nl < s.N ? __ldg(epi.bias + nl) : 0.0f;
+          const int64_t L = epi.nchw_L;
+          const bool relu = epi.act == GT_ACT_RELU;
+          float* col = nchw_base ? nchw_base + (n0 + 32 * j) * L : nullptr;  // NULL: this lane's row is past M
+#pragma unroll 8
+          for (int i = 0; i < 32; i++) {
+            float v = xpose[lane * EPI_LD + i];
+            const float b = __shfl_sync(0xffffffffu, my_bias, i);  // every lane takes part
+            if (col && n0 + 32 * j + i < s.N) {
+              if (epi.bias) v = __fadd_rn(v, b);
+              if (relu) v = go_max(v, 0.0f);
+              col[i * L] = v;
             }
           }
         } else if constexpr (EK == EK_COLMAJOR) {
@@ -1033,9 +1078,10 @@ template <bool A_MN, bool B_MN, int EK, int TBN = BN, int AS = A_TMA, int BS = B
 static char* launch_kernel(gt_ctx* ctx, const GemmShape& s, const CUtensorMap& ta, const CUtensorMap& tb,
                            const Epi<float>& epi, const SplitPlan& sp, const Gather& ga) {
   auto kern = gemm_tf32x3_pair_kernel<A_MN, B_MN, EK, TBN, AS, BS>;
+  using TL = Tile<TBN, halo_region<TBN, AS>()>;
   static bool configured[64] = {};
   if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
-    GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<TBN>::SMEM_BYTES));
+    GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TL::SMEM_BYTES));
     if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
   }
   const int64_t tiles = ceil_div(s.M, 2 * BM) * ceil_div(s.N, TBN);
@@ -1045,7 +1091,7 @@ static char* launch_kernel(gt_ctx* ctx, const GemmShape& s, const CUtensorMap& t
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = Tile<TBN>::SMEM_BYTES;
+  cfg.dynamicSmemBytes = TL::SMEM_BYTES;
   cfg.stream = ctx->stream;
   GT_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, s, epi, sp, ga));
   GT_LAUNCH_CHECK();
@@ -1114,6 +1160,35 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, SplitPlan sp,
     float acc = ws[i];
     for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
     epi.store(m, n, acc);
+  }
+}
+
+// The same with column partial sums (Epi::colsum_ws): a thread finishes one
+// column of 32 rows of a split tile and adds the finished values in row order.
+template <int TBN>
+__global__ void splitk_reduce_colsum_kernel(const float* __restrict__ ws, SplitPlan sp, int tiles, int n_tiles,
+                                            int64_t M, int64_t N, Epi<float> epi) {
+  constexpr int64_t TE = Tile<TBN>::TILE_ELEMS;
+  const int rest = tiles - sp.whole;
+  const int64_t total = (int64_t)rest * TE;
+  const int64_t units = total / 32;  // (tile, 32-row block, column)
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(u / (TE / 32));
+    const int64_t v = u - (int64_t)r * (TE / 32);
+    const int rb = (int)(v / TBN), c = (int)(v % TBN);
+    const int t = sp.whole + r;
+    const int64_t m0 = (int64_t)(t / n_tiles) * 2 * BM + 32 * rb, n = (int64_t)(t % n_tiles) * TBN + c;
+    if (m0 >= M || n >= N) continue;
+    float cs = 0.0f;
+    for (int j = 0; j < 32 && m0 + j < M; j++) {
+      const int64_t i = (int64_t)r * TE + (int64_t)(32 * rb + j) * TBN + c;
+      float acc = ws[i];
+      for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
+      const float y = epi.finish(m0 + j, n, acc);
+      epi.put(m0 + j, n, y);
+      cs = __fadd_rn(cs, y);
+    }
+    epi.colsum_ws[(m0 >> 5) * epi.ldcs + n] = cs;
   }
 }
 
@@ -1219,6 +1294,9 @@ static char* run_planned(gt_ctx* ctx, const GemmShape& s, const Epi<float>& epi,
   if (!err) {
     if (epi.bits_out)
       splitk_reduce_bits_kernel<<<grid_for(ctx, rest * TE / 32, 256), 256, 0, ctx->stream>>>(
+          sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
+    else if (epi.colsum_ws)
+      splitk_reduce_colsum_kernel<TBN><<<grid_for(ctx, rest * TE / 32, 256), 256, 0, ctx->stream>>>(
           sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
     else
       splitk_reduce_kernel<TBN><<<grid_for(ctx, rest * TE, 256), 256, 0, ctx->stream>>>(sp.ws, sp, (int)tiles,
@@ -1334,6 +1412,11 @@ char* tc_check_errors() {
     return errorf("tcgen05 GEMM: a pipeline wait timed out (site %d); results are invalid", e);
   }
   return nullptr;
+}
+
+bool tc_writes_colsums(const Epi<float>& epi, int64_t n_cols) {
+  const int k = tc::epi_kind(epi, n_cols);
+  return k == tc::EK_PLAIN || k == tc::EK_MASK || k == tc::EK_MASKBITS;
 }
 
 char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi,

@@ -82,11 +82,17 @@ template <typename T, int W, bool DEV_STEP>
 __global__ void adam_kernel(T* __restrict__ p, const T* __restrict__ g, T* __restrict__ m, T* __restrict__ v,
                             int64_t n, AdamScalars<T> s, T inv_bc2, T lr_bc1, const int64_t* step_dev, double lr,
                             double beta1, double beta2) {
-  if (DEV_STEP) {  // bias corrections from the device-side step counter, in float64
-    double t = (double)(*step_dev + 1);
-    double bc1 = 1.0 - pow(beta1, t), bc2 = 1.0 - pow(beta2, t);
-    inv_bc2 = (T)(1.0 / bc2);
-    lr_bc1 = (T)(lr / bc1);
+  if (DEV_STEP) {  // bias corrections from the device-side step counter, in float64, once per block
+    __shared__ T sc[2];
+    if (threadIdx.x == 0) {
+      const double t = (double)(*step_dev + 1);
+      const double bc1 = 1.0 - pow(beta1, t), bc2 = 1.0 - pow(beta2, t);
+      sc[0] = (T)(1.0 / bc2);
+      sc[1] = (T)(lr / bc1);
+    }
+    __syncthreads();
+    inv_bc2 = sc[0];
+    lr_bc1 = sc[1];
   }
   const int64_t nv = n / W;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {

@@ -19,6 +19,8 @@
 // A warp owns a row; the row's loss term goes to scratch and a second,
 // single-block kernel sums the B terms in a fixed order, so the loss is
 // deterministic. HBM traffic: read B*C logits, write B*C gradients.
+#include <algorithm>
+
 #include "gt_common.cuh"
 
 namespace gt {
@@ -79,10 +81,21 @@ __global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restr
 // recomputes, so both kernels produce identical bits. A log-probability
 // x_j - m - L is non-finite exactly when x_j - m or L is (x - m <= 0 and
 // 0 <= L <= log C), so the Pick's NaN rule needs no third pass either.
-template <typename T, int NPL>
+//
+// With COLS (and dx), each lane also sums the gradient values it writes, per
+// column, over the rows of its warp; the block's warps add theirs in warp
+// order and write one partial row per block to col_part (gridDim.x x C), which
+// xent_cols_kernel sums over the blocks: the column sums of dlogits, the bias
+// gradient of the Linear that produced the logits, without a second pass
+// over dlogits.
+template <typename T, int NPL, bool COLS = false>
 __global__ void xent_rows_reg_kernel(const T* __restrict__ x, const int32_t* __restrict__ labels, int64_t B, int C,
-                                     T c, T* __restrict__ row_terms, T* __restrict__ dx, int32_t* bad_label) {
+                                     T c, T* __restrict__ row_terms, T* __restrict__ dx, int32_t* bad_label,
+                                     T* __restrict__ col_part = nullptr) {
   const int lane = threadIdx.x & 31;
+  T cs[COLS ? NPL : 1];
+#pragma unroll
+  for (int t = 0; t < (COLS ? NPL : 1); t++) cs[t] = (T)0;
   int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t i = warp; i < B; i += nwarps) {
@@ -126,7 +139,9 @@ __global__ void xent_rows_reg_kernel(const T* __restrict__ x, const int32_t* __r
         const int j = lane + 32 * t;
         if (j < C) {
           const T g = mul_rn(q, v[t]);
-          dr[j] = j == y ? add_rn(-c, g) : g;
+          const T d = j == y ? add_rn(-c, g) : g;
+          dr[j] = d;
+          if constexpr (COLS) cs[t] = add_rn(cs[t], d);
         }
       }
     }
@@ -141,6 +156,52 @@ __global__ void xent_rows_reg_kernel(const T* __restrict__ x, const int32_t* __r
     }
     if (lane == 0) row_terms[i] = (nonfinite || bad) ? (T)NAN : picked;
   }
+  if constexpr (COLS) {
+    extern __shared__ unsigned char xent_smem[];
+    T* part = reinterpret_cast<T*>(xent_smem);  // [warps][C]
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int t = 0; t < NPL; t++)
+      if (lane + 32 * t < C) part[w * C + lane + 32 * t] = cs[t];
+    __syncthreads();
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+      T acc = part[j];
+      for (int k = 1; k < nw; k++) acc = add_rn(acc, part[k * C + j]);
+      col_part[(int64_t)blockIdx.x * C + j] = acc;
+    }
+  }
+}
+
+// db[j] = sum over the blocks of col_part[b][j], in block order.
+template <typename T>
+__global__ void xent_cols_kernel(const T* __restrict__ col_part, int blocks, int C, T* __restrict__ db) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < C; j += gridDim.x * blockDim.x) {
+    T acc = col_part[j];
+    for (int b = 1; b < blocks; b++) acc = add_rn(acc, col_part[(int64_t)b * C + j]);
+    db[j] = acc;
+  }
+}
+
+// The row kernel with column sums for rows of at most 1024 classes (a block
+// of 4 warps, at most 2 blocks per SM so that the partial rows stay few);
+// returns false for wider rows.
+template <typename T>
+static bool xent_rows_cols_launch(gt_ctx* ctx, const T* x, const int32_t* labels, int64_t B, int64_t C, T c,
+                                  T* terms, T* dx, int32_t* bad, T* col_part, int grid) {
+  const size_t sm = 4 * (size_t)C * sizeof(T);
+  if (C <= 32)
+    xent_rows_reg_kernel<T, 1, true><<<grid, 128, sm, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad, col_part);
+  else if (C <= 128)
+    xent_rows_reg_kernel<T, 4, true><<<grid, 128, sm, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad, col_part);
+  else if (C <= 512)
+    xent_rows_reg_kernel<T, 16, true><<<grid, 128, sm, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad,
+                                                                       col_part);
+  else if (C <= 1024)
+    xent_rows_reg_kernel<T, 32, true><<<grid, 128, sm, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad,
+                                                                       col_part);
+  else
+    return false;
+  return true;
 }
 
 // Launches the row kernel that fits C: register rows up to 1024 classes,
@@ -228,6 +289,38 @@ extern "C" char* gt_xent_fwd_bwd_noalloc(gt_ctx* ctx, int dtype, const void* log
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "xent launch", __FILE__, __LINE__);
   return nullptr;
+}
+
+extern "C" char* gt_xent_fwd_bwd_db(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
+                                    int64_t C, void* loss, void* dlogits, void* db, int32_t* bad_label) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  if (B <= 0 || C <= 0) return errorf("gt_xent_fwd_bwd_db: B and C must be positive");
+  if (!dlogits || !db) return errorf("gt_xent_fwd_bwd_db: dlogits and db must not be NULL");
+  if (C > 1024) {  // rows too wide for the register kernel: the gradient, then its column sums
+    GT_TRY(gt_xent_fwd_bwd(ctx, dtype, logits, labels, B, C, loss, dlogits, bad_label));
+    return gt_reduce(ctx, dtype, GT_SUM, dlogits, db, 1, B, C);
+  }
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  const int grid = (int)std::min<int64_t>(ceil_div(B, 4), 2 * (int64_t)ctx->sm_count);
+  void *terms = nullptr, *part = nullptr;
+  GT_TRY(scratch(ctx, B * es, &terms));
+  char* err = scratch(ctx, (size_t)grid * C * es, &part);
+  if (!err) {
+    GT_DISPATCH(dtype, {
+      T c = (T)(1.0 / (double)B);
+      xent_rows_cols_launch<T>(ctx, (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label, (T*)part,
+                               grid);
+      xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
+      xent_cols_kernel<T><<<grid_for(ctx, C, 256), 256, 0, ctx->stream>>>((const T*)part, grid, (int)C, (T*)db);
+    });
+    count_launch(3);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) err = cuda_error(e, "xent launch", __FILE__, __LINE__);
+  }
+  release(ctx, terms);
+  release(ctx, part);
+  return err;
 }
 
 extern "C" char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,

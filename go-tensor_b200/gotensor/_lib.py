@@ -89,6 +89,8 @@ CUDA_API = {
     "gt_bce_fwd_bwd": ("err", [_P, _INT, _P, _P, _I64, _P, _P]),
     "gt_linear_fwd_bits": ("err", [_P, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64]),
     "gt_linear_bwd_data_bits": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64]),
+    "gt_linear_bwd_data_db": ("err", [_P, _INT, _P, _P, _P, _INT, _P, _P, _I64, _I64, _I64]),
+    "gt_linear_bwd_data_bits_db": ("err", [_P, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64]),
     "gt_linear_bwd_weight": ("err", [_P, _INT, _P, _P, _P, _P, _I64, _I64, _I64]),
     "gt_act_bwd": ("err", [_P, _INT, _INT, _P, _P, _P, _I64]),
     "gt_bias_act": ("err", [_P, _INT, _P, _P, _I64, _I64, _I64, _INT]),
@@ -103,6 +105,7 @@ CUDA_API = {
     "gt_argmax_rows": ("err", [_P, _INT, _P, _I64, _I64, _P]),
     "gt_count_equal": ("err", [_P, _P, _P, _I64, _P]),
     "gt_xent_fwd_bwd": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P]),
+    "gt_xent_fwd_bwd_db": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P, _P]),
     "gt_xent_fwd_bwd_noalloc": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P]),
     "gt_sgd_step": ("err", [_P, _INT, _P, _P, _P, _I64, ctypes.POINTER(SgdCfg), _INT]),
     "gt_adam_step": ("err", [_P, _INT, _P, _P, _P, _P, _I64, ctypes.POINTER(AdamCfg), _I64]),

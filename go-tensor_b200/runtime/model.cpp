@@ -400,7 +400,11 @@ void Model::backward(bool join) {
   // derivative of the activation that produced that output is already in it.
   void* g = grad_a_.get();
   void* spare = grad_b_.get();
-  check(gt_xent_fwd_bwd(ctx_, dtype_, ops_.back().out, labels_device(), batch_, classes_, loss_.get(), g, nullptr));
+  if (ops_.back().db_upstream)  // the last Linear's bias gradient in the same pass
+    check(gt_xent_fwd_bwd_db(ctx_, dtype_, ops_.back().out, labels_device(), batch_, classes_, loss_.get(), g,
+                             gr + ops_.back().b_off * es_, nullptr));
+  else
+    check(gt_xent_fwd_bwd(ctx_, dtype_, ops_.back().out, labels_device(), batch_, classes_, loss_.get(), g, nullptr));
   bool g_pre = false;
   next_bucket_ = 0;
   for (int i = (int)ops_.size() - 1; i >= first_param_op_; i--) {
@@ -412,15 +416,15 @@ void Model::backward(bool join) {
       case Op::LINEAR: {
         if (world_ > 1 && i == first_param_op_ && !first_rows_.empty()) {
           // db first: it sits in the bucket of the first chunk issued
-          check(gt_reduce(ctx_, dtype_, GT_SUM, g, gr + op.b_off * es_, 1, op.M, op.N));
+          if (!op.db_upstream) check(gt_reduce(ctx_, dtype_, GT_SUM, g, gr + op.b_off * es_, 1, op.M, op.N));
           for (size_t j = first_rows_.size() - 1; j-- > 0;) {
             check(gt_linear_bwd_weight_rows(ctx_, dtype_, op.in, g, gr + op.w_off * es_, op.M, op.K, op.N,
                                             first_rows_[j], first_rows_[j + 1]));
             issue_ready_buckets(op.w_off + first_rows_[j] * op.K);
           }
         } else {
-          check(gt_linear_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, op.M, op.K,
-                                     op.N));
+          check(gt_linear_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_,
+                                     op.db_upstream ? nullptr : gr + op.b_off * es_, op.M, op.K, op.N));
           if (world_ > 1) issue_ready_buckets(op.w_off);
         }
         if (op.needs_dx) {
@@ -428,8 +432,16 @@ void Model::backward(bool join) {
           // into the GEMM epilogue when the producer is a Linear/Conv/act.
           const Op* src = op.src >= 0 ? &ops_[op.src] : nullptr;
           bool fuse = src && src->kind != Op::POOL && src->act != GT_ACT_NONE;
-          if (fuse && src->bits)
+          // the producer's bias gradient from this dX (its output gradient)
+          void* db_prev = src && src->kind == Op::LINEAR && src->db_upstream ? gr + src->b_off * es_ : nullptr;
+          if (fuse && src->bits && db_prev)
+            check(gt_linear_bwd_data_bits_db(ctx_, dtype_, g, p + op.w_off * es_, src->bits, spare, db_prev, op.M,
+                                             op.K, op.N));
+          else if (fuse && src->bits)
             check(gt_linear_bwd_data_bits(ctx_, dtype_, g, p + op.w_off * es_, src->bits, spare, op.M, op.K, op.N));
+          else if (db_prev)
+            check(gt_linear_bwd_data_db(ctx_, dtype_, g, p + op.w_off * es_, fuse ? op.in : nullptr,
+                                        fuse ? src->act : GT_ACT_NONE, spare, db_prev, op.M, op.K, op.N));
           else
             check(gt_linear_bwd_data(ctx_, dtype_, g, p + op.w_off * es_, fuse ? op.in : nullptr,
                                      fuse ? src->act : GT_ACT_NONE, spare, op.M, op.K, op.N));

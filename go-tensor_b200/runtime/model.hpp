@@ -86,6 +86,10 @@ struct Op {
   int src = -1;                 // op that produced this op's input, identities skipped (-1: the batch)
   uint32_t* bits = nullptr;     // LINEAR + ReLU, float32: bit mask of the output for the next Linear's dX
   void* cols = nullptr;         // CONV: the forward's im2col columns, reused by the backward
+  // LINEAR: the bias gradient is written by the op that writes this op's
+  // output gradient (the loss for the last layer, the next Linear's dX
+  // otherwise), as the column sums of that gradient.
+  bool db_upstream = false;
 };
 
 class Model {

@@ -183,6 +183,17 @@ GT_API char* gt_linear_fwd_bits(gt_ctx* ctx, int dtype, const void* x, const voi
  * the bit mask of y_prev (M, K): the same result bit for bit. */
 GT_API char* gt_linear_bwd_data_bits(gt_ctx* ctx, int dtype, const void* dy, const void* w, const uint32_t* bits,
                                      void* dx, int64_t M, int64_t K, int64_t N);
+/* gt_linear_bwd_data and gt_linear_bwd_data_bits that also write db_prev (K)
+ * = the column sums of dx: the bias gradient of the Linear that produced this
+ * layer's input (the sumTo of its bias, tensor/ops.go:418-433), which
+ * follows from dx alone. On the float32 tensor-core path the GEMM's epilogue
+ * sums each 32-row block while storing it and one small kernel adds the
+ * blocks, so dx is not read again; elsewhere a reduction over dx follows.
+ * No counterpart in the reference (whose backward reduces dy per layer). */
+GT_API char* gt_linear_bwd_data_db(gt_ctx* ctx, int dtype, const void* dy, const void* w, const void* y_prev,
+                                   int act_prev, void* dx, void* db_prev, int64_t M, int64_t K, int64_t N);
+GT_API char* gt_linear_bwd_data_bits_db(gt_ctx* ctx, int dtype, const void* dy, const void* w, const uint32_t* bits,
+                                        void* dx, void* db_prev, int64_t M, int64_t K, int64_t N);
 /* dw (N, K) = dy (M, N)^T @ x (M, K); db (N) = sum over rows of dy (NULL: skip).
  * Replaces the MatMul backward for the weight (tensor/ops.go:324-326), the
  * Permute backward of W.T() and sumTo for the bias (tensor/ops.go:418-433). */
@@ -269,6 +280,14 @@ GT_API char* gt_bce_fwd_bwd(gt_ctx* ctx, int dtype, const void* pred, const void
  * Labels outside [0, C) set *bad_label (device int32, may be NULL) to 1. */
 GT_API char* gt_xent_fwd_bwd(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
                       int64_t C, void* loss, void* dlogits, int32_t* bad_label);
+
+/* gt_xent_fwd_bwd that also writes db (C) = the column sums of dlogits: the
+ * bias gradient of the Linear that produced the logits (its sumTo over the
+ * batch, tensor/ops.go:418-433), summed in the same pass that writes the
+ * gradient (rows of up to 1024 classes; wider rows add a reduction over
+ * dlogits). dlogits and db must not be NULL. No counterpart in the reference. */
+GT_API char* gt_xent_fwd_bwd_db(gt_ctx* ctx, int dtype, const void* logits, const int32_t* labels, int64_t B,
+                                int64_t C, void* loss, void* dlogits, void* db, int32_t* bad_label);
 
 /* Largest batch gt_xent_fwd_bwd_noalloc accepts: its per-row loss terms live
  * in a fixed 2 MiB device buffer inside the library (8 bytes per row). */

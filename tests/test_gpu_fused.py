@@ -457,3 +457,66 @@ def test_adam_device_step_counter():
     check(lib().gt_download(ctx(), cnt.ctypes.data, step, 8))
     assert cnt[0] == 3
     cuda_backend().ctx.release(step)
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("bc", [(8192, 1000), (64, 10), (1000, 33), (300, 1500)])
+def test_xent_db_is_the_column_sum_of_dlogits(dt, npdt, tol, bc):
+    """gt_xent_fwd_bwd_db: the loss and dlogits of gt_xent_fwd_bwd, bit for
+    bit, and db = the column sums of dlogits, the last Linear's bias gradient
+    (sumTo over the batch, tensor/ops.go:418-433); rows wider than 1024
+    classes take the reduction path."""
+    B, C = bc
+    rng = np.random.default_rng(B + 3 * C)
+    x = (rng.standard_normal((B, C)) * 3).astype(npdt)
+    y = rng.integers(0, C, B).astype(np.int32)
+    labels = cuda_backend().ctx.alloc(4 * B)
+    check(lib().gt_upload(ctx(), labels, y.ctypes.data, 4 * B))
+    xd = dev(x)
+    loss1, dl1, loss2, dl2, db = new(1, dt), new(B * C, dt), new(1, dt), new(B * C, dt), new(C, dt)
+    check(lib().gt_xent_fwd_bwd(ctx(), dt, xd.ptr, labels, B, C, loss1.ptr, dl1.ptr, None))
+    check(lib().gt_xent_fwd_bwd_db(ctx(), dt, xd.ptr, labels, B, C, loss2.ptr, dl2.ptr, db.ptr, None))
+    assert_bits(host(loss2), host(loss1), "loss")
+    dl = host(dl1)
+    assert_bits(host(dl2), dl, "dlogits")
+    cpu = T.backend_for(T.CPU)
+    want = cpu.ToHost(cpu.Reduce(0, cpu.FromHost(dl), 1, B, C))
+    assert_close(host(db), want, tol, "db")
+    cuda_backend().ctx.release(labels)
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("mkn", [(8192, 4096, 1000), (1024, 4096, 4096), (256, 128, 10), (300, 36, 132)])
+@pytest.mark.parametrize("act", [1, 2])
+def test_linear_bwd_data_db_is_the_column_sum_of_dx(dt, npdt, tol, mkn, act):
+    """gt_linear_bwd_data_db and gt_linear_bwd_data_bits_db: dx of the entry
+    points they extend, bit for bit, and db_prev = the column sums of dx (the
+    bias gradient of the layer before). The shapes take the tensor-core path
+    whole and K-split (the column sums then come from the split reduction)
+    and the SIMT path."""
+    M, K, N = mkn  # dx (M, K) = dy (M, N) @ w (N, K) * act'(y_prev)
+    rng = np.random.default_rng(M + K + N + act)
+    y_prev = rng.standard_normal((M, K)).astype(npdt)
+    if act == 1:
+        y_prev = np.maximum(y_prev, 0)
+    else:
+        y_prev = np.tanh(y_prev).astype(npdt)
+    w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(npdt)
+    dy = (rng.standard_normal((M, N)) / M).astype(npdt)
+    dyd, wd, yd = dev(dy), dev(w), dev(y_prev)
+    dx1, dx2, db = new(M * K, dt), new(M * K, dt), new(K, dt)
+    check(lib().gt_linear_bwd_data(ctx(), dt, dyd.ptr, wd.ptr, yd.ptr, act, dx1.ptr, M, K, N))
+    check(lib().gt_linear_bwd_data_db(ctx(), dt, dyd.ptr, wd.ptr, yd.ptr, act, dx2.ptr, db.ptr, M, K, N))
+    dx = host(dx1)
+    assert_bits(host(dx2), dx, "dx")
+    cpu = T.backend_for(T.CPU)
+    want = cpu.ToHost(cpu.Reduce(0, cpu.FromHost(dx), 1, M, K))
+    assert_close(host(db), want, tol, "db_prev")
+    if act == 1:  # the same through the ReLU bit mask
+        ldw = (M + 31) // 32
+        bits = new(K * ldw, T.Float32)
+        check(lib().gt_relu_bits(ctx(), dt, yd.ptr, bits.ptr, M, K))
+        dx3, db3 = new(M * K, dt), new(K, dt)
+        check(lib().gt_linear_bwd_data_bits_db(ctx(), dt, dyd.ptr, wd.ptr, bits.ptr, dx3.ptr, db3.ptr, M, K, N))
+        assert_bits(host(dx3), dx, "dx through the bit mask")
+        assert_close(host(db3), want, tol, "db_prev through the bit mask")
