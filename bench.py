@@ -625,6 +625,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="wide_mlp")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="global batch override (a small case of the workload, for profiling); default: the config's")
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -641,6 +643,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.batch:
+        WORKLOADS[args.workload] = dict(WORKLOADS[args.workload], batch=args.batch,
+                                        name=WORKLOADS[args.workload]["name"] + f"_batch{args.batch}")
     if args.impl == "reference":
         return run_reference(args)
     if args.gemm_only:

@@ -79,6 +79,8 @@ char* gt_init(int device, gt_ctx** out) {
   GT_CUDA(cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming));
   GT_CUDA(cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming));
   for (auto& e : ctx->marks) GT_CUDA(cudaEventCreate(&e));
+  GT_CUDA(cudaMalloc((void**)&ctx->adam_done, sizeof(unsigned int)));
+  GT_CUDA(cudaMemset(ctx->adam_done, 0, sizeof(unsigned int)));
   cudaDriverEntryPointQueryResult q;
   GT_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ctx->encode_tiled, cudaEnableDefault, &q));
   if (q != cudaDriverEntryPointSuccess) ctx->encode_tiled = nullptr;
@@ -97,6 +99,7 @@ char* gt_destroy(gt_ctx* ctx) {
   cudaEventDestroy(ctx->fork);
   cudaEventDestroy(ctx->join);
   for (auto& e : ctx->marks) cudaEventDestroy(e);
+  if (ctx->adam_done) cudaFree(ctx->adam_done);
   cudaStreamDestroy(ctx->stream);
   cudaStreamDestroy(ctx->comm_stream);
   cudaStreamDestroy(ctx->copy_stream);

@@ -123,6 +123,30 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN), (sizeof(T) == 4 && BM *
   }
 }
 
+// Small K (the input gradient of a classifier: K = its 10 classes): C = A
+// (M x K, row-major) @ B (K x N, row-major), a thread per four consecutive
+// columns of a row. B's row k is read as one 16-byte vector per thread
+// (coalesced), A(m, k) is the same for the warp's threads (broadcast), and
+// each output is the same FMA chain over k, in order, as gemm_simt_kernel's,
+// so the results are identical; the outputs leave as contiguous runs.
+template <typename T>
+__global__ void gemm_smallk_kernel(GemmShape s, const T* __restrict__ A, const T* __restrict__ B, Epi<T> epi) {
+  const int64_t qn = s.N / 4, total = s.M * qn;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = u / qn, n = 4 * (u - m * qn);
+    T acc[4] = {(T)0, (T)0, (T)0, (T)0};
+    const T* a = A + m * s.lda;
+    for (int64_t k = 0; k < s.K; k++) {
+      const T av = __ldg(a + k);
+      const T* b = B + k * s.ldb + n;
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[j] = fma(av, __ldg(b + j), acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) epi.store(m, n + j, acc[j]);
+  }
+}
+
 // out(m, n) = epilogue(sum of the splits' partials in split order).
 template <typename T>
 __global__ void simt_split_reduce_kernel(const T* __restrict__ ws, int splits, int64_t M, int64_t N, Epi<T> epi) {
@@ -351,6 +375,14 @@ static char* f64_main(gt_ctx* ctx, const GemmShape& s, const double* A, const do
 template <typename T>
 char* gemm_simt(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>& epi) {
   if (s.M <= 0 || s.N <= 0) return nullptr;
+  // K of a few classes over a wide output (row-major operands, N a multiple
+  // of 4): the output is the cost, written in contiguous runs
+  if (s.K <= 32 && !s.trans_a && !s.trans_b && s.N % 4 == 0 && s.ldb % 4 == 0 && s.M * s.N >= 4096 &&
+      epi.nchw_L == 0 && !epi.col_major) {
+    gemm_smallk_kernel<T><<<grid_for(ctx, s.M * s.N / 4, 256), 256, 0, ctx->stream>>>(s, A, B, epi);
+    GT_LAUNCH_CHECK();
+    return nullptr;
+  }
   // float64 outputs of at least 128 x 128 with K long enough to amortise the
   // one-CTA-per-SM epilogue go to the tensor-core kernel.
   if constexpr (sizeof(T) == 8)

@@ -28,6 +28,7 @@ struct gt_ctx {
   cudaEvent_t marks[8] = {};                   // gt_mark timing points
   struct gt_gemm_timer* gemm_timer = nullptr;  // gt_gemm_timer_start .. _stop
   int gemm_sm_reserve = 0;  // SMs the GEMM kernels leave free (gt_set_gemm_sm_reserve)
+  unsigned int* adam_done = nullptr;  // 4 bytes of device memory: the Adam kernel's finished-block count
 };
 
 namespace gt {

@@ -78,10 +78,16 @@ __device__ __forceinline__ void adam_one(T& p, T g, T& m, T& v, const AdamScalar
   p = sub_rn(p, div_rn(mul_rn(m, lr_bc1), denom));
 }
 
+// One pass over the parameters: each thread loads two groups of W elements of
+// p, g, m, v before updating either (more loads in flight per thread). With
+// DEV_STEP the bias corrections come from the device-side step counter, read
+// once per block; the last block to finish advances the counter (every block
+// has read it by then: a block counts itself done only after reading), so a
+// captured graph replays the update with no second kernel.
 template <typename T, int W, bool DEV_STEP>
 __global__ void adam_kernel(T* __restrict__ p, const T* __restrict__ g, T* __restrict__ m, T* __restrict__ v,
-                            int64_t n, AdamScalars<T> s, T inv_bc2, T lr_bc1, const int64_t* step_dev, double lr,
-                            double beta1, double beta2) {
+                            int64_t n, AdamScalars<T> s, T inv_bc2, T lr_bc1, int64_t* step_dev,
+                            unsigned int* blocks_done, double lr, double beta1, double beta2) {
   if (DEV_STEP) {  // bias corrections from the device-side step counter, in float64, once per block
     __shared__ T sc[2];
     if (threadIdx.x == 0) {
@@ -95,24 +101,45 @@ __global__ void adam_kernel(T* __restrict__ p, const T* __restrict__ g, T* __res
     lr_bc1 = sc[1];
   }
   const int64_t nv = n / W;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
-    Pack<T, W> pp = reinterpret_cast<const Pack<T, W>*>(p)[i];
-    Pack<T, W> gg = reinterpret_cast<const Pack<T, W>*>(g)[i];
-    Pack<T, W> mm = reinterpret_cast<const Pack<T, W>*>(m)[i];
-    Pack<T, W> vv = reinterpret_cast<const Pack<T, W>*>(v)[i];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  using P = Pack<T, W>;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += 2 * stride) {
+    const int64_t i2 = i + stride;
+    const bool two = i2 < nv;
+    P pp[2], gg[2], mm[2], vv[2];
+    pp[0] = reinterpret_cast<const P*>(p)[i], gg[0] = reinterpret_cast<const P*>(g)[i];
+    mm[0] = reinterpret_cast<const P*>(m)[i], vv[0] = reinterpret_cast<const P*>(v)[i];
+    if (two) {
+      pp[1] = reinterpret_cast<const P*>(p)[i2], gg[1] = reinterpret_cast<const P*>(g)[i2];
+      mm[1] = reinterpret_cast<const P*>(m)[i2], vv[1] = reinterpret_cast<const P*>(v)[i2];
+    }
 #pragma unroll
-    for (int j = 0; j < W; j++) adam_one(pp.v[j], gg.v[j], mm.v[j], vv.v[j], s, inv_bc2, lr_bc1);
-    reinterpret_cast<Pack<T, W>*>(p)[i] = pp;
-    reinterpret_cast<Pack<T, W>*>(m)[i] = mm;
-    reinterpret_cast<Pack<T, W>*>(v)[i] = vv;
+    for (int u = 0; u < 2; u++) {
+      if (u == 1 && !two) break;
+      const int64_t k = u ? i2 : i;
+#pragma unroll
+      for (int j = 0; j < W; j++) adam_one(pp[u].v[j], gg[u].v[j], mm[u].v[j], vv[u].v[j], s, inv_bc2, lr_bc1);
+      reinterpret_cast<P*>(p)[k] = pp[u];
+      reinterpret_cast<P*>(m)[k] = mm[u];
+      reinterpret_cast<P*>(v)[k] = vv[u];
+    }
   }
-  for (int64_t i = nv * W + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = nv * W + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     T pv = p[i], mv = m[i], vv = v[i];
     adam_one(pv, g[i], mv, vv, s, inv_bc2, lr_bc1);
     p[i] = pv;
     m[i] = mv;
     v[i] = vv;
+  }
+  if (DEV_STEP) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();  // this block's read of the step is ordered before its count
+      if (atomicAdd(blocks_done, 1u) == gridDim.x - 1) {  // the last block: everyone has read the step
+        *step_dev += 1;
+        *blocks_done = 0;
+      }
+    }
   }
 }
 
@@ -121,6 +148,16 @@ static bool all_aligned16(const void* a, const void* b, const void* c, const voi
 }
 
 __global__ void step_incr_kernel(int64_t* step) { *step += 1; }
+
+// Threads for an elementwise pass of n elements, W per thread, two groups per
+// thread: whole blocks of 256, at most the SMs' resident threads.
+static int adam_grid(const gt_ctx* ctx, int64_t n, int W) { return grid_for(ctx, n, 256, 2 * W); }
+
+static char* adam_done_counter(gt_ctx* ctx, unsigned int** out) {
+  if (!ctx->adam_done) return errorf("gt_adam_step_dev: the context has no block counter");
+  *out = ctx->adam_done;
+  return nullptr;
+}
 
 template <typename T>
 static AdamScalars<T> adam_scalars(const gt_adam_cfg& c) {
@@ -182,13 +219,13 @@ char* gt_adam_step(gt_ctx* ctx, int dtype, void* p, const void* g, void* m, void
   GT_DISPATCH(dtype, {
     constexpr int W = 16 / sizeof(T);
     if (all_aligned16(p, g, m, v))
-      adam_kernel<T, W, false><<<grid_for(ctx, n, 256, W), 256, 0, ctx->stream>>>(
-          (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)(1.0 / bc2), (T)(c.lr / bc1), nullptr, c.lr,
-          c.beta1, c.beta2);
+      adam_kernel<T, W, false><<<adam_grid(ctx, n, W), 256, 0, ctx->stream>>>(
+          (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)(1.0 / bc2), (T)(c.lr / bc1), nullptr, nullptr,
+          c.lr, c.beta1, c.beta2);
     else
-      adam_kernel<T, 1, false><<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(
-          (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)(1.0 / bc2), (T)(c.lr / bc1), nullptr, c.lr,
-          c.beta1, c.beta2);
+      adam_kernel<T, 1, false><<<adam_grid(ctx, n, 1), 256, 0, ctx->stream>>>(
+          (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)(1.0 / bc2), (T)(c.lr / bc1), nullptr, nullptr,
+          c.lr, c.beta1, c.beta2);
   });
   GT_LAUNCH_CHECK();
   return nullptr;
@@ -200,19 +237,27 @@ char* gt_adam_step_dev(gt_ctx* ctx, int dtype, void* p, const void* g, void* m, 
   GT_CHECK_DTYPE(dtype);
   if (!cfg_in || !step_dev) return errorf("gt_adam_step_dev: null argument");
   gt_adam_cfg c = adam_defaults(cfg_in);
-  if (n > 0) {
-    GT_DISPATCH(dtype, {
-      constexpr int W = 16 / sizeof(T);
-      if (all_aligned16(p, g, m, v))
-        adam_kernel<T, W, true><<<grid_for(ctx, n, 256, W), 256, 0, ctx->stream>>>(
-            (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)0, (T)0, step_dev, c.lr, c.beta1, c.beta2);
-      else
-        adam_kernel<T, 1, true><<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(
-            (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)0, (T)0, step_dev, c.lr, c.beta1, c.beta2);
-    });
+  if (n <= 0) {
+    step_incr_kernel<<<1, 1, 0, ctx->stream>>>(step_dev);
     GT_LAUNCH_CHECK();
+    return nullptr;
   }
-  step_incr_kernel<<<1, 1, 0, ctx->stream>>>(step_dev);
+  // blocks_done: a counter the kernel's last block resets to zero, so it
+  // starts every launch at zero; one per context, shared by every update on
+  // its stream (which run one after another).
+  unsigned int* done = nullptr;
+  GT_TRY(adam_done_counter(ctx, &done));
+  GT_DISPATCH(dtype, {
+    constexpr int W = 16 / sizeof(T);
+    if (all_aligned16(p, g, m, v))
+      adam_kernel<T, W, true><<<adam_grid(ctx, n, W), 256, 0, ctx->stream>>>(
+          (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)0, (T)0, step_dev, done, c.lr, c.beta1,
+          c.beta2);
+    else
+      adam_kernel<T, 1, true><<<adam_grid(ctx, n, 1), 256, 0, ctx->stream>>>(
+          (T*)p, (const T*)g, (T*)m, (T*)v, n, adam_scalars<T>(c), (T)0, (T)0, step_dev, done, c.lr, c.beta1,
+          c.beta2);
+  });
   GT_LAUNCH_CHECK();
   return nullptr;
 }
