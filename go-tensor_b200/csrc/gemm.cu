@@ -138,15 +138,6 @@ __global__ void relu_bits_kernel(const T* __restrict__ y, uint32_t* __restrict__
   }
 }
 
-// db[n] = sum over the 32-row blocks of ws[b * N + n], blocks in order.
-__global__ void colsum_finish_kernel(const float* __restrict__ ws, int64_t blocks, int64_t N, float* __restrict__ db) {
-  for (int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
-    float acc = ws[n];
-    for (int64_t b = 1; b < blocks; b++) acc = __fadd_rn(acc, ws[b * N + n]);
-    db[n] = acc;
-  }
-}
-
 // dx = the GEMM of s with epilogue e (a Linear's input gradient, M x K), and
 // db_prev (K) = its column sums: the bias gradient of the Linear that
 // produced this layer's input (sumTo over the batch, tensor/ops.go:418-433).
@@ -165,11 +156,11 @@ static char* bwd_data_with_db(gt_ctx* ctx, int dtype, const GemmShape& s, const 
     char* err = gemm<float>(ctx, s, (const float*)dy, (const float*)w, e);
     const bool fused = !err && g_gemm_taken == 2;
     if (fused) {
-      colsum_finish_kernel<<<grid_for(ctx, K, 256), 256, 0, ctx->stream>>>((const float*)ws, blocks, K,
-                                                                          (float*)db_prev);
+      column_sums_kernel<float><<<(unsigned)ceil_div(K, 32), 1024, 0, ctx->stream>>>((const float*)ws, blocks, K,
+                                                                                     (float*)db_prev);
       count_launch();
       cudaError_t ce = cudaGetLastError();
-      if (ce != cudaSuccess) err = cuda_error(ce, "colsum_finish_kernel launch", __FILE__, __LINE__);
+      if (ce != cudaSuccess) err = cuda_error(ce, "column_sums_kernel launch", __FILE__, __LINE__);
     }
     release(ctx, ws);
     if (err || fused) return err;

@@ -132,6 +132,39 @@ __device__ __forceinline__ T go_max(T a, T b) {
   return a > b ? a : b;
 }
 
+// out[c] = sum over r of part[r * cols + c], for cols columns and rows partial
+// rows, in a fixed order (deterministic): a block of 32 warps takes 32
+// consecutive columns; warp w adds rows [w * rows / 32, (w + 1) * rows / 32)
+// in order (each load a coalesced 128-byte row), and the 32 warp sums are
+// then added in warp order. Launch with ceil(cols / 32) blocks of 1024
+// threads.
+template <typename T>
+__global__ void __launch_bounds__(1024) column_sums_kernel(const T* __restrict__ part, int64_t rows, int64_t cols,
+                                                           T* __restrict__ out) {
+  __shared__ T ws[32][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  const int64_t r0 = w * rows / 32, r1 = (w + 1) * rows / 32;
+  T acc = (T)0;
+  if (c < cols) {
+    if (r0 < r1) acc = part[r0 * cols + c];
+#pragma unroll 8
+    for (int64_t r = r0 + 1; r < r1; r++) acc = acc + part[r * cols + c];
+  }
+  ws[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && c < cols) {
+    T s = (T)0;
+    bool first = true;
+    for (int k = 0; k < 32; k++)
+      if (k * rows / 32 < (k + 1) * rows / 32) {
+        s = first ? ws[k][lane] : s + ws[k][lane];
+        first = false;
+      }
+    out[c] = s;
+  }
+}
+
 // Forward activations, evaluated like go-tensor's CPU backend: ReLU is Go's
 // max(x, 0); Tanh and Sigmoid are computed in float64 then rounded to T
 // (internal/cpu/cpu.go:110-135).

@@ -85,7 +85,7 @@ __global__ void xent_rows_kernel(const T* __restrict__ x, const int32_t* __restr
 // With COLS (and dx), each lane also sums the gradient values it writes, per
 // column, over the rows of its warp; the block's warps add theirs in warp
 // order and write one partial row per block to col_part (gridDim.x x C), which
-// xent_cols_kernel sums over the blocks: the column sums of dlogits, the bias
+// column_sums_kernel adds over the blocks: the column sums of dlogits, the bias
 // gradient of the Linear that produced the logits, without a second pass
 // over dlogits.
 template <typename T, int NPL, bool COLS = false>
@@ -172,19 +172,111 @@ __global__ void xent_rows_reg_kernel(const T* __restrict__ x, const int32_t* __r
   }
 }
 
-// db[j] = sum over the blocks of col_part[b][j], in block order.
-template <typename T>
-__global__ void xent_cols_kernel(const T* __restrict__ col_part, int blocks, int C, T* __restrict__ db) {
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < C; j += gridDim.x * blockDim.x) {
-    T acc = col_part[j];
-    for (int b = 1; b < blocks; b++) acc = add_rn(acc, col_part[(int64_t)b * C + j]);
-    db[j] = acc;
+// Rows of 129 to 128 * VPT classes: a block of 128 threads per row (rows
+// blockIdx.x, + gridDim.x, ...), thread t holding elements t, t + 128, ...:
+// more rows in flight than a warp per row with 32 values in registers. One
+// float64 exp per element as above; the sum adds each thread's values in
+// order, then the warp butterfly, then the four warps in order. With COLS
+// each thread also sums, per column, the gradient values of its block's rows
+// and writes them as the block's partial row of col_part.
+template <typename T, int VPT, bool COLS>
+__global__ void __launch_bounds__(128) xent_rows_blk_kernel(const T* __restrict__ x, const int32_t* __restrict__ labels,
+                                                            int64_t B, int C, T c, T* __restrict__ row_terms,
+                                                            T* __restrict__ dx, int32_t* bad_label,
+                                                            T* __restrict__ col_part) {
+  __shared__ T red[4];
+  __shared__ T pick;
+  __shared__ int nonfin;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  T cs[COLS ? VPT : 1];
+#pragma unroll
+  for (int u = 0; u < (COLS ? VPT : 1); u++) cs[u] = (T)0;
+  // the next row's values are loaded while this row is computed
+  T nv[VPT];
+  if (blockIdx.x < B) {
+#pragma unroll
+    for (int u = 0; u < VPT; u++) {
+      const int j = tid + 128 * u;
+      nv[u] = j < C ? __ldg(x + (int64_t)blockIdx.x * C + j) : (T)(-INFINITY);
+    }
+  }
+  for (int64_t i = blockIdx.x; i < B; i += gridDim.x) {
+    const int32_t y = labels[i];
+    const bool bad = y < 0 || y >= C;
+    if (bad && tid == 0 && bad_label) *bad_label = 1;
+    T v[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; u++) v[u] = nv[u];
+    if (i + gridDim.x < B) {
+#pragma unroll
+      for (int u = 0; u < VPT; u++) {
+        const int j = tid + 128 * u;
+        nv[u] = j < C ? __ldg(x + (i + gridDim.x) * C + j) : (T)(-INFINITY);
+      }
+    }
+    T m = (T)(-INFINITY);
+#pragma unroll
+    for (int u = 0; u < VPT; u++)
+      if (tid + 128 * u < C) m = go_max(m, v[u]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = go_max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) red[w] = m;
+    if (tid == 0) nonfin = 0, pick = (T)0;
+    __syncthreads();
+    m = go_max(go_max(red[0], red[1]), go_max(red[2], red[3]));
+    __syncthreads();  // red is reused below
+    T S = (T)0;
+    bool nf = false;
+#pragma unroll
+    for (int u = 0; u < VPT; u++) {
+      const int j = tid + 128 * u;
+      if (j < C) {
+        const T sv = sub_rn(v[u], m);
+        if (j == y) pick = sv;  // the label's shifted logit (one thread)
+        else if (!isfinite(sv)) nf = true;
+        v[u] = (T)exp((double)sv);
+        S = add_rn(S, v[u]);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) S = add_rn(S, __shfl_xor_sync(0xffffffffu, S, off));
+    if (lane == 0) red[w] = S;
+    if (__any_sync(0xffffffffu, nf) && lane == 0) nonfin = 1;
+    __syncthreads();
+    S = add_rn(add_rn(add_rn(red[0], red[1]), red[2]), red[3]);
+    const T Lse = (T)log((double)S);
+    const T q = div_rn(c, S);
+    if (dx) {
+      T* dr = dx + i * C;
+#pragma unroll
+      for (int u = 0; u < VPT; u++) {
+        const int j = tid + 128 * u;
+        if (j < C) {
+          const T g = mul_rn(q, v[u]);
+          const T d = j == y ? add_rn(-c, g) : g;
+          dr[j] = d;
+          if constexpr (COLS) cs[u] = add_rn(cs[u], d);
+        }
+      }
+    }
+    if (tid == 0) {
+      const bool nonfinite = nonfin || (!isfinite(Lse) && C > 1);
+      row_terms[i] = (nonfinite || bad) ? (T)NAN : add_rn(sub_rn(pick, Lse), (T)0);
+    }
+    __syncthreads();  // red, pick and nonfin are rewritten by the next row
+  }
+  if constexpr (COLS) {
+#pragma unroll
+    for (int u = 0; u < VPT; u++) {
+      const int j = tid + 128 * u;
+      if (j < C) col_part[(int64_t)blockIdx.x * C + j] = cs[u];
+    }
   }
 }
 
 // The row kernel with column sums for rows of at most 1024 classes (a block
-// of 4 warps, at most 2 blocks per SM so that the partial rows stay few);
-// returns false for wider rows.
+// of 4 warps, at most 8 blocks per SM: one partial row per block, which
+// column_sums_kernel adds); returns false for wider rows.
 template <typename T>
 static bool xent_rows_cols_launch(gt_ctx* ctx, const T* x, const int32_t* labels, int64_t B, int64_t C, T c,
                                   T* terms, T* dx, int32_t* bad, T* col_part, int grid) {
@@ -194,18 +286,21 @@ static bool xent_rows_cols_launch(gt_ctx* ctx, const T* x, const int32_t* labels
   else if (C <= 128)
     xent_rows_reg_kernel<T, 4, true><<<grid, 128, sm, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad, col_part);
   else if (C <= 512)
-    xent_rows_reg_kernel<T, 16, true><<<grid, 128, sm, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad,
-                                                                       col_part);
+    xent_rows_blk_kernel<T, 4, true><<<grid, 128, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad, col_part);
   else if (C <= 1024)
-    xent_rows_reg_kernel<T, 32, true><<<grid, 128, sm, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad,
-                                                                       col_part);
+    xent_rows_blk_kernel<T, 8, true><<<grid, 128, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad, col_part);
   else
     return false;
   return true;
 }
 
-// Launches the row kernel that fits C: register rows up to 1024 classes,
-// else the streaming kernel.
+// Blocks for the block-per-row kernel: up to 16 per SM, the rows loop over them.
+static int xent_blk_grid(const gt_ctx* ctx, int64_t B) {
+  return (int)std::min<int64_t>(B, 16 * (int64_t)ctx->sm_count);
+}
+
+// Launches the row kernel that fits C: a warp per row up to 128 classes, a
+// block per row up to 1024, else the streaming kernel.
 template <typename T>
 static void xent_rows_launch(gt_ctx* ctx, const T* x, const int32_t* labels, int64_t B, int64_t C, T c, T* terms,
                              T* dx, int32_t* bad) {
@@ -215,9 +310,11 @@ static void xent_rows_launch(gt_ctx* ctx, const T* x, const int32_t* labels, int
   else if (C <= 128)
     xent_rows_reg_kernel<T, 4><<<grid, 256, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad);
   else if (C <= 512)
-    xent_rows_reg_kernel<T, 16><<<grid, 256, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad);
+    xent_rows_blk_kernel<T, 4, false><<<xent_blk_grid(ctx, B), 128, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms,
+                                                                                      dx, bad, nullptr);
   else if (C <= 1024)
-    xent_rows_reg_kernel<T, 32><<<grid, 256, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms, dx, bad);
+    xent_rows_blk_kernel<T, 8, false><<<xent_blk_grid(ctx, B), 128, 0, ctx->stream>>>(x, labels, B, (int)C, c, terms,
+                                                                                      dx, bad, nullptr);
   else
     xent_rows_kernel<T><<<grid, 256, 0, ctx->stream>>>(x, labels, B, C, c, terms, dx, bad);
 }
@@ -302,7 +399,8 @@ extern "C" char* gt_xent_fwd_bwd_db(gt_ctx* ctx, int dtype, const void* logits, 
     return gt_reduce(ctx, dtype, GT_SUM, dlogits, db, 1, B, C);
   }
   const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
-  const int grid = (int)std::min<int64_t>(ceil_div(B, 4), 2 * (int64_t)ctx->sm_count);
+  const int grid = C <= 128 ? (int)std::min<int64_t>(ceil_div(B, 4), 8 * (int64_t)ctx->sm_count)
+                            : xent_blk_grid(ctx, B);
   void *terms = nullptr, *part = nullptr;
   GT_TRY(scratch(ctx, B * es, &terms));
   char* err = scratch(ctx, (size_t)grid * C * es, &part);
@@ -312,7 +410,7 @@ extern "C" char* gt_xent_fwd_bwd_db(gt_ctx* ctx, int dtype, const void* logits, 
       xent_rows_cols_launch<T>(ctx, (const T*)logits, labels, B, C, c, (T*)terms, (T*)dlogits, bad_label, (T*)part,
                                grid);
       xent_sum_kernel<T><<<1, 1024, 0, ctx->stream>>>((const T*)terms, B, c, (T*)loss);
-      xent_cols_kernel<T><<<grid_for(ctx, C, 256), 256, 0, ctx->stream>>>((const T*)part, grid, (int)C, (T*)db);
+      column_sums_kernel<T><<<(unsigned)ceil_div(C, 32), 1024, 0, ctx->stream>>>((const T*)part, grid, C, (T*)db);
     });
     count_launch(3);
     cudaError_t e = cudaGetLastError();

@@ -273,6 +273,15 @@ void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t
       bits_.emplace_back(ctx_, (size_t)((src.M + 31) / 32) * (size_t)src.N * sizeof(uint32_t));
       src.bits = (uint32_t*)bits_.back().get();
     }
+  // Bias gradients computed where the output gradient is written: the last
+  // Linear's by the loss (its logits' gradient), a Linear whose output feeds
+  // another Linear's dX by that dX GEMM (its output gradient, with the
+  // activation's derivative already applied).
+  if (!ops_.empty() && ops_.back().kind == Op::LINEAR && ops_.back().act == GT_ACT_NONE)
+    ops_.back().db_upstream = true;
+  for (auto& op : ops_)
+    if (op.kind == Op::LINEAR && op.needs_dx && op.src >= 0 && ops_[op.src].kind == Op::LINEAR)
+      ops_[op.src].db_upstream = true;
   // A float64 conv keeps its forward's im2col columns for its backward; the
   // float32 convs are implicit GEMMs and keep none.
   for (auto& op : ops_) {
