@@ -328,6 +328,186 @@ static char* col2im_launch(gt_ctx* ctx, const T* cols, T* x, const gt_geom& g) {
   return nullptr;
 }
 
+
+// Weight and bias gradients of a convolution whose output went through
+// [ReLU ->] MaxPool2d with k x k windows at stride k that tile it exactly,
+// computed from the pooled gradient. The reference's output gradient is
+// MaxPool2dBackward of it (the pooled gradient at each window's first
+// maximum, zero elsewhere: tensor/conv.go:63-70, internal/cpu/linalg.go:
+// 169-191) times ReLU's Step factor (tensor/ops.go:110), and the weight
+// gradient sums it against the patches (tensor/conv.go:40-59). Only window
+// maxima carry a nonzero term, so pooled position q adds g_q * patch(p_q) to
+// dW and g_q to db, with p_q its window's maximum and g_q = grad_q *
+// Step(pooled_q). A zero term still counts when its patch value is infinite
+// or NaN (0 * inf = NaN), so an image holding a non-finite value takes every
+// window position, zeros included, as the dense sum does.
+//
+// One block per image. The zero-padded image is staged in shared memory;
+// warp w takes output channels w, w + 8, ...; lane l takes pooled positions
+// l, l + 32, ... and keeps CKK + 1 running sums (fused multiply-adds). The
+// warp adds its lanes' sums in lane order through shared memory and writes
+// the image's partials part_w[n][o * CKK + k] and part_b[n][o];
+// column_sums_kernel then adds the images in a fixed order.
+constexpr int kPoolWgradWarps = 8;
+
+template <typename T>
+__host__ __device__ constexpr size_t pool_wgrad_red_bytes(int nk) {
+  return (size_t)kPoolWgradWarps * (nk + 1) * 33 * sizeof(T);
+}
+// The patch offset table, padded to 16 bytes so that the image after it is
+// aligned for any T.
+__host__ __device__ constexpr size_t pool_wgrad_koff_bytes(int nk) { return ((size_t)nk * sizeof(int) + 15) / 16 * 16; }
+
+// KS = 3: 3 x 3 windows over at most NK / 9 channels, the patch offsets
+// computed in registers; KS = 0: any window, offsets from a shared table.
+template <typename T, int NK, int KS>
+__global__ void __launch_bounds__(32 * kPoolWgradWarps)
+    conv_wgrad_pool_kernel(const T* __restrict__ x, const T* __restrict__ grad, const uint8_t* __restrict__ idx,
+                           const T* __restrict__ pooled, int relu, int C, int H, int W, int KH, int KW, int stride,
+                           int pad, int kp, int PH, int PW, int O, T* __restrict__ part_w, T* __restrict__ part_b) {
+  extern __shared__ __align__(16) unsigned char pool_wgrad_smem[];
+  const int Hs = H + 2 * pad, Ws = W + 2 * pad, plane = Hs * Ws, KHW = KH * KW, CKK = C * KHW;
+  T* red = reinterpret_cast<T*>(pool_wgrad_smem);
+  int* koff = reinterpret_cast<int*>(pool_wgrad_smem + pool_wgrad_red_bytes<T>(NK));
+  T* xs = reinterpret_cast<T*>(pool_wgrad_smem + pool_wgrad_red_bytes<T>(NK) + pool_wgrad_koff_bytes(NK));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t n = blockIdx.x;
+  const T* xn = x + n * C * H * W;
+  bool bad = false;
+  for (int e = tid; e < C * plane; e += blockDim.x) {
+    const int c = e / plane, r = e - c * plane, hs = r / Ws, ws = r - hs * Ws, h = hs - pad, w = ws - pad;
+    const T v = (h >= 0 && h < H && w >= 0 && w < W) ? xn[((int64_t)c * H + h) * W + w] : (T)0;
+    bad |= !isfinite(v);
+    xs[e] = v;
+  }
+  for (int k = tid; k < NK; k += blockDim.x) {
+    int off = 0;
+    if (k < CKK) {
+      const int c = k / KHW, r = k - c * KHW, kh = r / KW, kw = r - kh * KW;
+      off = c * plane + kh * Ws + kw;
+    }
+    koff[k] = off;
+  }
+  const bool dense = __syncthreads_or(bad);
+  const int P = PH * PW, win = kp * kp;
+  T* rw = red + warp * (NK + 1) * 33;
+  for (int o = warp; o < O; o += kPoolWgradWarps) {
+    T acc[NK + 1];
+#pragma unroll
+    for (int k = 0; k <= NK; k++) acc[k] = (T)0;
+    const int64_t qbase = (n * O + o) * P;
+    for (int q = lane; q < P; q += 32) {
+      T g = grad[qbase + q];
+      if (relu) g = mul_rn(g, pooled[qbase + q] > (T)0 ? (T)1 : (T)0);
+      const int m = idx[qbase + q];
+      const int qh = q / PW, qw = q - qh * PW;
+      const int i0 = dense ? 0 : m, i1 = dense ? win : min(m + 1, win);  // an index past the window adds nothing
+      for (int i = i0; i < i1; i++) {
+        const T gi = i == m ? g : (T)0;
+        const int ih = i / kp, iw = i - ih * kp;
+        // the patch of output position (qh*kp + ih, qw*kp + iw), in the padded image
+        const T* xp = xs + (qh * kp + ih) * stride * Ws + (qw * kp + iw) * stride;
+        if constexpr (KS == 3) {
+#pragma unroll
+          for (int c = 0; c < NK / 9; c++)
+            if (c < C) {
+              const T* xc = xp + c * plane;
+#pragma unroll
+              for (int kh = 0; kh < 3; kh++)
+#pragma unroll
+                for (int kw = 0; kw < 3; kw++) acc[c * 9 + kh * 3 + kw] = fma(gi, xc[kh * Ws + kw], acc[c * 9 + kh * 3 + kw]);
+            }
+        } else {
+#pragma unroll
+          for (int k = 0; k < NK; k++)
+            if (k < CKK) acc[k] = fma(gi, xp[koff[k]], acc[k]);
+        }
+        acc[NK] = acc[NK] + gi;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k <= NK; k++) rw[k * 33 + lane] = acc[k];
+    __syncwarp();
+    for (int k = lane; k <= NK; k += 32) {
+      if (k < CKK || k == NK) {
+        T s = rw[k * 33];
+        for (int j = 1; j < 32; j++) s = s + rw[k * 33 + j];
+        if (k == NK)
+          part_b[n * O + o] = s;
+        else
+          part_w[(n * O + o) * CKK + k] = s;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Shared memory of conv_wgrad_pool_kernel: the lane-sum buffer, the patch
+// offset table and the padded image.
+template <typename T, int NK>
+static size_t pool_wgrad_smem_bytes(const gt_geom& g) {  // the same for both KS
+  return pool_wgrad_red_bytes<T>(NK) + pool_wgrad_koff_bytes(NK) +
+         (size_t)g.C * (g.H + 2 * g.pad) * (g.W + 2 * g.pad) * sizeof(T);
+}
+
+template <typename T, int NK, int KS>
+static char* pool_wgrad_launch(gt_ctx* ctx, const T* x, const T* grad, const uint8_t* idx, const T* pooled, int relu,
+                               const gt_geom& g, const gt_geom& pg, int64_t O, T* part_w, T* part_b) {
+  const size_t smem = pool_wgrad_smem_bytes<T, NK>(g);
+  static bool configured[64] = {};
+  int dev = 0;
+  GT_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !configured[dev]) {
+    GT_CUDA(cudaFuncSetAttribute(conv_wgrad_pool_kernel<T, NK, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024));
+    configured[dev] = true;
+  }
+  conv_wgrad_pool_kernel<T, NK, KS><<<(unsigned)g.N, 32 * kPoolWgradWarps, smem, ctx->stream>>>(
+      x, grad, idx, pooled, relu, (int)g.C, (int)g.H, (int)g.W, (int)g.KH, (int)g.KW, (int)g.stride, (int)g.pad,
+      (int)pg.KH, (int)pg.OH, (int)pg.OW, (int)O, part_w, part_b);
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+// The arguments of one gt_conv_bwd_weight_pool launch, and the choice of
+// kernel variant: 3 x 3 windows with the patch offsets in registers, or the
+// offset table for other windows.
+struct PoolWgradArgs {
+  gt_ctx* ctx;
+  int dtype, relu;
+  const void *x, *grad, *pooled;
+  const uint8_t* idx;
+  const gt_geom *g, *pg;
+  int64_t O;
+  void *part_w, *part_b;
+};
+
+template <typename T>
+static char* pool_wgrad_dispatch(const PoolWgradArgs& a) {
+  const int64_t ckk = a.g->C * a.g->KH * a.g->KW;
+  const bool k3 = a.g->KH == 3 && a.g->KW == 3;
+  const T *x = (const T*)a.x, *grad = (const T*)a.grad, *pooled = (const T*)a.pooled;
+  T *pw = (T*)a.part_w, *pb = (T*)a.part_b;
+  if (k3 && ckk <= 9) return pool_wgrad_launch<T, 9, 3>(a.ctx, x, grad, a.idx, pooled, a.relu, *a.g, *a.pg, a.O, pw, pb);
+  if (k3 && ckk <= 27)
+    return pool_wgrad_launch<T, 27, 3>(a.ctx, x, grad, a.idx, pooled, a.relu, *a.g, *a.pg, a.O, pw, pb);
+  if (ckk <= 16) return pool_wgrad_launch<T, 16, 0>(a.ctx, x, grad, a.idx, pooled, a.relu, *a.g, *a.pg, a.O, pw, pb);
+  return pool_wgrad_launch<T, 32, 0>(a.ctx, x, grad, a.idx, pooled, a.relu, *a.g, *a.pg, a.O, pw, pb);
+}
+
+// Whether gt_conv_bwd_weight_pool runs conv_wgrad_pool_kernel for these
+// geometries (otherwise it goes through the full-resolution gradient).
+static bool pool_wgrad_fits(const gt_geom& g, const gt_geom& pg, int64_t O, size_t es) {
+  const int64_t CKK = g.C * g.KH * g.KW;
+  if (pg.KH != pg.KW || pg.stride != pg.KH || pg.OH * pg.KH != pg.H || pg.OW * pg.KW != pg.W || pg.KH > 16) return false;
+  if (CKK > 32 || g.N > INT32_MAX || O > 65536) return false;
+  const int64_t padded = g.C * (g.H + 2 * g.pad) * (g.W + 2 * g.pad);
+  const size_t smem = (es == 8 ? pool_wgrad_red_bytes<double>(32) : pool_wgrad_red_bytes<float>(32)) +
+                      pool_wgrad_koff_bytes(32) +
+                      (size_t)padded * es;
+  return padded < INT32_MAX / 2 && smem <= 200 * 1024 && O * pg.OH * pg.OW < INT32_MAX / 2;
+}
+
 }  // namespace gt
 
 using namespace gt;
@@ -432,7 +612,7 @@ char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t
 // false if the geometry does not qualify.
 static char* conv_implicit(gt_ctx* ctx, const float* x, const float* w, int flip, int64_t rows, int64_t cols,
                            const float* bias, float* y, const gt_geom& g, int act, int64_t O_w, int64_t C_w,
-                           bool* done) {
+                           bool* done, uint8_t* pool_idx = nullptr) {
   *done = false;
   if ((act != GT_ACT_NONE && act != GT_ACT_RELU) || g.stride != 1) return nullptr;
   const int64_t pitch = (cols + 3) / 4 * 4, rows_pad = conv_weight_rows(rows);
@@ -445,14 +625,14 @@ static char* conv_implicit(gt_ctx* ctx, const float* x, const float* w, int flip
   count_launch();
   cudaError_t e = cudaGetLastError();
   char* err = e != cudaSuccess ? cuda_error(e, "split_weight_kernel launch", __FILE__, __LINE__)
-                               : conv_fwd_gemm(ctx, x, (const float*)ws, pitch, bias, y, g, rows, act, done);
+                               : conv_fwd_gemm(ctx, x, (const float*)ws, pitch, bias, y, g, rows, act, done, pool_idx);
   release(ctx, ws);
   return err;
 }
 
 static char* conv_fwd_implicit(gt_ctx* ctx, const float* x, const float* w, const float* bias, float* y,
-                               const gt_geom& g, int64_t O, int act, bool* done) {
-  return conv_implicit(ctx, x, w, 0, O, g.C * g.KH * g.KW, bias, y, g, act, O, g.C, done);
+                               const gt_geom& g, int64_t O, int act, bool* done, uint8_t* pool_idx = nullptr) {
+  return conv_implicit(ctx, x, w, 0, O, g.C * g.KH * g.KW, bias, y, g, act, O, g.C, done, pool_idx);
 }
 
 // The implicit-GEMM input gradient of a stride-1 convolution with a square
@@ -673,6 +853,89 @@ char* gt_conv_bwd(gt_ctx* ctx, int dtype, const void* cols, const void* dy, cons
   }
   release(ctx, dcols);
   release(ctx, dyp);
+  return err;
+}
+
+
+char* gt_conv_fwd_pool(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* pooled,
+                       uint8_t* idx, const gt_geom* g, const gt_geom* pg, int64_t O, int act) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_conv_fwd_pool"));
+  GT_TRY(check_geom(pg, "gt_conv_fwd_pool"));
+  if (O <= 0 || !pooled || !idx) return errorf("gt_conv_fwd_pool: bad arguments");
+  if (pg->N != g->N || pg->C != O || pg->H != g->OH || pg->W != g->OW || pg->pad != 0)
+    return errorf("gt_conv_fwd_pool: the pooling geometry does not take the convolution's output");
+  if (pg->stride < pg->KH || pg->stride < pg->KW) return errorf("gt_conv_fwd_pool: windows overlap");
+  if (g->N * O * pg->OH * pg->OW == 0) return nullptr;
+  // 2 x 2 windows at stride 2 that tile the output: pooled in the epilogue
+  if (dtype == GT_FLOAT32 && pg->KH == 2 && pg->KW == 2 && pg->stride == 2 && g->OH % 2 == 0 && g->OW % 2 == 0) {
+    bool done = false;
+    GT_TRY(conv_fwd_implicit(ctx, (const float*)x, (const float*)w, (const float*)bias, (float*)pooled, *g, O, act,
+                             &done, idx));
+    if (done) return nullptr;
+  }
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  void* y = nullptr;
+  GT_TRY(scratch(ctx, (size_t)(g->N * O * g->OH * g->OW) * es, &y));
+  char* err = gt_conv_fwd(ctx, dtype, x, w, bias, y, g, O, act);
+  if (!err) err = gt_maxpool_fwd_idx(ctx, dtype, y, pooled, idx, pg);
+  release(ctx, y);
+  return err;
+}
+
+char* gt_conv_bwd_weight_pool(gt_ctx* ctx, int dtype, const void* x, const void* grad, const uint8_t* idx,
+                              const void* pooled, int relu_mask, void* dw, void* db, const gt_geom* g,
+                              const gt_geom* pg, int64_t O) {
+  GT_ENTER(ctx);
+  GT_CHECK_DTYPE(dtype);
+  GT_TRY(check_geom(g, "gt_conv_bwd_weight_pool"));
+  GT_TRY(check_geom(pg, "gt_conv_bwd_weight_pool"));
+  if (O <= 0 || !dw || !grad || !idx) return errorf("gt_conv_bwd_weight_pool: bad arguments");
+  if (relu_mask && !pooled) return errorf("gt_conv_bwd_weight_pool: relu_mask needs the pooled output");
+  if (pg->N != g->N || pg->C != O || pg->H != g->OH || pg->W != g->OW || pg->pad != 0)
+    return errorf("gt_conv_bwd_weight_pool: the pooling geometry does not take the convolution's output");
+  if (pg->stride < pg->KH || pg->stride < pg->KW)
+    return errorf("gt_conv_bwd_weight_pool: windows overlap; use gt_maxpool_bwd and gt_conv_bwd_weight");
+  const int64_t CKK = g->C * g->KH * g->KW, NL = g->N * g->OH * g->OW;
+  const size_t es = dtype == GT_FLOAT64 ? 8 : 4;
+  if (NL == 0) {
+    GT_CUDA(cudaMemsetAsync(dw, 0, O * CKK * es, ctx->stream));
+    if (db) GT_CUDA(cudaMemsetAsync(db, 0, O * es, ctx->stream));
+    return nullptr;
+  }
+  if (!pool_wgrad_fits(*g, *pg, O, es)) {  // through the full-resolution output gradient
+    void* dy = nullptr;
+    GT_TRY(scratch(ctx, (size_t)(g->N * O * g->OH * g->OW) * es, &dy));
+    char* err = gt_maxpool_bwd_idx(ctx, dtype, grad, idx, pooled, relu_mask, dy, pg);
+    if (!err) err = gt_conv_bwd_weight(ctx, dtype, x, dy, dw, db, g, O);
+    release(ctx, dy);
+    return err;
+  }
+  void *part_w = nullptr, *part_b = nullptr;
+  GT_TRY(scratch(ctx, (size_t)(g->N * O * CKK) * es, &part_w));
+  char* err = scratch(ctx, (size_t)(g->N * O) * es, &part_b);
+  PoolWgradArgs a{ctx, dtype, relu_mask ? 1 : 0, x, grad, pooled, idx, g, pg, O, part_w, part_b};
+  auto run = [](void* p) -> char* {
+    const PoolWgradArgs& a = *(const PoolWgradArgs*)p;
+    return a.dtype == GT_FLOAT64 ? pool_wgrad_dispatch<double>(a) : pool_wgrad_dispatch<float>(a);
+  };
+  // timed like the GEMM it replaces: dW (O, CKK) over every output position
+  if (!err) err = timed_gemm_like(ctx, O, CKK, NL, 5, run, &a);
+  if (!err) {
+    GT_DISPATCH(dtype, {
+      column_sums_kernel<T><<<(unsigned)ceil_div(O * CKK, 32), 1024, 0, ctx->stream>>>((const T*)part_w, g->N,
+                                                                                      O * CKK, (T*)dw);
+      if (db)
+        column_sums_kernel<T><<<(unsigned)ceil_div(O, 32), 1024, 0, ctx->stream>>>((const T*)part_b, g->N, O,
+                                                                                  (T*)db);
+    });
+    count_launch(db ? 2 : 1);
+    cudaError_t ce = cudaGetLastError();
+    if (ce != cudaSuccess) err = cuda_error(ce, "column_sums_kernel launch", __FILE__, __LINE__);
+  }
+  release(ctx, part_w);
+  release(ctx, part_b);
   return err;
 }
 

@@ -59,14 +59,14 @@ static char* gemm_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const flo
 // records the convolution's own GEMM shape (M = positions or patch entries
 // without the bias-gradient row), so its flops are the algorithmic ones.
 char* conv_fwd_gemm(gt_ctx* ctx, const float* x, const float* w, int64_t w_pitch, const float* bias, float* y,
-                    const gt_geom& g, int64_t O, int act, bool* done) {
+                    const gt_geom& g, int64_t O, int act, bool* done, uint8_t* pool_idx) {
   *done = false;
   if (g_gemm_path == 1) return nullptr;  // SIMT pinned: the explicit path
   GemmShape ts{g.N * g.OH * g.OW, O, g.C * g.KH * g.KW, false, true, 0, 0};
   return timed_gemm(
       ctx, ts,
       [&] {
-        char* e = conv_fwd_tc(ctx, x, w, w_pitch, bias, y, g, O, act, done);
+        char* e = conv_fwd_tc(ctx, x, w, w_pitch, bias, y, g, O, act, done, pool_idx);
         if (*done) g_gemm_taken = 4;
         return e;
       },
@@ -86,6 +86,17 @@ char* conv_wgrad_gemm(gt_ctx* ctx, const float* x, const float* dy, float* dw, f
         return e;
       },
       done);
+}
+
+// A kernel that computes a GEMM's result by other means, timed and recorded
+// like the GEMMs under `path` (the fused pool-backward weight gradient).
+char* timed_gemm_like(gt_ctx* ctx, int64_t M, int64_t N, int64_t K, int path, char* (*run)(void*), void* arg) {
+  GemmShape ts{M, N, K, false, false, 0, 0};
+  return timed_gemm(ctx, ts, [&] {
+    char* e = run(arg);
+    g_gemm_taken = path;
+    return e;
+  });
 }
 
 template <>

@@ -52,6 +52,12 @@ struct Epi {
   // Linear as C, the column sums are the bias gradient of the layer before.
   T* colsum_ws = nullptr;
   int64_t ldcs = 0;
+  // With pos_major: 2 x 2 / stride-2 max pooling after the bias and
+  // activation (tcgen05 implicit convolution only). out receives the pooled
+  // (images, nchw_M, OH / 2, OW / 2) values and pool_idx the offset (kh * 2 +
+  // kw) of each window's first maximum; the convolution output itself is not
+  // stored.
+  uint8_t* pool_idx = nullptr;
 
   // The finished value of C(m, n): bias, activation, activation derivative.
   __device__ __forceinline__ T finish(int64_t m, int64_t n, T acc) const {
@@ -129,16 +135,25 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
 //     ReLU.
 //   conv_wgrad_tc: dw (O, C*KH*KW) and db (O, or NULL) from x and dy
 //     (N, O, OH, OW); needs OH * OW % 16 == 0.
+//   With pool_idx, conv_fwd_tc also applies 2 x 2 / stride-2 max pooling
+//     (MaxPool2d(2) after the convolution and its activation): y receives the
+//     pooled (N, O, OH / 2, OW / 2) values and pool_idx each window's
+//     first-max offset; needs even OH and OW.
 char* conv_fwd_tc(gt_ctx* ctx, const float* x, const float* ws, int64_t w_pitch, const float* bias, float* y,
-                  const gt_geom& g, int64_t O, int act, bool* done);
+                  const gt_geom& g, int64_t O, int act, bool* done, uint8_t* pool_idx = nullptr);
 char* conv_wgrad_tc(gt_ctx* ctx, const float* x, const float* dy, float* dw, float* db, const gt_geom& g, int64_t O,
                     bool* done);
 
 // The same through the GEMM launch timer (gemm.cu); the conv entry points call these.
 char* conv_fwd_gemm(gt_ctx* ctx, const float* x, const float* w, int64_t w_pitch, const float* bias, float* y,
-                    const gt_geom& g, int64_t O, int act, bool* done);
+                    const gt_geom& g, int64_t O, int act, bool* done, uint8_t* pool_idx = nullptr);
 char* conv_wgrad_gemm(gt_ctx* ctx, const float* x, const float* dy, float* dw, float* db, const gt_geom& g,
                       int64_t O, bool* done);
+
+// Runs run(arg) between the GEMM launch timer's events, recorded as an
+// M x N x K GEMM on `path`: kernels that compute a GEMM's result another way
+// (5: the fused pool-backward weight gradient, conv.cu).
+char* timed_gemm_like(gt_ctx* ctx, int64_t M, int64_t N, int64_t K, int path, char* (*run)(void*), void* arg);
 
 // Whether a float32 GEMM with this epilogue, if it runs on the tcgen05 path,
 // writes its column partial sums (Epi::colsum_ws).

@@ -153,6 +153,11 @@ struct Gather {
   int L = 1, KHW = 1, CKK = 0, ones_row = -1;
   int rp = 0, box_w = 0, box_h = 0, box_c = 0, box_n = 1;
   int bh = 1, rows_pi = 1;  // A_IM2COL_POS
+  // A_IM2COL_POS with 2 x 2 pooling fused into the epilogue (EK_NCHW_POOL):
+  // the CTA's rows are its positions in window order, row 4 w + k = offset k
+  // (kh * 2 + kw) of 2 x 2 window w, so a window's four values sit in four
+  // adjacent lanes. Set by the host for that kind; the kernel keys on EK.
+  int pool2 = 0;
   int r16 = 1, w16 = 16;    // A_IM2COL_CK
   uint32_t halo_bytes = 0;  // box_w * box_h * box_c * box_n * 4
   int b_lo_row = 0;         // B_SPLIT2: first row of the lo plane
@@ -396,13 +401,23 @@ __device__ __forceinline__ void split_store4(uint8_t* hi, uint8_t* lo, uint32_t 
 // swizzle); the warp's halo reads are 32 consecutive positions. Entries past
 // C*KH*KW are zero; taps in the padding read the halo's zero fill
 // (internal/cpu/linalg.go:130-139).
+template <bool POOL2>
 __device__ __forceinline__ void pos_rows(const Gather& g, int lane, int (&hb)[4]) {
   const int plane = g.box_w * g.box_h;
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const int r = lane + 32 * i;
-    const int n = r / g.rows_pi, rem = r - n * g.rows_pi;
-    const int oh = rem / g.OW, ow = rem - oh * g.OW;
+    int n, oh, ow;
+    if constexpr (POOL2) {
+      const int w = r >> 2, k = r & 3, per = g.rows_pi >> 2, pw = g.OW >> 1;
+      n = w / per;
+      const int rem = w - n * per, pr = rem / pw, pc = rem - pr * pw;
+      oh = 2 * pr + (k >> 1), ow = 2 * pc + (k & 1);
+    } else {
+      n = r / g.rows_pi;
+      const int rem = r - n * g.rows_pi;
+      oh = rem / g.OW, ow = rem - oh * g.OW;
+    }
     hb[i] = n * g.box_c * plane + oh * g.box_w + ow + g.rp - g.pad;
   }
 }
@@ -502,10 +517,17 @@ enum EpiKind : int {
   EK_NCHW_POS = 6,   // + bias[n] (optional), ReLU (optional), m = position, n = channel, stored NCHW:
                      // an implicit-GEMM convolution's forward pass or input gradient
   EK_COLMAJOR = 7,   // stored transposed, with the bias-gradient row: a convolution's weight gradient
+  EK_NCHW_POOL = 8,  // EK_NCHW_POS followed by 2 x 2 / stride-2 max pooling: only the pooled values
+                     // and their first-max offsets are stored (rows in window order, Gather::pool2)
 };
 
 inline int epi_kind(const Epi<float>& e, int64_t n_cols) {
   if (e.col_major) return !e.bias && e.act == GT_ACT_NONE && !e.dmask && !e.dbits && !e.bits_out ? EK_COLMAJOR : -2;
+  if (e.pos_major && e.pool_idx)
+    return e.nchw_L > 0 && !e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask &&
+                   !e.dbits && !e.bits_out
+               ? EK_NCHW_POOL
+               : -2;
   if (e.pos_major)
     return e.nchw_L > 0 && !e.bias_by_row && (e.act == GT_ACT_NONE || e.act == GT_ACT_RELU) && !e.dmask &&
                    !e.dbits && !e.bits_out
@@ -838,7 +860,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int it = 0;
       bool stop = false;
       int rows4[4] = {0, 0, 0, 0}, kind4[4] = {0, 0, 0, 0};
-      if constexpr (AS == A_IM2COL_POS) pos_rows(ga, lane, rows4);
+      if constexpr (AS == A_IM2COL_POS) pos_rows<EK == EK_NCHW_POOL>(ga, lane, rows4);
       for (int u = pair; u < units && !stop; u += pairs) {
         int t, kb, ke;
         unit_of(u, tiles, sp, num_k, t, kb, ke);
@@ -973,6 +995,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               if (epi.bias) v = __fadd_rn(v, b);
               if (relu) v = go_max(v, 0.0f);
               col[i * L] = v;
+            }
+          }
+        } else if constexpr (EK == EK_NCHW_POOL) {
+          // bias, ReLU, then each window's first maximum in offset order
+          // (v0 = (0,0), v1 = (0,1), v2 = (1,0), v3 = (1,1): MaxPool2d's
+          // v > best rule). Lane 4 w' + k takes channel i0 + k of the warp's
+          // window w' (rows 4 w' .. 4 w' + 3 of this warp's buffer; the four
+          // reads of a group are conflict-free), so every lane pools and
+          // stores.
+          const int64_t nl = n0 + 32 * j + lane;
+          const float my_bias = epi.bias && nl < s.N ? __ldg(epi.bias + nl) : 0.0f;
+          const bool relu = epi.act == GT_ACT_RELU;
+          const int64_t P4 = epi.nchw_L / 4;
+          const int k = lane & 3, row0 = lane & ~3;
+          // lanes 4 w' .. 4 w' + 3 hold window 8 q + w' of the CTA's 32; its
+          // pooled output for channel c goes to pool_base + c * P4 (-1: past
+          // M). Recomputed per block to keep it out of the total's live range.
+          int64_t pool_base = -1;
+          {
+            const int w = (32 * q + lane) >> 2, per = ga.rows_pi >> 2, pw = ga.OW >> 1;
+            const int wn = w / per, rem = w - wn * per, pr = rem / pw, pc = rem - pr * pw;
+            const int64_t m_tl = (m0 - 32 * q) + (int64_t)wn * ga.rows_pi + (int64_t)(2 * pr) * ga.OW + 2 * pc;
+            if (m_tl < s.M) {
+              const int64_t img = m_tl / epi.nchw_L, pos = m_tl - img * epi.nchw_L, oh = pos / ga.OW;
+              pool_base = img * epi.nchw_M * P4 + (oh / 2) * pw + (pos - oh * ga.OW) / 2;
+            }
+          }
+#pragma unroll 1
+          for (int i0 = 0; i0 < 32; i0 += 4) {
+            const float b = __shfl_sync(0xffffffffu, my_bias, i0 + k);
+            float v[4];
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+              v[p] = xpose[(row0 + p) * EPI_LD + i0 + k];
+              if (epi.bias) v[p] = __fadd_rn(v[p], b);
+              if (relu) v[p] = go_max(v[p], 0.0f);
+            }
+            const int64_t c = n0 + 32 * j + i0 + k;
+            if (pool_base >= 0 && c < s.N) {
+              float best = v[0];
+              int kb = 0;
+              if (v[1] > best) best = v[1], kb = 1;
+              if (v[2] > best) best = v[2], kb = 2;
+              if (v[3] > best) best = v[3], kb = 3;
+              epi.out[pool_base + c * P4] = best;
+              epi.pool_idx[pool_base + c * P4] = (uint8_t)kb;
             }
           }
         } else if constexpr (EK == EK_COLMAJOR) {
@@ -1138,6 +1206,7 @@ static char* launch_kind(gt_ctx* ctx, const GemmShape& s, const float* A, const 
     case EK_MASK: return launch_layout<EK_MASK>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_CONV: return launch_layout<EK_CONV>(ctx, s, A, B, epi, a_mn, b_mn, sp);
     case EK_NCHW_POS:
+    case EK_NCHW_POOL:
     case EK_COLMAJOR: return errorf("gemm_tc: the implicit convolution layouts have their own launchers");
     default: return launch_layout<EK_GENERIC>(ctx, s, A, B, epi, a_mn, b_mn, sp);
   }
@@ -1160,6 +1229,51 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, SplitPlan sp,
     float acc = ws[i];
     for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
     epi.store(m, n, acc);
+  }
+}
+
+// The split tiles of a pooled implicit convolution (EK_NCHW_POOL): a thread
+// finishes the four rows of one 2 x 2 window (rows 4 w .. 4 w + 3 of a CTA,
+// Gather::pool2) for one channel, each summed in split order as
+// splitk_reduce_kernel sums it, and stores the window's first maximum and its
+// offset, as the kernel's own pooled epilogue does for whole tiles.
+template <int TBN>
+__global__ void splitk_reduce_pool_kernel(const float* __restrict__ ws, SplitPlan sp, int tiles, int n_tiles,
+                                          int64_t M, int64_t N, Epi<float> epi, int rows_pi, int OW) {
+  constexpr int64_t TE = Tile<TBN>::TILE_ELEMS;
+  const int rest = tiles - sp.whole;
+  const int64_t total = (int64_t)rest * TE, work = (int64_t)rest * 2 * (BM / 4) * TBN;
+  const int per = rows_pi >> 2, pw = OW >> 1;
+  const int64_t L = epi.nchw_L, P4 = L / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < work; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / (2 * (BM / 4) * TBN));
+    const int64_t e = i - (int64_t)r * 2 * (BM / 4) * TBN;
+    const int wg = (int)(e / TBN), cl = (int)(e - (int64_t)wg * TBN);
+    const int t = sp.whole + r;
+    const int64_t n = (int64_t)(t % n_tiles) * TBN + cl;
+    if (n >= N) continue;
+    const int rank = wg / (BM / 4), w = wg - rank * (BM / 4);
+    const int nl = w / per, rem = w - nl * per, pr = rem / pw, pc = rem - pr * pw;
+    const int64_t m_tl =
+        (int64_t)(t / n_tiles) * 2 * BM + rank * BM + (int64_t)nl * rows_pi + (int64_t)(2 * pr) * OW + 2 * pc;
+    if (m_tl >= M) continue;
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int64_t at = (int64_t)r * TE + (int64_t)(rank * BM + 4 * w + k) * TBN + cl;
+      float acc = ws[at];
+      for (int s = 1; s < sp.splits; s++) acc = __fadd_rn(acc, ws[(int64_t)s * total + at]);
+      v[k] = epi.finish(m_tl, n, acc);
+    }
+    float best = v[0];
+    int kb = 0;
+    if (v[1] > best) best = v[1], kb = 1;
+    if (v[2] > best) best = v[2], kb = 2;
+    if (v[3] > best) best = v[3], kb = 3;
+    const int64_t img = m_tl / L, pos = m_tl - img * L, oh = pos / OW;
+    const int64_t o = (img * epi.nchw_M + n) * P4 + (oh / 2) * pw + (pos - oh * OW) / 2;
+    epi.out[o] = best;
+    epi.pool_idx[o] = (uint8_t)kb;
   }
 }
 
@@ -1279,7 +1393,7 @@ static SplitPlan choose_plan(int64_t tiles, int64_t pairs, int64_t num_k, int64_
 // split order and finishes with the epilogue.
 template <int TBN, typename Fire>
 static char* run_planned(gt_ctx* ctx, const GemmShape& s, const Epi<float>& epi, int64_t tiles, int64_t n_tiles,
-                         Fire&& fire) {
+                         Fire&& fire, const Gather* ga = nullptr) {
   constexpr int64_t TE = Tile<TBN>::TILE_ELEMS;
   SplitPlan sp = choose_plan(tiles, pairs_available(ctx), ceil_div(s.K, BK), TE);
   sp.wait_limit_ns = g_wait_limit_ns;
@@ -1292,7 +1406,10 @@ static char* run_planned(gt_ctx* ctx, const GemmShape& s, const Epi<float>& epi,
   sp.ws = (float*)ws;
   char* err = fire(sp);
   if (!err) {
-    if (epi.bits_out)
+    if (epi.pool_idx)  // pooled implicit convolution (ga set by its launcher)
+      splitk_reduce_pool_kernel<TBN><<<grid_for(ctx, rest * TE / 4, 256), 256, 0, ctx->stream>>>(
+          sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi, ga->rows_pi, ga->OW);
+    else if (epi.bits_out)
       splitk_reduce_bits_kernel<<<grid_for(ctx, rest * TE / 32, 256), 256, 0, ctx->stream>>>(
           sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
     else if (epi.colsum_ws)
@@ -1316,6 +1433,21 @@ static char* conv_fwd_launch(gt_ctx* ctx, const GemmShape& s, const CUtensorMap&
   return run_planned<TBN>(ctx, s, e, tiles, n_tiles, [&](const SplitPlan& sp) {
     return launch_kernel<false, false, EK_NCHW_POS, TBN, A_IM2COL_POS, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga);
   });
+}
+
+// The forward with 2 x 2 pooling in the epilogue; split tiles are pooled by
+// splitk_reduce_pool_kernel. The split plan is the unpooled forward's, so the
+// pooled values are those of conv_fwd_launch followed by pooling, bit for bit.
+template <int TBN>
+static char* conv_fwd_pool_launch(gt_ctx* ctx, const GemmShape& s, const CUtensorMap& ta, const CUtensorMap& tb,
+                                  const Epi<float>& e, const Gather& ga) {
+  const int64_t n_tiles = ceil_div(s.N, TBN), tiles = ceil_div(s.M, 2 * BM) * n_tiles;
+  return run_planned<TBN>(
+      ctx, s, e, tiles, n_tiles,
+      [&](const SplitPlan& sp) {
+        return launch_kernel<false, false, EK_NCHW_POOL, TBN, A_IM2COL_POS, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga);
+      },
+      &ga);
 }
 
 template <int TBN>
@@ -1439,7 +1571,7 @@ char* gemm_tc_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* 
 }
 
 char* conv_fwd_tc(gt_ctx* ctx, const float* x, const float* ws, int64_t w_pitch, const float* bias, float* y,
-                  const gt_geom& g, int64_t O, int act, bool* done) {
+                  const gt_geom& g, int64_t O, int act, bool* done, uint8_t* pool_idx) {
   *done = false;
   const int64_t L = g.OH * g.OW, P = g.N * L, CKK = g.C * g.KH * g.KW;
   if (P < 1 || O < 1 || CKK < 1 || ctx->sm_count < 2 || !tc::fits32(g, O)) return nullptr;
@@ -1449,6 +1581,12 @@ char* conv_fwd_tc(gt_ctx* ctx, const float* x, const float* ws, int64_t w_pitch,
   GemmShape s{P, O, CKK, false, true, 0, w_pitch};
   tc::Gather ga;
   if (!tc::halo_pos(g, ga) || ((uintptr_t)x & 15)) return nullptr;
+  if (pool_idx) {
+    // windows must not straddle CTAs: a CTA's 128 positions are whole row
+    // pairs of one image (an even number of rows) or whole images
+    if (g.OH % 2 || g.OW % 2 || (ga.box_n == 1 && ga.bh % 2)) return nullptr;
+    ga.pool2 = 1;
+  }
   ga.b_lo_row = (int)conv_weight_rows(O);
   Epi<float> e;
   e.out = y;
@@ -1457,13 +1595,20 @@ char* conv_fwd_tc(gt_ctx* ctx, const float* x, const float* ws, int64_t w_pitch,
   e.nchw_L = L;
   e.nchw_M = O;
   e.pos_major = true;
+  e.pool_idx = pool_idx;
   const int tbn = (int)conv_tile_width(O);
   CUtensorMap ta, tb;
   GT_TRY(tc::make_halo_map(ctx, &ta, x, g, ga));
   GT_TRY(tc::make_map(ctx, &tb, ws, CKK, 2 * ga.b_lo_row, w_pitch, false, tbn / 2));
-  char* err = tbn == 64    ? tc::conv_fwd_launch<64>(ctx, s, ta, tb, e, ga)
-              : tbn == 128 ? tc::conv_fwd_launch<128>(ctx, s, ta, tb, e, ga)
-                           : tc::conv_fwd_launch<256>(ctx, s, ta, tb, e, ga);
+  char* err = nullptr;
+  if (pool_idx)
+    err = tbn == 64    ? tc::conv_fwd_pool_launch<64>(ctx, s, ta, tb, e, ga)
+          : tbn == 128 ? tc::conv_fwd_pool_launch<128>(ctx, s, ta, tb, e, ga)
+                       : tc::conv_fwd_pool_launch<256>(ctx, s, ta, tb, e, ga);
+  else
+    err = tbn == 64    ? tc::conv_fwd_launch<64>(ctx, s, ta, tb, e, ga)
+          : tbn == 128 ? tc::conv_fwd_launch<128>(ctx, s, ta, tb, e, ga)
+                       : tc::conv_fwd_launch<256>(ctx, s, ta, tb, e, ga);
   if (!err) *done = true;
   return err;
 }

@@ -102,6 +102,10 @@ CUDA_API = {
     "gt_conv_bwd": ("err", [_P, _INT, _P, _P, _P, _P, _P, _P, ctypes.POINTER(GtGeom), _I64]),
     "gt_maxpool_fwd_idx": ("err", [_P, _INT, _P, _P, _P, ctypes.POINTER(GtGeom)]),
     "gt_maxpool_bwd_idx": ("err", [_P, _INT, _P, _P, _P, _INT, _P, ctypes.POINTER(GtGeom)]),
+    "gt_conv_fwd_pool": ("err", [_P, _INT, _P, _P, _P, _P, _P, ctypes.POINTER(GtGeom), ctypes.POINTER(GtGeom),
+                                 _I64, _INT]),
+    "gt_conv_bwd_weight_pool": ("err", [_P, _INT, _P, _P, _P, _P, _INT, _P, _P, ctypes.POINTER(GtGeom),
+                                        ctypes.POINTER(GtGeom), _I64]),
     "gt_argmax_rows": ("err", [_P, _INT, _P, _I64, _I64, _P]),
     "gt_count_equal": ("err", [_P, _P, _P, _I64, _P]),
     "gt_xent_fwd_bwd": ("err", [_P, _INT, _P, _P, _I64, _I64, _P, _P, _P]),

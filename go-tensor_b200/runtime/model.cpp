@@ -282,10 +282,36 @@ void Model::plan(const std::vector<gth_layer>& layers, const std::vector<int64_t
   for (auto& op : ops_)
     if (op.kind == Op::LINEAR && op.needs_dx && op.src >= 0 && ops_[op.src].kind == Op::LINEAR)
       ops_[op.src].db_upstream = true;
+  // The first conv [+ ReLU] followed by a MaxPool2d with non-overlapping
+  // windows: its weight gradient comes straight from the pooled gradient
+  // (gt_conv_bwd_weight_pool), and the pool's own backward is skipped.
+  for (size_t i = 0; i < ops_.size(); i++) {
+    Op& pool = ops_[i];
+    if (pool.kind != Op::POOL || pool.src < 0 || pool.g.stride < pool.g.KH || pool.g.stride < pool.g.KW) continue;
+    Op& conv = ops_[pool.src];
+    if (conv.kind != Op::CONV || conv.needs_dx) continue;
+    if (conv.act != GT_ACT_NONE && !(conv.act == GT_ACT_RELU && pool.relu_in)) continue;
+    conv.fused_pool = (int)i;
+    pool.wgrad_fused = true;
+  }
+  // A float32 conv [+ ReLU] followed by a 2 x 2 / stride-2 MaxPool2d writes
+  // only the pooled output and its indices (gt_conv_fwd_pool): nothing reads
+  // the conv's own output, because the pool's backward takes the ReLU mask
+  // from the pooled values.
+  if (dtype_ == GT_FLOAT32)
+    for (size_t i = 0; i < ops_.size(); i++) {
+      Op& pool = ops_[i];
+      if (pool.kind != Op::POOL || pool.src < 0 || pool.g.KH != 2 || pool.g.KW != 2 || pool.g.stride != 2) continue;
+      Op& conv = ops_[pool.src];
+      if (conv.kind != Op::CONV || (conv.act != GT_ACT_NONE && !(conv.act == GT_ACT_RELU && pool.relu_in))) continue;
+      conv.pool_fwd = (int)i;
+      pool.fwd_fused = true;
+    }
   // A float64 conv keeps its forward's im2col columns for its backward; the
-  // float32 convs are implicit GEMMs and keep none.
+  // float32 convs are implicit GEMMs and keep none, nor does a conv whose
+  // weight gradient comes from the pooled gradient.
   for (auto& op : ops_) {
-    if (op.kind != Op::CONV || dtype_ != GT_FLOAT64) continue;
+    if (op.kind != Op::CONV || dtype_ != GT_FLOAT64 || op.fused_pool >= 0) continue;
     const int64_t rows = op.g.N * op.g.OH * op.g.OW, ckk = op.g.C * op.g.KH * op.g.KW;
     if (rows * ckk == 0) continue;
     cols_.emplace_back(ctx_, (size_t)(rows * ckk) * es_);
@@ -367,7 +393,11 @@ void Model::forward() {
                               op.N, op.act));
         break;
       case Op::CONV:
-        if (op.cols)
+        if (op.pool_fwd >= 0) {  // the pooled output and indices only
+          Op& pool = ops_[op.pool_fwd];
+          check(gt_conv_fwd_pool(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, pool.out, pool.idx, &op.g,
+                                 &pool.g, op.O, op.act));
+        } else if (op.cols)
           check(gt_conv_fwd_cols(ctx_, dtype_, op.in, p + op.w_off * es_, p + op.b_off * es_, op.out, op.cols, &op.g,
                                  op.O, op.act));
         else
@@ -375,7 +405,7 @@ void Model::forward() {
                             op.act));
         break;
       case Op::POOL:
-        check(gt_maxpool_fwd_idx(ctx_, dtype_, op.in, op.out, op.idx, &op.g));
+        if (!op.fwd_fused) check(gt_maxpool_fwd_idx(ctx_, dtype_, op.in, op.out, op.idx, &op.g));
         break;
       case Op::ACT:
         check(gt_unary(ctx_, dtype_, unary_of(op.act), 0.0, op.in, op.out, numel(op.out_shape)));
@@ -460,6 +490,13 @@ void Model::backward(bool join) {
         break;
       }
       case Op::CONV:
+        if (op.fused_pool >= 0) {  // g is the pooled gradient; no dx (first conv)
+          const Op& pool = ops_[op.fused_pool];
+          check(gt_conv_bwd_weight_pool(ctx_, dtype_, op.in, g, pool.idx, pool.out, pool.relu_in ? 1 : 0,
+                                        gr + op.w_off * es_, gr + op.b_off * es_, &op.g, &pool.g, op.O));
+          if (world_ > 1) issue_ready_buckets(op.w_off);
+          break;
+        }
         if (!op.cols) {  // float32 (implicit GEMMs from x and dy), or no output positions
           check(gt_conv_bwd_weight(ctx_, dtype_, op.in, g, gr + op.w_off * es_, gr + op.b_off * es_, &op.g, op.O));
           if (world_ > 1) issue_ready_buckets(op.w_off);
@@ -481,6 +518,10 @@ void Model::backward(bool join) {
         if (op.needs_dx) std::swap(g, spare);
         break;
       case Op::POOL:
+        if (op.wgrad_fused) {  // the conv before takes g as it is (ReLU mask included)
+          g_pre = op.relu_in;
+          break;
+        }
         if (op.g.stride >= op.g.KH && op.g.stride >= op.g.KW) {
           // Routes g to each window's first maximum; with relu_in the ReLU
           // mask of the producer is applied in the same pass.

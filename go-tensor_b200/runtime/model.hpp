@@ -90,6 +90,16 @@ struct Op {
   // output gradient (the loss for the last layer, the next Linear's dX
   // otherwise), as the column sums of that gradient.
   bool db_upstream = false;
+  // CONV: index of the MaxPool2d after it whose pooled gradient gives this
+  // conv's weight gradient directly (gt_conv_bwd_weight_pool); POOL: its
+  // backward is left to that conv.
+  int fused_pool = -1;
+  bool wgrad_fused = false;
+  // CONV: index of the MaxPool2d after it whose output and indices this
+  // conv's forward writes (gt_conv_fwd_pool); POOL: its forward is left to
+  // that conv.
+  int pool_fwd = -1;
+  bool fwd_fused = false;
 };
 
 class Model {

@@ -244,6 +244,28 @@ GT_API char* gt_maxpool_fwd_idx(gt_ctx* ctx, int dtype, const void* x, void* out
  * relu_mask is set (ReLU before the pool). Writes every element of dx. */
 GT_API char* gt_maxpool_bwd_idx(gt_ctx* ctx, int dtype, const void* grad, const uint8_t* idx, const void* pooled,
                          int relu_mask, void* dx, const gt_geom* g);
+/* Conv2d [+ ReLU] followed by MaxPool2d (geometry pg, non-overlapping windows):
+ * pooled and idx as gt_conv_fwd then gt_maxpool_fwd_idx would give them, bit
+ * for bit. For float32 2 x 2 windows at stride 2 on the implicit-GEMM path the
+ * pooling runs in the convolution's epilogue and the convolution's output is
+ * never stored (the backward needs only the pooled values and the indices:
+ * gt_maxpool_bwd_idx, gt_conv_bwd_weight_pool); otherwise the output goes
+ * through scratch memory. act is GT_ACT_NONE or GT_ACT_RELU on the fused path.
+ * No counterpart in the reference (tensor/conv.go:40-70 runs the two ops). */
+GT_API char* gt_conv_fwd_pool(gt_ctx* ctx, int dtype, const void* x, const void* w, const void* bias, void* pooled,
+                              uint8_t* idx, const gt_geom* g, const gt_geom* pg, int64_t out_channels, int act);
+/* dw (O, C, KH, KW) and db (O) (NULL: skip) of a Conv2d (geometry g) whose
+ * output went through [ReLU ->] MaxPool2d (geometry pg, non-overlapping
+ * windows), from the pooled gradient: the same results as
+ * gt_maxpool_bwd_idx(grad, idx, pooled, relu_mask, dy, pg) followed by
+ * gt_conv_bwd_weight(x, dy, dw, db, g, O), within rounding. For k x k windows
+ * at stride k that tile the output, with C*KH*KW <= 32 (a first convolution),
+ * the full-resolution gradient dy is never written: only window maxima carry
+ * a nonzero term (MaxPool2dBackward, tensor/conv.go:63-70). Other geometries
+ * go through dy in scratch memory. No counterpart in the reference. */
+GT_API char* gt_conv_bwd_weight_pool(gt_ctx* ctx, int dtype, const void* x, const void* grad, const uint8_t* idx,
+                                     const void* pooled, int relu_mask, void* dw, void* db, const gt_geom* g,
+                                     const gt_geom* pg, int64_t out_channels);
 
 /* out[r] (int32) = Tensor.Argmax of row r of x (rows x n) (tensor/ops.go:176-192):
  * the first index of the row's maximum, comparing as the reference does

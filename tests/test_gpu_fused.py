@@ -520,3 +520,128 @@ def test_linear_bwd_data_db_is_the_column_sum_of_dx(dt, npdt, tol, mkn, act):
         check(lib().gt_linear_bwd_data_bits_db(ctx(), dt, dyd.ptr, wd.ptr, bits.ptr, dx3.ptr, db3.ptr, M, K, N))
         assert_bits(host(dx3), dx, "dx through the bit mask")
         assert_close(host(db3), want, tol, "db_prev through the bit mask")
+
+
+# (N, C, H, W, O, kernel, stride, pad, pool window): the conv stack's and the
+# CNN's first convolutions, a strided one, 3 x 3 windows, and two that take
+# the fallback through the full-resolution gradient (C*KH*KW > 32; a pool
+# that leaves the last row and column out).
+POOL_CONVS = [(4, 3, 32, 32, 64, 3, 1, 1, 2), (4, 1, 28, 28, 32, 3, 1, 1, 2), (2, 2, 11, 11, 8, 3, 2, 1, 2),
+              (2, 3, 12, 12, 16, 3, 1, 1, 3), (2, 4, 8, 8, 8, 3, 1, 1, 2), (2, 3, 9, 9, 8, 3, 1, 1, 2)]
+
+
+def _pool_wgrad_case(dt, npdt, cs, relu, rng, x=None):
+    """Forward conv [+ ReLU] -> MaxPool2d on the device, then the fused
+    weight gradient and the two-call chain on the same pooled gradient."""
+    N, C, H, W, O, k, s, p, kp = cs
+    if x is None:
+        x = rng.standard_normal((N, C, H, W)).astype(npdt)
+    w = (rng.standard_normal((O, C, k, k)) / np.sqrt(C * k * k)).astype(npdt)
+    b = (0.1 * rng.standard_normal(O)).astype(npdt)
+    g = T.conv_geom("Conv2d", [N, C, H, W], k, k, s, p)
+    pg = T.conv_geom("MaxPool2d", [N, O, g.OH, g.OW], kp, kp, kp, 0)
+    gg = ctypes.byref(_lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_]))
+    pgg = ctypes.byref(_lib.GtGeom(*[getattr(pg, f) for f, _ in _lib.GtGeom._fields_]))
+    y = new(N * O * g.OH * g.OW, dt)
+    check(lib().gt_conv_fwd(ctx(), dt, dev(x).ptr, dev(w).ptr, dev(b).ptr, y.ptr, gg, O, 1 if relu else 0))
+    npool = N * O * pg.OH * pg.OW
+    pooled, idx = new(npool, dt), new(npool, T.Float32)
+    check(lib().gt_maxpool_fwd_idx(ctx(), dt, y.ptr, pooled.ptr, idx.ptr, pgg))
+    grad = (rng.standard_normal(npool) / npool).astype(npdt)
+    xd, gd = dev(x), dev(grad)
+    dw, db = new(O * C * k * k, dt), new(O, dt)
+    check(lib().gt_conv_bwd_weight_pool(ctx(), dt, xd.ptr, gd.ptr, idx.ptr, pooled.ptr, 1 if relu else 0, dw.ptr,
+                                        db.ptr, gg, pgg, O))
+    dy, dw2, db2 = new(N * O * g.OH * g.OW, dt), new(O * C * k * k, dt), new(O, dt)
+    check(lib().gt_maxpool_bwd_idx(ctx(), dt, gd.ptr, idx.ptr, pooled.ptr, 1 if relu else 0, dy.ptr, pgg))
+    check(lib().gt_conv_bwd_weight(ctx(), dt, xd.ptr, dy.ptr, dw2.ptr, db2.ptr, gg, O))
+    return x, w, b, grad, host(dw), host(db), host(dw2), host(db2)
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+@pytest.mark.parametrize("cs", POOL_CONVS)
+@pytest.mark.parametrize("relu", [True, False])
+def test_conv_bwd_weight_pool(dt, npdt, tol, cs, relu):
+    """The fused pool-backward weight gradient against the oracle's Conv2d
+    [-> ReLU] -> MaxPool2d backward (tensor/conv.go:40-70) and against the
+    two device calls it replaces."""
+    N, C, H, W, O, k, s, p, kp = cs
+    rng = np.random.default_rng(sum(cs) + relu)
+    x, w, b, grad, dw, db, dw2, db2 = _pool_wgrad_case(dt, npdt, cs, relu, rng)
+    g = T.conv_geom("Conv2d", [N, C, H, W], k, k, s, p)
+    ws, bs = ref(w, O, C, k, k).SetRequiresGrad(True), ref(b, O).SetRequiresGrad(True)
+    out = T.Conv2d(ref(x, N, C, H, W), ws, bs, s, p)
+    if relu:
+        out = out.ReLU()
+    pooled = T.MaxPool2d(out, kp, kp)
+    pooled.Backward(ref(grad, N, O, g.OH // kp, g.OW // kp))
+    want_w, want_b = ws.Grad().Float64s(), bs.Grad().Float64s()
+    assert_close(dw, want_w, tol, "dw vs oracle")
+    assert_close(db, want_b, tol, "db vs oracle")
+    assert_close(dw, dw2, tol, "dw vs the two calls")
+    assert_close(db, db2, tol, "db vs the two calls")
+
+
+@pytest.mark.parametrize("dt,npdt,tol", DT)
+def test_conv_bwd_weight_pool_non_finite_input(dt, npdt, tol):
+    """An infinite input value meets zero entries of the output gradient
+    (positions that are not window maxima): 0 * inf = NaN in the dense sum, so
+    the fused kernel must leave the same weight-gradient entries non-finite
+    as the two calls (whose 3xTF32 GEMM turns every product with an infinity
+    into NaN, where the fused kernel keeps g * inf = inf at a window maximum)."""
+    cs = (3, 3, 16, 16, 8, 3, 1, 1, 2)
+    N, C, H, W = cs[:4]
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((N, C, H, W)).astype(npdt)
+    x[1, 2, 5, 7] = np.inf
+    x[2, 0, 0, 3] = -np.inf
+    *_, dw, db, dw2, db2 = _pool_wgrad_case(dt, npdt, cs, True, rng, x=x)
+    assert np.isnan(dw2).any() and np.isnan(dw).any()
+    np.testing.assert_array_equal(np.isfinite(dw), np.isfinite(dw2))
+    fin = np.isfinite(dw2)
+    assert_close(dw[fin], dw2[fin], tol, "finite dw entries")
+    assert_close(db, db2, tol, "db")
+
+
+# (N, C, H, W, O, kernel, pad, pool window): the conv stack's four layers
+# (whole-row and whole-image position tiles, an odd image count that leaves
+# half of the last tile empty), a 64-wide image, and geometries that take the
+# unfused path (a 128-wide image, 28 x 28, 3 x 3 windows).
+CONV_POOLS = [(2, 3, 32, 32, 64, 3, 1, 2), (3, 64, 16, 16, 128, 3, 1, 2), (3, 128, 8, 8, 256, 3, 1, 2),
+              (5, 256, 4, 4, 512, 3, 1, 2), (1, 8, 64, 64, 32, 3, 1, 2), (1, 4, 128, 128, 16, 3, 1, 2),
+              (2, 1, 28, 28, 32, 3, 1, 2), (2, 3, 12, 12, 16, 3, 1, 3)]
+
+
+@pytest.mark.parametrize("cs", CONV_POOLS)
+@pytest.mark.parametrize("act", [0, 1])
+def test_conv_fwd_pool_bit_exact(cs, act):
+    """gt_conv_fwd_pool gives the pooled values and first-max indices of
+    gt_conv_fwd followed by gt_maxpool_fwd_idx bit for bit (the pooled
+    epilogue changes only which lane holds which position), and the oracle's
+    Conv2d [-> ReLU] -> MaxPool2d within tolerance."""
+    N, C, H, W, O, k, p, kp = cs
+    rng = np.random.default_rng(sum(cs) + act)
+    x = rng.standard_normal((N, C, H, W)).astype(np.float32)
+    w = (rng.standard_normal((O, C, k, k)) / np.sqrt(C * k * k)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(O)).astype(np.float32)
+    g = T.conv_geom("Conv2d", [N, C, H, W], k, k, 1, p)
+    pg = T.conv_geom("MaxPool2d", [N, O, g.OH, g.OW], kp, kp, kp, 0)
+    gg = ctypes.byref(_lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_]))
+    pgg = ctypes.byref(_lib.GtGeom(*[getattr(pg, f) for f, _ in _lib.GtGeom._fields_]))
+    xd, wd, bd = dev(x), dev(w), dev(b)
+    npool = N * O * pg.OH * pg.OW
+    pooled, idx = new(npool, T.Float32), new((npool + 3) // 4, T.Float32)
+    check(lib().gt_conv_fwd_pool(ctx(), 0, xd.ptr, wd.ptr, bd.ptr, pooled.ptr, idx.ptr, gg, pgg, O, act))
+    y = new(N * O * g.OH * g.OW, T.Float32)
+    pooled2, idx2 = new(npool, T.Float32), new((npool + 3) // 4, T.Float32)
+    check(lib().gt_conv_fwd(ctx(), 0, xd.ptr, wd.ptr, bd.ptr, y.ptr, gg, O, act))
+    check(lib().gt_maxpool_fwd_idx(ctx(), 0, y.ptr, pooled2.ptr, idx2.ptr, pgg))
+    got, want = host(pooled), host(pooled2)
+    assert_bits(got, want, "pooled values")
+    gi = host(idx).view(np.uint8)[:npool]
+    wi = host(idx2).view(np.uint8)[:npool]
+    np.testing.assert_array_equal(gi, wi)
+    out = T.Conv2d(ref(x, N, C, H, W), ref(w, O, C, k, k), ref(b, O), 1, p)
+    if act:
+        out = out.ReLU()
+    assert_close(got, T.MaxPool2d(out, kp, kp).Float64s(), 1e-4, "pooled vs oracle")
