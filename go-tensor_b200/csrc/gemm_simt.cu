@@ -159,131 +159,6 @@ __global__ void simt_split_reduce_kernel(const T* __restrict__ ws, int splits, i
   }
 }
 
-// FP64 main kernel on the FP64 tensor-core path (mma.sync m8n8k4 f64, 256
-// fused multiply-adds per warp instruction, so eight warps per SM keep the
-// pipe busy where DFMA would be issue-bound): a 128 x 128 tile per CTA over
-// 16-deep K slices, staged k-major in shared memory by cp.async (8-byte
-// elements, out-of-range ones zero-filled) in a two-slice ring, so the next
-// slice's loads run under this slice's MMAs. Sixteen warps (four per
-// scheduler, which the MMA latency needs): warp w computes rows
-// 32 * (w / 4) .. +32 and columns 32 * (w % 4) .. +32 as 4 x 4 MMA tiles.
-// Fragment reads: thread t takes k = t % 4 and m (or n) = t / 4 of a tile;
-// with rows of 132 doubles those 32 reads fall in distinct banks.
-namespace f64k {
-constexpr int BM = 128, BN = 128, BK = 16, PITCH = 132, THREADS = 512;
-constexpr int STAGES = 2;  // slices in the shared-memory ring
-constexpr size_t SMEM = (size_t)STAGES * 2 * BK * PITCH * sizeof(double);
-
-__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool valid) {
-  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
-}
-
-__device__ __forceinline__ void mma_f64(double (&c)[2], double a, double b) {
-  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
-               : "+d"(c[0]), "+d"(c[1])
-               : "d"(a), "d"(b));
-}
-}  // namespace f64k
-
-template <bool TA, bool TB>
-__global__ void __launch_bounds__(f64k::THREADS, 1)
-    gemm_f64_kernel(GemmShape s, const double* __restrict__ A, const double* __restrict__ B, Epi<double> epi,
-                    int64_t k_per_split, double* __restrict__ ws) {
-  using namespace f64k;
-  extern __shared__ double sm[];
-  double* As = sm;                         // [STAGES][BK][PITCH]
-  double* Bs = sm + STAGES * BK * PITCH;   // [STAGES][BK][PITCH]
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int wm = 32 * (warp >> 2), wn = 32 * (warp & 3);
-  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
-  const int64_t k_begin = (int64_t)blockIdx.z * k_per_split;
-  const int64_t k_end = k_begin + k_per_split < s.K ? k_begin + k_per_split : s.K;
-  const int slices = (int)((k_end - k_begin + BK - 1) / BK);
-
-  // Each thread copies 4 elements of A and 4 of B per slice, coalesced along
-  // whichever index is contiguous in global memory (no bytes are read for an
-  // out-of-range element; its address is clamped to the base).
-  auto load = [&](int slice, int stage) {
-    const int64_t k0 = k_begin + (int64_t)slice * BK;
-    double* as = As + stage * BK * PITCH;
-    double* bs = Bs + stage * BK * PITCH;
-#pragma unroll
-    for (int r = 0; r < BM * BK / THREADS; r++) {
-      const int e = tid + THREADS * r;
-      const int kk = TA ? e / BM : e % BK, mm = TA ? e % BM : e / BK;
-      const int64_t gm = m0 + mm, gk = k0 + kk;
-      const bool ok = gm < s.M && gk < k_end;
-      cp_async8(as + kk * PITCH + mm, ok ? (TA ? A + gk * s.lda + gm : A + gm * s.lda + gk) : A, ok);
-    }
-#pragma unroll
-    for (int r = 0; r < BN * BK / THREADS; r++) {
-      const int e = tid + THREADS * r;
-      const int kk = TB ? e % BK : e / BN, nn = TB ? e / BK : e % BN;
-      const int64_t gn = n0 + nn, gk = k0 + kk;
-      const bool ok = gn < s.N && gk < k_end;
-      cp_async8(bs + kk * PITCH + nn, ok ? (TB ? B + gn * s.ldb + gk : B + gk * s.ldb + gn) : B, ok);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-
-  double acc[4][4][2];
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-#pragma unroll
-    for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
-
-  const int fk = lane & 3, fr = lane >> 2;  // fragment k and row / column
-  // One commit group per slice (empty past the end), so waiting until at
-  // most STAGES - 1 groups are pending means slice t has landed.
-#pragma unroll
-  for (int p = 0; p < STAGES - 1; p++) {
-    if (p < slices) load(p, p);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
-  }
-  for (int t = 0; t < slices; t++) {
-    const int next = t + STAGES - 1;
-    if (next < slices) load(next, next % STAGES);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group %0;" ::"n"(STAGES - 1) : "memory");
-    __syncthreads();
-    const double* as = As + (t % STAGES) * BK * PITCH + fk * PITCH + wm + fr;
-    const double* bs = Bs + (t % STAGES) * BK * PITCH + fk * PITCH + wn + fr;
-#pragma unroll
-    for (int k4 = 0; k4 < BK; k4 += 4) {
-      double a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; i++) a[i] = as[k4 * PITCH + 8 * i];
-#pragma unroll
-      for (int j = 0; j < 4; j++) b[j] = bs[k4 * PITCH + 8 * j];
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) mma_f64(acc[i][j], a[i], b[j]);
-    }
-    __syncthreads();  // the stage is refilled STAGES - 1 slices on
-  }
-
-  // Thread t holds C(8 i + t / 4, 8 j + 2 (t % 4) + {0, 1}) of the warp's tile.
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int64_t m = m0 + wm + 8 * i + fr;
-    if (m >= s.M) continue;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int64_t n = n0 + wn + 8 * j + 2 * fk + h;
-        if (n >= s.N) continue;
-        if (ws)
-          ws[((int64_t)blockIdx.z * s.M + m) * s.N + n] = acc[i][j][h];
-        else
-          epi.store(m, n, acc[i][j][h]);
-      }
-    }
-  }
-}
-
 // Splits for a launch of `blocks` output tiles: enough to give every SM two
 // blocks, each split at least 128 deep in K, at most 1024 splits and a 256 MB
 // workspace.
@@ -327,42 +202,255 @@ static char* simt_launch(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B
   return nullptr;
 }
 
-// The FP64 main kernel (one CTA per SM). K is split when the tiles cannot
-// fill the SMs once: S = SMs / tiles ways, each split at least 256 deep.
+// FP64 main kernel on the FP64 tensor-core path (mma.sync m8n8k4 f64, 256
+// fused multiply-adds per warp instruction, so sixteen warps per SM keep the
+// pipe busy where DFMA would be issue-bound): a 128 x 128 tile per CTA over
+// 32-deep K slices, staged k-major in shared memory by cp.async (8-byte
+// elements, out-of-range ones zero-filled) in a three-slice ring with one
+// barrier per slice, so two slices' loads run under the MMAs. Sixteen warps
+// (four per scheduler, which the MMA latency needs): warp w computes rows
+// 32 * (w / 4) .. +32 and columns 32 * (w % 4) .. +32 as 4 x 4 MMA tiles.
+// Fragment reads: thread t takes k = t % 4 and m (or n) = t / 4 of a tile;
+// with rows of 132 doubles those reads fall in distinct banks. An operand
+// whose K index is contiguous in memory is copied as 4 x 4 blocks (four
+// consecutive k of four rows per 16 threads: 32-byte runs in global memory,
+// distinct banks in shared memory).
+//
+// Work units: units 0 .. whole-1 are whole tiles; after them each remaining
+// tile is `splits` units over consecutive K ranges of k_per, whose partial
+// tiles go to ws and are added in K order by f64_tail_reduce_kernel (the last
+// wave's tiles spread over all SMs instead of leaving most of them idle).
+namespace f64k {
+constexpr int BM = 128, BN = 128, BK = 32, PITCH = 132, THREADS = 512;
+constexpr int STAGES = 3;  // slices in the shared-memory ring
+constexpr size_t SMEM = (size_t)STAGES * 2 * BK * PITCH * sizeof(double);
+static_assert(BM * BK % THREADS == 0 && BN * BK % THREADS == 0 && BK % 4 == 0, "copy mapping");
+
+struct Plan {
+  int whole = 0;        // units that are whole tiles
+  int splits = 1;       // units per remaining tile
+  int64_t k_per = 0;    // K range of a split unit (a multiple of BK)
+  int64_t gx = 1;       // tiles along N
+};
+
+__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
+}
+
+__device__ __forceinline__ void mma_f64(double (&c)[2], double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+               : "+d"(c[0]), "+d"(c[1])
+               : "d"(a), "d"(b));
+}
+
+// Element e (of the BK x 128 slice a thread block copies) -> (k, row).
+// KC: the operand's K index is contiguous in memory (4 x 4 blocks);
+// otherwise the row index is (one row of 128 per k).
+template <bool KC>
+__device__ __forceinline__ void slice_elem(int e, int& kk, int& rr) {
+  if constexpr (KC) {
+    const int rest = e >> 4;
+    kk = (e & 3) + 4 * (rest % (BK / 4));
+    rr = ((e >> 2) & 3) + 4 * (rest / (BK / 4));
+  } else {
+    kk = e / 128;
+    rr = e % 128;
+  }
+}
+}  // namespace f64k
+
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(f64k::THREADS, 1)
+    gemm_f64_kernel(GemmShape s, const double* __restrict__ A, const double* __restrict__ B, Epi<double> epi,
+                    f64k::Plan plan, double* __restrict__ ws) {
+  using namespace f64k;
+  extern __shared__ double sm[];
+  double* As = sm;                         // [STAGES][BK][PITCH]
+  double* Bs = sm + STAGES * BK * PITCH;   // [STAGES][BK][PITCH]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = 32 * (warp >> 2), wn = 32 * (warp & 3);
+  const int u = blockIdx.x;
+  int64_t tile, k_begin = 0, k_end = s.K;
+  int split = -1;
+  if (u < plan.whole) {
+    tile = u;
+  } else {
+    const int r = u - plan.whole;
+    tile = plan.whole + r / plan.splits;
+    split = r % plan.splits;
+    k_begin = (int64_t)split * plan.k_per;
+    k_end = k_begin + plan.k_per < s.K ? k_begin + plan.k_per : s.K;
+  }
+  const int64_t m0 = (tile / plan.gx) * BM, n0 = (tile % plan.gx) * BN;
+  const int slices = (int)((k_end - k_begin + BK - 1) / BK);
+
+  // A is K-contiguous unless transposed; B is K-contiguous when transposed.
+  auto load = [&](int slice, int stage) {
+    const int64_t k0 = k_begin + (int64_t)slice * BK;
+    double* as = As + stage * BK * PITCH;
+    double* bs = Bs + stage * BK * PITCH;
+#pragma unroll
+    for (int r = 0; r < BM * BK / THREADS; r++) {
+      int kk, mm;
+      slice_elem<!TA>(tid + THREADS * r, kk, mm);
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      const bool ok = gm < s.M && gk < k_end;
+      cp_async8(as + kk * PITCH + mm, ok ? (TA ? A + gk * s.lda + gm : A + gm * s.lda + gk) : A, ok);
+    }
+#pragma unroll
+    for (int r = 0; r < BN * BK / THREADS; r++) {
+      int kk, nn;
+      slice_elem<TB>(tid + THREADS * r, kk, nn);
+      const int64_t gn = n0 + nn, gk = k0 + kk;
+      const bool ok = gn < s.N && gk < k_end;
+      cp_async8(bs + kk * PITCH + nn, ok ? (TB ? B + gn * s.ldb + gk : B + gk * s.ldb + gn) : B, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  double acc[4][4][2];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
+
+  const int fk = lane & 3, fr = lane >> 2;  // fragment k and row / column
+  // One commit group per slice (empty past the end). At slice t: waiting
+  // until at most STAGES - 2 groups are pending means slice t has landed;
+  // the barrier then makes every thread's copies visible and frees the
+  // stage slice t - 1 used, which the load of slice t + STAGES - 1 refills.
+#pragma unroll
+  for (int p = 0; p < STAGES - 1; p++) {
+    if (p < slices) load(p, p);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int t = 0; t < slices; t++) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(STAGES - 2) : "memory");
+    __syncthreads();
+    const int next = t + STAGES - 1;
+    if (next < slices) load(next, next % STAGES);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    const double* as = As + (t % STAGES) * BK * PITCH + fk * PITCH + wm + fr;
+    const double* bs = Bs + (t % STAGES) * BK * PITCH + fk * PITCH + wn + fr;
+#pragma unroll
+    for (int k4 = 0; k4 < BK; k4 += 4) {
+      double a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) a[i] = as[k4 * PITCH + 8 * i];
+#pragma unroll
+      for (int j = 0; j < 4; j++) b[j] = bs[k4 * PITCH + 8 * j];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) mma_f64(acc[i][j], a[i], b[j]);
+    }
+  }
+
+  // Thread t holds C(8 i + t / 4, 8 j + 2 (t % 4) + {0, 1}) of the warp's tile;
+  // a split unit writes its partial tile, row-major 128 x 128, to ws.
+  double* part = split < 0 ? nullptr : ws + ((tile - plan.whole) * plan.splits + split) * (int64_t)(BM * BN);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int64_t m = m0 + wm + 8 * i + fr;
+    if (m >= s.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int64_t n = n0 + wn + 8 * j + 2 * fk + h;
+        if (n >= s.N) continue;
+        if (part)
+          part[(m - m0) * BN + (n - n0)] = acc[i][j][h];
+        else
+          epi.store(m, n, acc[i][j][h]);
+      }
+    }
+  }
+}
+
+// The split tiles: C = epilogue(sum of a tile's partials in K order).
+__global__ void f64_tail_reduce_kernel(const double* __restrict__ ws, f64k::Plan plan, int64_t tiles, GemmShape s,
+                                       Epi<double> epi) {
+  using namespace f64k;
+  const int64_t total = (tiles - plan.whole) * (int64_t)(BM * BN);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (BM * BN), e = i - r * (BM * BN), tile = plan.whole + r;
+    const int64_t m = (tile / plan.gx) * BM + e / BN, n = (tile % plan.gx) * BN + e % BN;
+    if (m >= s.M || n >= s.N) continue;
+    const double* p = ws + r * plan.splits * (int64_t)(BM * BN) + e;
+    double acc = p[0];
+    for (int k = 1; k < plan.splits; k++) acc = add_rn(acc, p[(int64_t)k * BM * BN]);
+    epi.store(m, n, acc);
+  }
+}
+
+// The unit plan: whole tiles while they fill every SM, then the remaining
+// tiles in the number of K ranges that minimises (rounds of units) x (unit
+// depth) plus the partials' traffic (one CTA per SM; ranges at least 128 deep).
+static f64k::Plan f64_plan(int64_t tiles, int64_t gx, int64_t K, int64_t sms) {
+  using namespace f64k;
+  Plan best;
+  best.gx = gx;
+  best.whole = (int)tiles;
+  best.k_per = K;
+  const int64_t rest = tiles % sms, whole = tiles - rest;
+  if (rest == 0) return best;
+  const double tile_s = 2.0 * BM * BN * (double)K / (37e12 / (double)sms);  // one tile on one SM
+  auto cost = [&](int64_t S) {
+    const int64_t k_per = ceil_div(ceil_div(K, S), (int64_t)BK) * BK, units = rest * ceil_div(K, k_per);
+    const double depth = (double)k_per / (double)K;
+    const double traffic = S > 1 ? 2.0 * (double)units * BM * BN * 8 / 6.5e12 : 0.0;
+    return (double)((whole + sms - 1) / sms) * tile_s + (double)ceil_div(units, sms) * depth * tile_s + traffic;
+  };
+  double best_cost = cost(1);
+  for (int64_t S = 2; S <= 32 && K / S >= 128; S++) {
+    const double c = cost(S);
+    if (c < 0.97 * best_cost) {
+      best_cost = c;
+      best.k_per = ceil_div(ceil_div(K, S), (int64_t)BK) * BK;
+      best.splits = (int)ceil_div(K, best.k_per);
+      best.whole = (int)whole;
+    }
+  }
+  return best;
+}
+
 template <bool TA, bool TB>
 static char* f64_launch(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
   using namespace f64k;
-  const int64_t gx = ceil_div(s.N, BN), gy = ceil_div(s.M, BM);
-  if (gy > 65535) return errorf("gemm_simt: M = %lld is too large", (long long)s.M);
+  const int64_t gx = ceil_div(s.N, BN), gy = ceil_div(s.M, BM), tiles = gx * gy;
   auto kern = gemm_f64_kernel<TA, TB>;
   static bool configured[64] = {};
   if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
     GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
     if (ctx->device >= 0 && ctx->device < 64) configured[ctx->device] = true;
   }
-  int64_t S = gx * gy < ctx->sm_count ? ctx->sm_count / (gx * gy) : 1;
-  S = S < s.K / 256 ? S : s.K / 256;
-  while (S > 1 && (double)S * s.M * s.N * sizeof(double) > (double)(256u << 20)) S /= 2;
-  if (S <= 1) {
-    kern<<<dim3((unsigned)gx, (unsigned)gy), THREADS, SMEM, ctx->stream>>>(s, A, B, epi, s.K, nullptr);
-    GT_LAUNCH_CHECK();
-    return nullptr;
+  Plan plan = f64_plan(tiles, gx, s.K, ctx->sm_count);
+  // keep the partials under 256 MB
+  while (plan.splits > 1 && (double)(tiles - plan.whole) * plan.splits * BM * BN * 8 > (double)(256u << 20)) {
+    plan.k_per = ceil_div(ceil_div(s.K, (int64_t)plan.splits / 2), (int64_t)BK) * BK;
+    plan.splits = (int)ceil_div(s.K, plan.k_per);
   }
-  const int64_t k_per = ceil_div(ceil_div(s.K, S), (int64_t)BK) * BK;
-  const int splits = (int)ceil_div(s.K, k_per);
-  void* ws = nullptr;
-  GT_TRY(scratch(ctx, (size_t)splits * s.M * s.N * sizeof(double), &ws));
-  kern<<<dim3((unsigned)gx, (unsigned)gy, (unsigned)splits), THREADS, SMEM, ctx->stream>>>(s, A, B, epi, k_per,
-                                                                                         (double*)ws);
+  if (plan.splits <= 1) plan.whole = (int)tiles;
+  const int64_t units = plan.whole + (tiles - plan.whole) * plan.splits;
+  if (units > INT32_MAX) return errorf("gemm_f64: %lld output tiles", (long long)units);
+  double* ws = nullptr;
+  if (plan.splits > 1) {
+    void* w = nullptr;
+    GT_TRY(scratch(ctx, (size_t)(tiles - plan.whole) * plan.splits * BM * BN * sizeof(double), &w));
+    ws = (double*)w;
+  }
+  kern<<<(unsigned)units, THREADS, SMEM, ctx->stream>>>(s, A, B, epi, plan, ws);
   count_launch();
   cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) {
-    simt_split_reduce_kernel<double>
-        <<<grid_for(ctx, s.M * s.N, 256), 256, 0, ctx->stream>>>((const double*)ws, splits, s.M, s.N, epi);
+  if (e == cudaSuccess && ws) {
+    f64_tail_reduce_kernel<<<grid_for(ctx, (tiles - plan.whole) * BM * BN, 256), 256, 0, ctx->stream>>>(
+        ws, plan, tiles, s, epi);
     count_launch();
     e = cudaGetLastError();
   }
-  release(ctx, ws);
+  if (ws) release(ctx, ws);
   if (e != cudaSuccess) return cuda_error(e, "gemm_f64 launch", __FILE__, __LINE__);
   return nullptr;
 }
