@@ -210,21 +210,26 @@ static char* simt_launch(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B
 // barrier per slice, so two slices' loads run under the MMAs. Sixteen warps
 // (four per scheduler, which the MMA latency needs): warp w computes rows
 // 32 * (w / 4) .. +32 and columns 32 * (w % 4) .. +32 as 4 x 4 MMA tiles.
-// Fragment reads: thread t takes k = t % 4 and m (or n) = t / 4 of a tile;
-// with rows of 132 doubles those reads fall in distinct banks. An operand
-// whose K index is contiguous in memory is copied as 4 x 4 blocks (four
-// consecutive k of four rows per 16 threads: 32-byte runs in global memory,
-// distinct banks in shared memory).
+// Each operand keeps its memory order in shared memory, so every 32-byte
+// sector a copy brings lands in one contiguous run: an operand whose K index
+// is contiguous is stored [row][k] in rows of 36 doubles, the other [k][row]
+// in rows of 132. Fragment reads (thread t takes k = t % 4 and row t / 4 of
+// an 8 x 4 block) then fall in distinct banks in both layouts. Copies are 16
+// bytes (two elements) when both operands' bases and leading dimensions allow
+// it, else 8.
 //
 // Work units: units 0 .. whole-1 are whole tiles; after them each remaining
 // tile is `splits` units over consecutive K ranges of k_per, whose partial
 // tiles go to ws and are added in K order by f64_tail_reduce_kernel (the last
 // wave's tiles spread over all SMs instead of leaving most of them idle).
 namespace f64k {
-constexpr int BM = 128, BN = 128, BK = 32, PITCH = 132, THREADS = 512;
-constexpr int STAGES = 3;  // slices in the shared-memory ring
-constexpr size_t SMEM = (size_t)STAGES * 2 * BK * PITCH * sizeof(double);
-static_assert(BM * BK % THREADS == 0 && BN * BK % THREADS == 0 && BK % 4 == 0, "copy mapping");
+constexpr int BM = 128, BN = 128, BK = 32, THREADS = 512;
+constexpr int PITCH = 132;  // [k][row] layout: row stride of a k
+constexpr int PK = 36;      // [row][k] layout: row stride of a row
+constexpr int STAGES = 3;   // slices in the shared-memory ring
+constexpr int OPS = BK * PITCH > 128 * PK ? BK * PITCH : 128 * PK;  // doubles per operand and stage
+constexpr size_t SMEM = (size_t)STAGES * 2 * OPS * sizeof(double);
+static_assert(BM == 128 && BN == 128 && 128 * BK % (2 * THREADS) == 0 && BK % 4 == 0, "copy mapping");
 
 struct Plan {
   int whole = 0;        // units that are whole tiles
@@ -238,36 +243,68 @@ __device__ __forceinline__ void cp_async8(double* dst, const double* src, bool v
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
 }
 
+__device__ __forceinline__ void cp_async16(double* dst, const double* src, int bytes) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void mma_f64(double (&c)[2], double a, double b) {
   asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
                : "+d"(c[0]), "+d"(c[1])
                : "d"(a), "d"(b));
 }
 
-// Element e (of the BK x 128 slice a thread block copies) -> (k, row).
-// KC: the operand's K index is contiguous in memory (4 x 4 blocks);
-// otherwise the row index is (one row of 128 per k).
-template <bool KC>
-__device__ __forceinline__ void slice_elem(int e, int& kk, int& rr) {
-  if constexpr (KC) {
-    const int rest = e >> 4;
-    kk = (e & 3) + 4 * (rest % (BK / 4));
-    rr = ((e >> 2) & 3) + 4 * (rest / (BK / 4));
+// Copies the BK x 128 slice [k0, k0 + BK) x [r0, r0 + 128) of an operand
+// into one stage. KC: element (k, r) is at src[r * ld + k] (stored [row][k],
+// rows of PK); otherwise at src[k * ld + r] (stored [k][row], rows of
+// PITCH). Elements past k_end or rlim are zero-filled without being read.
+template <bool KC, bool V16>
+__device__ __forceinline__ void copy_slice(double* dst, const double* __restrict__ src, int64_t ld, int64_t k0,
+                                           int64_t k_end, int64_t r0, int64_t rlim, int tid) {
+  if constexpr (V16) {
+#pragma unroll
+    for (int q = 0; q < 128 * BK / (2 * THREADS); q++) {
+      const int e = tid + THREADS * q;
+      if constexpr (KC) {  // two consecutive k of one row
+        const int r = e / (BK / 2), k = 2 * (e % (BK / 2));
+        const int64_t gr = r0 + r, gk = k0 + k;
+        const int bytes = gr < rlim ? (gk + 1 < k_end ? 16 : gk < k_end ? 8 : 0) : 0;
+        cp_async16(dst + r * PK + k, bytes ? src + gr * ld + gk : src, bytes);
+      } else {  // two consecutive rows of one k
+        const int k = e / 64, r = 2 * (e % 64);
+        const int64_t gr = r0 + r, gk = k0 + k;
+        const int bytes = gk < k_end ? (gr + 1 < rlim ? 16 : gr < rlim ? 8 : 0) : 0;
+        cp_async16(dst + k * PITCH + r, bytes ? src + gk * ld + gr : src, bytes);
+      }
+    }
   } else {
-    kk = e / 128;
-    rr = e % 128;
+#pragma unroll
+    for (int q = 0; q < 128 * BK / THREADS; q++) {
+      const int e = tid + THREADS * q;
+      const int k = KC ? e % BK : e / 128, r = KC ? e / BK : e % 128;
+      const int64_t gr = r0 + r, gk = k0 + k;
+      const bool ok = gr < rlim && gk < k_end;
+      cp_async8(dst + (KC ? r * PK + k : k * PITCH + r), ok ? (KC ? src + gr * ld + gk : src + gk * ld + gr) : src,
+                ok);
+    }
   }
+}
+
+// Element (k, r) of a stage in its layout.
+template <bool KC>
+__device__ __forceinline__ int stage_at(int k, int r) {
+  return KC ? r * PK + k : k * PITCH + r;
 }
 }  // namespace f64k
 
-template <bool TA, bool TB>
+template <bool TA, bool TB, bool V16>
 __global__ void __launch_bounds__(f64k::THREADS, 1)
     gemm_f64_kernel(GemmShape s, const double* __restrict__ A, const double* __restrict__ B, Epi<double> epi,
                     f64k::Plan plan, double* __restrict__ ws) {
   using namespace f64k;
   extern __shared__ double sm[];
-  double* As = sm;                         // [STAGES][BK][PITCH]
-  double* Bs = sm + STAGES * BK * PITCH;   // [STAGES][BK][PITCH]
+  double* As = sm;                 // [STAGES][OPS]
+  double* Bs = sm + STAGES * OPS;  // [STAGES][OPS]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int wm = 32 * (warp >> 2), wn = 32 * (warp & 3);
   const int u = blockIdx.x;
@@ -288,24 +325,8 @@ __global__ void __launch_bounds__(f64k::THREADS, 1)
   // A is K-contiguous unless transposed; B is K-contiguous when transposed.
   auto load = [&](int slice, int stage) {
     const int64_t k0 = k_begin + (int64_t)slice * BK;
-    double* as = As + stage * BK * PITCH;
-    double* bs = Bs + stage * BK * PITCH;
-#pragma unroll
-    for (int r = 0; r < BM * BK / THREADS; r++) {
-      int kk, mm;
-      slice_elem<!TA>(tid + THREADS * r, kk, mm);
-      const int64_t gm = m0 + mm, gk = k0 + kk;
-      const bool ok = gm < s.M && gk < k_end;
-      cp_async8(as + kk * PITCH + mm, ok ? (TA ? A + gk * s.lda + gm : A + gm * s.lda + gk) : A, ok);
-    }
-#pragma unroll
-    for (int r = 0; r < BN * BK / THREADS; r++) {
-      int kk, nn;
-      slice_elem<TB>(tid + THREADS * r, kk, nn);
-      const int64_t gn = n0 + nn, gk = k0 + kk;
-      const bool ok = gn < s.N && gk < k_end;
-      cp_async8(bs + kk * PITCH + nn, ok ? (TB ? B + gn * s.ldb + gk : B + gk * s.ldb + gn) : B, ok);
-    }
+    copy_slice<!TA, V16>(As + stage * OPS, A, s.lda, k0, k_end, m0, s.M, tid);
+    copy_slice<TB, V16>(Bs + stage * OPS, B, s.ldb, k0, k_end, n0, s.N, tid);
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
@@ -331,15 +352,15 @@ __global__ void __launch_bounds__(f64k::THREADS, 1)
     const int next = t + STAGES - 1;
     if (next < slices) load(next, next % STAGES);
     else asm volatile("cp.async.commit_group;" ::: "memory");
-    const double* as = As + (t % STAGES) * BK * PITCH + fk * PITCH + wm + fr;
-    const double* bs = Bs + (t % STAGES) * BK * PITCH + fk * PITCH + wn + fr;
+    const double* as = As + (t % STAGES) * OPS + stage_at<!TA>(fk, wm + fr);
+    const double* bs = Bs + (t % STAGES) * OPS + stage_at<TB>(fk, wn + fr);
 #pragma unroll
     for (int k4 = 0; k4 < BK; k4 += 4) {
       double a[4], b[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++) a[i] = as[k4 * PITCH + 8 * i];
+      for (int i = 0; i < 4; i++) a[i] = as[stage_at<!TA>(k4, 8 * i)];
 #pragma unroll
-      for (int j = 0; j < 4; j++) b[j] = bs[k4 * PITCH + 8 * j];
+      for (int j = 0; j < 4; j++) b[j] = bs[stage_at<TB>(k4, 8 * j)];
 #pragma unroll
       for (int i = 0; i < 4; i++)
 #pragma unroll
@@ -416,11 +437,11 @@ static f64k::Plan f64_plan(int64_t tiles, int64_t gx, int64_t K, int64_t sms) {
   return best;
 }
 
-template <bool TA, bool TB>
+template <bool TA, bool TB, bool V16>
 static char* f64_launch(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
   using namespace f64k;
   const int64_t gx = ceil_div(s.N, BN), gy = ceil_div(s.M, BM), tiles = gx * gy;
-  auto kern = gemm_f64_kernel<TA, TB>;
+  auto kern = gemm_f64_kernel<TA, TB, V16>;
   static bool configured[64] = {};
   if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
     GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM));
@@ -455,9 +476,18 @@ static char* f64_launch(gt_ctx* ctx, const GemmShape& s, const double* A, const 
   return nullptr;
 }
 
+template <bool V16>
+static char* f64_layouts(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
+  if (s.trans_a)
+    return s.trans_b ? f64_launch<true, true, V16>(ctx, s, A, B, epi) : f64_launch<true, false, V16>(ctx, s, A, B, epi);
+  return s.trans_b ? f64_launch<false, true, V16>(ctx, s, A, B, epi) : f64_launch<false, false, V16>(ctx, s, A, B, epi);
+}
+
+// 16-byte copies need 16-byte aligned bases and even leading dimensions
+// (every copied pair then starts on a 16-byte boundary).
 static char* f64_main(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
-  if (s.trans_a) return s.trans_b ? f64_launch<true, true>(ctx, s, A, B, epi) : f64_launch<true, false>(ctx, s, A, B, epi);
-  return s.trans_b ? f64_launch<false, true>(ctx, s, A, B, epi) : f64_launch<false, false>(ctx, s, A, B, epi);
+  const bool v16 = !((uintptr_t)A & 15) && !((uintptr_t)B & 15) && !(s.lda & 1) && !(s.ldb & 1);
+  return v16 ? f64_layouts<true>(ctx, s, A, B, epi) : f64_layouts<false>(ctx, s, A, B, epi);
 }
 
 template <typename T>
