@@ -103,6 +103,14 @@ template <>
 char* gemm<double>(gt_ctx* ctx, const GemmShape& s, const double* A, const double* B, const Epi<double>& epi) {
   if (g_gemm_path == 2) return errorf("gemm: the tcgen05 path has no float64 kind");
   return timed_gemm(ctx, s, [&] {
+    if (g_gemm_path == 0) {  // the thin kernels only on the automatic path
+      bool done = false;
+      char* e = gemm_thin<double>(ctx, s, A, B, epi, &done);
+      if (e || done) {
+        g_gemm_taken = 6;
+        return e;
+      }
+    }
     g_gemm_taken = 1;
     return gemm_simt<double>(ctx, s, A, B, epi);
   });
@@ -110,7 +118,17 @@ char* gemm<double>(gt_ctx* ctx, const GemmShape& s, const double* A, const doubl
 
 template <>
 char* gemm<float>(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {
-  return timed_gemm(ctx, s, [&] { return gemm_f32(ctx, s, A, B, epi); });
+  return timed_gemm(ctx, s, [&] {
+    if (g_gemm_path == 0) {  // the thin kernels only on the automatic path
+      bool done = false;
+      char* e = gemm_thin<float>(ctx, s, A, B, epi, &done);
+      if (e || done) {
+        g_gemm_taken = 6;
+        return e;
+      }
+    }
+    return gemm_f32(ctx, s, A, B, epi);
+  });
 }
 
 static char* gemm_f32(gt_ctx* ctx, const GemmShape& s, const float* A, const float* B, const Epi<float>& epi) {

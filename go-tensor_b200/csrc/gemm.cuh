@@ -159,6 +159,12 @@ char* timed_gemm_like(gt_ctx* ctx, int64_t M, int64_t N, int64_t K, int path, ch
 // writes its column partial sums (Epi::colsum_ws).
 bool tc_writes_colsums(const Epi<float>& epi, int64_t n_cols);
 
+// Thin GEMMs (gemm_simt.cu): N <= 32 with B transposed (a classifier's
+// forward), or M <= 32 with A transposed and a plain epilogue (its weight
+// gradient). *done = false when the shape does not qualify.
+template <typename T>
+char* gemm_thin(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>& epi, bool* done);
+
 // Dispatches to the fastest qualifying path.
 template <typename T>
 char* gemm(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>& epi);

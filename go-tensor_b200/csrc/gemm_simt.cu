@@ -13,6 +13,8 @@
 // reads contiguous rows); each thread accumulates a TM x TN block in
 // registers with FMA in the dtype. Loads are coalesced along whichever of
 // (m, k) / (k, n) is contiguous for the transpose flags.
+#include <algorithm>
+
 #include "gemm.cuh"
 
 namespace gt {
@@ -146,6 +148,131 @@ __global__ void gemm_smallk_kernel(GemmShape s, const T* __restrict__ A, const T
     for (int j = 0; j < 4; j++) epi.store(m, n + j, acc[j]);
   }
 }
+
+// Thin GEMMs, where a classifier's 10 classes make one dimension tiny and
+// the cost is streaming the other operand once:
+//
+// gemm_thin_n_kernel, N <= NN (the forward x @ W^T of a classifier): a warp
+// per row of C; lane l accumulates k = l, l + 32, ... of all N dot products
+// (A's row read once, coalesced; W's N rows stay in L1), then the lanes' sums
+// are added by a xor butterfly (the same order on every lane) and lane n
+// stores C(m, n) through the epilogue.
+template <typename T, int NN>
+__global__ void __launch_bounds__(256) gemm_thin_n_kernel(GemmShape s, const T* __restrict__ A,
+                                                          const T* __restrict__ B, Epi<T> epi) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int N = (int)s.N;
+  for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < s.M; m += warps) {
+    T acc[NN];
+#pragma unroll
+    for (int n = 0; n < NN; n++) acc[n] = (T)0;
+    const T* a = A + m * s.lda;
+#pragma unroll 2
+    for (int64_t k = lane; k < s.K; k += 32) {
+      const T av = a[k];
+#pragma unroll
+      for (int n = 0; n < NN; n++)
+        if (n < N) acc[n] = fma(av, __ldg(B + n * s.ldb + k), acc[n]);
+    }
+    T mine = (T)0;
+#pragma unroll
+    for (int n = 0; n < NN; n++) {
+      if (n < N) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc[n] = acc[n] + __shfl_xor_sync(0xffffffffu, acc[n], off);
+      }
+      if (lane == n) mine = acc[n];
+    }
+    if (lane < N) epi.store(m, lane, mine);
+  }
+}
+
+// gemm_thin_m_kernel, M <= MM (a classifier's weight gradient dY^T @ X): a
+// thread per column n of C over the block's K range; the range's rows of A
+// (M values each) are staged in shared memory and broadcast, B's row is read
+// coalesced. part[y][m][n] holds the partial sums of K range y; the ranges are
+// added in order afterwards (column_sums_kernel over the y rows).
+template <typename T, int MM>
+__global__ void __launch_bounds__(256) gemm_thin_m_kernel(GemmShape s, const T* __restrict__ A,
+                                                          const T* __restrict__ B, int64_t k_per,
+                                                          T* __restrict__ part) {
+  __shared__ T as[64][MM];
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t k0 = (int64_t)blockIdx.y * k_per, k1 = k0 + k_per < s.K ? k0 + k_per : s.K;
+  const int M = (int)s.M;
+  T acc[MM];
+#pragma unroll
+  for (int m = 0; m < MM; m++) acc[m] = (T)0;
+  for (int64_t kc = k0; kc < k1; kc += 64) {
+    const int kn = (int)(k1 - kc < 64 ? k1 - kc : 64);
+    __syncthreads();
+    for (int e = threadIdx.x; e < 64 * MM; e += blockDim.x) {
+      const int kk = e / MM, mm = e - kk * MM;
+      as[kk][mm] = kk < kn && mm < M ? A[(kc + kk) * s.lda + mm] : (T)0;
+    }
+    __syncthreads();
+    if (n < s.N) {
+      const T* b = B + kc * s.ldb + n;
+#pragma unroll 4
+      for (int kk = 0; kk < kn; kk++) {
+        const T bv = b[(int64_t)kk * s.ldb];
+#pragma unroll
+        for (int m = 0; m < MM; m++) acc[m] = fma(as[kk][m], bv, acc[m]);
+      }
+    }
+  }
+  if (n < s.N)
+#pragma unroll
+    for (int m = 0; m < MM; m++)
+      if (m < M) part[((int64_t)blockIdx.y * M + m) * s.N + n] = acc[m];
+}
+
+template <typename T>
+char* gemm_thin(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const Epi<T>& epi, bool* done) {
+  *done = false;
+  if (s.M <= 0 || s.N <= 0 || s.K <= 0) return nullptr;
+  const bool generic_out = epi.nchw_L == 0 && !epi.col_major && !epi.pos_major && !epi.colsum_ws && !epi.bits_out &&
+                           !epi.pool_idx && !epi.dbits;
+  if (!generic_out) return nullptr;
+  if (s.N <= 32 && !s.trans_a && s.trans_b && s.M >= 16 && s.K >= 32) {
+    const int grid = (int)std::min<int64_t>(ceil_div(s.M, 8), (int64_t)ctx->sm_count * 8);
+    if (s.N <= 16)
+      gemm_thin_n_kernel<T, 16><<<grid, 256, 0, ctx->stream>>>(s, A, B, epi);
+    else
+      gemm_thin_n_kernel<T, 32><<<grid, 256, 0, ctx->stream>>>(s, A, B, epi);
+    GT_LAUNCH_CHECK();
+    *done = true;
+    return nullptr;
+  }
+  const bool plain = !epi.bias && epi.act == GT_ACT_NONE && !epi.dmask && epi.ldc == s.N;
+  if (s.M <= 32 && s.trans_a && !s.trans_b && plain && s.N >= 64 && s.K >= 64) {
+    const int64_t gx = ceil_div(s.N, 256);
+    int64_t S = ceil_div(4 * (int64_t)ctx->sm_count, gx);
+    S = std::min<int64_t>(S, ceil_div(s.K, 32));
+    const int64_t k_per = ceil_div(s.K, S);
+    S = ceil_div(s.K, k_per);
+    if (S > 65535) return nullptr;
+    void* part = nullptr;
+    GT_TRY(scratch(ctx, (size_t)(S * s.M * s.N) * sizeof(T), &part));
+    if (s.M <= 16)
+      gemm_thin_m_kernel<T, 16><<<dim3((unsigned)gx, (unsigned)S), 256, 0, ctx->stream>>>(s, A, B, k_per, (T*)part);
+    else
+      gemm_thin_m_kernel<T, 32><<<dim3((unsigned)gx, (unsigned)S), 256, 0, ctx->stream>>>(s, A, B, k_per, (T*)part);
+    column_sums_kernel<T><<<(unsigned)ceil_div(s.M * s.N, 32), 1024, 0, ctx->stream>>>((const T*)part, S, s.M * s.N,
+                                                                                     epi.out);
+    count_launch(2);
+    cudaError_t e = cudaGetLastError();
+    release(ctx, part);
+    if (e != cudaSuccess) return cuda_error(e, "gemm_thin_m launch", __FILE__, __LINE__);
+    *done = true;
+    return nullptr;
+  }
+  return nullptr;
+}
+
+template char* gemm_thin<float>(gt_ctx*, const GemmShape&, const float*, const float*, const Epi<float>&, bool*);
+template char* gemm_thin<double>(gt_ctx*, const GemmShape&, const double*, const double*, const Epi<double>&, bool*);
 
 // out(m, n) = epilogue(sum of the splits' partials in split order).
 template <typename T>

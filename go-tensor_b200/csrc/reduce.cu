@@ -64,6 +64,7 @@ __global__ void reduce_cols_kernel(const T* __restrict__ x, T* __restrict__ out,
     int64_t lo = s * chunk, hi = lo + chunk < n ? lo + chunk : n;
     const T* xp = x + (o * n) * inner + i;
     T acc = reduce_identity<T>(op);
+#pragma unroll 8
     for (int64_t k = lo; k < hi; k++) acc = reduce_op(op, acc, xp[k * inner]);
     out[t] = acc;
   }
@@ -114,8 +115,11 @@ static char* launch_reduce(gt_ctx* ctx, int op, const T* x, T* out, int64_t oute
     GT_LAUNCH_CHECK();
     if (nsplit > 1) {  // partials are (nsplit, outer*inner): reduce the middle axis
       int64_t cols = outer * inner;
-      reduce_cols_kernel<T><<<grid_for(ctx, cols, threads), threads, 0, ctx->stream>>>(partials, out, 1, nsplit, cols,
-                                                                                        op, nsplit, 1);
+      if (op == GT_SUM)  // 32 warps per 32 columns, in a fixed order
+        column_sums_kernel<T><<<(unsigned)ceil_div(cols, 32), 1024, 0, ctx->stream>>>(partials, nsplit, cols, out);
+      else
+        reduce_cols_kernel<T><<<grid_for(ctx, cols, threads), threads, 0, ctx->stream>>>(partials, out, 1, nsplit,
+                                                                                          cols, op, nsplit, 1);
       GT_LAUNCH_CHECK();
     }
   }

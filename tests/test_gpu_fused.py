@@ -62,7 +62,9 @@ def apply_act(t, act):
 
 @pytest.mark.parametrize("dt,npdt,tol", DT)
 @pytest.mark.parametrize("act", [0, 1, 2, 3])
-@pytest.mark.parametrize("mkn", [(64, 784, 128), (257, 129, 65), (1024, 512, 1000), (5, 3, 7)])
+# the last four: classifiers (N <= 32 runs the thin kernel: a warp per row)
+@pytest.mark.parametrize("mkn", [(64, 784, 128), (257, 129, 65), (1024, 512, 1000), (5, 3, 7), (4096, 1024, 10),
+                                 (256, 128, 10), (1000, 2048, 10), (100, 64, 20)])
 def test_linear_fwd(dt, npdt, tol, act, mkn):
     M, K, N = mkn
     rng = np.random.default_rng(M + K + N)
@@ -78,7 +80,10 @@ def test_linear_fwd(dt, npdt, tol, act, mkn):
 
 @pytest.mark.parametrize("dt,npdt,tol", DT)
 @pytest.mark.parametrize("act_prev", [0, 1, 2, 3])
-@pytest.mark.parametrize("mkn", [(64, 784, 128), (257, 129, 65), (512, 1024, 1000)])
+# the last three: classifiers (dW with 10 or 20 rows runs the thin kernel: a
+# thread per column, K split, partials added in order)
+@pytest.mark.parametrize("mkn", [(64, 784, 128), (257, 129, 65), (512, 1024, 1000), (4096, 1024, 10), (64, 128, 10),
+                                 (300, 96, 20)])
 def test_linear_bwd(dt, npdt, tol, act_prev, mkn):
     M, K, N = mkn
     rng = np.random.default_rng(M * 3 + K + N)
