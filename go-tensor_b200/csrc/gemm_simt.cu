@@ -125,9 +125,19 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN), (sizeof(T) == 4 && BM *
   }
 }
 
+// Four consecutive elements from a 4-element-aligned address, as vectors.
+__device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
+  const float4 q = __ldg((const float4*)p);
+  v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+}
+__device__ __forceinline__ void load4(const double* p, double (&v)[4]) {
+  const double2 q0 = __ldg((const double2*)p), q1 = __ldg((const double2*)p + 1);
+  v[0] = q0.x, v[1] = q0.y, v[2] = q1.x, v[3] = q1.y;
+}
+
 // Small K (the input gradient of a classifier: K = its 10 classes): C = A
 // (M x K, row-major) @ B (K x N, row-major), a thread per four consecutive
-// columns of a row. B's row k is read as one 16-byte vector per thread
+// columns of a row. B's row k is read as one four-element vector per thread
 // (coalesced), A(m, k) is the same for the warp's threads (broadcast), and
 // each output is the same FMA chain over k, in order, as gemm_simt_kernel's,
 // so the results are identical; the outputs leave as contiguous runs.
@@ -138,11 +148,13 @@ __global__ void gemm_smallk_kernel(GemmShape s, const T* __restrict__ A, const T
     const int64_t m = u / qn, n = 4 * (u - m * qn);
     T acc[4] = {(T)0, (T)0, (T)0, (T)0};
     const T* a = A + m * s.lda;
+#pragma unroll 4
     for (int64_t k = 0; k < s.K; k++) {
       const T av = __ldg(a + k);
-      const T* b = B + k * s.ldb + n;
+      T bv[4];
+      load4(B + k * s.ldb + n, bv);
 #pragma unroll
-      for (int j = 0; j < 4; j++) acc[j] = fma(av, __ldg(b + j), acc[j]);
+      for (int j = 0; j < 4; j++) acc[j] = fma(av, bv[j], acc[j]);
     }
 #pragma unroll
     for (int j = 0; j < 4; j++) epi.store(m, n + j, acc[j]);
@@ -347,8 +359,8 @@ static char* simt_launch(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B
 //
 // Work units: units 0 .. whole-1 are whole tiles; after them each remaining
 // tile is `splits` units over consecutive K ranges of k_per, whose partial
-// tiles go to ws and are added in K order by f64_tail_reduce_kernel (the last
-// wave's tiles spread over all SMs instead of leaving most of them idle).
+// tiles go to ws and are added in K order by f64_tail_reduce_kernel, so the
+// last wave's tiles spread over all SMs instead of leaving most of them idle.
 namespace f64k {
 constexpr int BM = 128, BN = 128, BK = 32, THREADS = 512;
 constexpr int PITCH = 132;  // [k][row] layout: row stride of a k
@@ -623,7 +635,7 @@ char* gemm_simt(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const E
   // K of a few classes over a wide output (row-major operands, N a multiple
   // of 4): the output is the cost, written in contiguous runs
   if (s.K <= 32 && !s.trans_a && !s.trans_b && s.N % 4 == 0 && s.ldb % 4 == 0 && s.M * s.N >= 4096 &&
-      epi.nchw_L == 0 && !epi.col_major) {
+      !((uintptr_t)B & (4 * sizeof(T) - 1)) && epi.nchw_L == 0 && !epi.col_major) {
     gemm_smallk_kernel<T><<<grid_for(ctx, s.M * s.N / 4, 256), 256, 0, ctx->stream>>>(s, A, B, epi);
     GT_LAUNCH_CHECK();
     return nullptr;

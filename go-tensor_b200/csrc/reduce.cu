@@ -63,10 +63,16 @@ __global__ void reduce_cols_kernel(const T* __restrict__ x, T* __restrict__ out,
     int64_t o = c / inner, i = c - o * inner;
     int64_t lo = s * chunk, hi = lo + chunk < n ? lo + chunk : n;
     const T* xp = x + (o * n) * inner + i;
-    T acc = reduce_identity<T>(op);
-#pragma unroll 8
-    for (int64_t k = lo; k < hi; k++) acc = reduce_op(op, acc, xp[k * inner]);
-    out[t] = acc;
+    // four interleaved accumulators, so that four loads are in flight, added
+    // in a fixed order at the end
+    T a0 = reduce_identity<T>(op), a1 = a0, a2 = a0, a3 = a0;
+    int64_t k = lo;
+    for (; k + 4 <= hi; k += 4) {
+      const T v0 = xp[k * inner], v1 = xp[(k + 1) * inner], v2 = xp[(k + 2) * inner], v3 = xp[(k + 3) * inner];
+      a0 = reduce_op(op, a0, v0), a1 = reduce_op(op, a1, v1), a2 = reduce_op(op, a2, v2), a3 = reduce_op(op, a3, v3);
+    }
+    for (; k < hi; k++) a0 = reduce_op(op, a0, xp[k * inner]);
+    out[t] = reduce_op(op, reduce_op(op, a0, a1), reduce_op(op, a2, a3));
   }
 }
 
