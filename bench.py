@@ -454,9 +454,9 @@ def l2_note(key, model):
 
 # dram__bytes_read.sum + dram__bytes_write.sum of the GEMM launches of one
 # training step of the wide MLP, from one ncu capture of
-# `bench.py --steps 1 --warmup 3 --skip-cpu` (launches 19-37: the second
-# warm-up step, replayed from the CUDA graph).
-GEMM_TRAFFIC_BYTES_PER_STEP = {"wide_mlp": 4_224_623_616}
+# `bench.py --workload wide_mlp --steps 1 --warmup 3 --skip-cpu` (launches
+# 16-31: the second warm-up step, replayed from the CUDA graph).
+GEMM_TRAFFIC_BYTES_PER_STEP = {"wide_mlp": 4_234_614_272}
 GEMM_LAUNCHES_PER_STEP = {"wide_mlp": 8}
 # The wide MLP's SGD update: DRAM traffic of its launch in the same capture.
 OPT_TRAFFIC_BYTES = {"wide_mlp": 698_175_488}

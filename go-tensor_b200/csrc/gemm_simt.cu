@@ -164,28 +164,35 @@ __global__ void gemm_smallk_kernel(GemmShape s, const T* __restrict__ A, const T
 // Thin GEMMs, where a classifier's 10 classes make one dimension tiny and
 // the cost is streaming the other operand once:
 //
-// gemm_thin_n_kernel, N <= NN (the forward x @ W^T of a classifier): a warp
-// per row of C; lane l accumulates k = l, l + 32, ... of all N dot products
-// (A's row read once, coalesced; W's N rows stay in L1), then the lanes' sums
-// are added by a xor butterfly (the same order on every lane) and lane n
-// stores C(m, n) through the epilogue.
+// gemm_thin_n_kernel, N <= NN (the forward x @ W^T of a classifier): WR
+// warps per row of C (8 / WR rows per 256-thread block), warp w of a row
+// taking the w-th of WR equal K ranges; lane l accumulates k = l, l + 32, ...
+// of its range for all N dot products (A's row read once, coalesced; W's N
+// rows stay in L1). The lanes' sums are added by a xor butterfly (the same
+// order on every lane), the row's WR warp sums in warp order through shared
+// memory, and lane n stores C(m, n) through the epilogue.
 template <typename T, int NN>
 __global__ void __launch_bounds__(256) gemm_thin_n_kernel(GemmShape s, const T* __restrict__ A,
-                                                          const T* __restrict__ B, Epi<T> epi) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+                                                          const T* __restrict__ B, Epi<T> epi, int WR) {
+  __shared__ T part[8][NN];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rows_per_block = 8 / WR, r = warp / WR, w = warp - r * WR;
   const int N = (int)s.N;
-  for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < s.M; m += warps) {
+  const int64_t kr = (s.K + WR - 1) / WR, k_lo = w * kr, k_hi = k_lo + kr < s.K ? k_lo + kr : s.K;
+  for (int64_t m0 = (int64_t)blockIdx.x * rows_per_block; m0 < s.M; m0 += (int64_t)gridDim.x * rows_per_block) {
+    const int64_t m = m0 + r;
     T acc[NN];
 #pragma unroll
     for (int n = 0; n < NN; n++) acc[n] = (T)0;
-    const T* a = A + m * s.lda;
+    if (m < s.M) {
+      const T* a = A + m * s.lda;
 #pragma unroll 2
-    for (int64_t k = lane; k < s.K; k += 32) {
-      const T av = a[k];
+      for (int64_t k = k_lo + lane; k < k_hi; k += 32) {
+        const T av = a[k];
 #pragma unroll
-      for (int n = 0; n < NN; n++)
-        if (n < N) acc[n] = fma(av, __ldg(B + n * s.ldb + k), acc[n]);
+        for (int n = 0; n < NN; n++)
+          if (n < N) acc[n] = fma(av, __ldg(B + n * s.ldb + k), acc[n]);
+      }
     }
     T mine = (T)0;
 #pragma unroll
@@ -196,7 +203,18 @@ __global__ void __launch_bounds__(256) gemm_thin_n_kernel(GemmShape s, const T* 
       }
       if (lane == n) mine = acc[n];
     }
-    if (lane < N) epi.store(m, lane, mine);
+    if (WR == 1) {
+      if (m < s.M && lane < N) epi.store(m, lane, mine);
+      continue;
+    }
+    if (lane < N) part[warp][lane] = mine;
+    __syncthreads();
+    if (w == 0 && m < s.M && lane < N) {
+      T sum = part[warp][lane];
+      for (int j = 1; j < WR; j++) sum = sum + part[warp + j][lane];
+      epi.store(m, lane, sum);
+    }
+    __syncthreads();
   }
 }
 
@@ -248,11 +266,16 @@ char* gemm_thin(gt_ctx* ctx, const GemmShape& s, const T* A, const T* B, const E
                            !epi.pool_idx && !epi.dbits;
   if (!generic_out) return nullptr;
   if (s.N <= 32 && !s.trans_a && s.trans_b && s.M >= 16 && s.K >= 32) {
-    const int grid = (int)std::min<int64_t>(ceil_div(s.M, 8), (int64_t)ctx->sm_count * 8);
+    // warps per row: K ranges of at least 256, while the rows alone leave
+    // fewer than 32 warps per SM
+    int wr = 1;
+    while (wr < 8 && s.K / (2 * wr) >= 256 && s.M * wr < 32 * (int64_t)ctx->sm_count) wr *= 2;
+    const int64_t rows_per_block = 8 / wr;
+    const int grid = (int)std::min<int64_t>(ceil_div(s.M, rows_per_block), (int64_t)ctx->sm_count * 8);
     if (s.N <= 16)
-      gemm_thin_n_kernel<T, 16><<<grid, 256, 0, ctx->stream>>>(s, A, B, epi);
+      gemm_thin_n_kernel<T, 16><<<grid, 256, 0, ctx->stream>>>(s, A, B, epi, wr);
     else
-      gemm_thin_n_kernel<T, 32><<<grid, 256, 0, ctx->stream>>>(s, A, B, epi);
+      gemm_thin_n_kernel<T, 32><<<grid, 256, 0, ctx->stream>>>(s, A, B, epi, wr);
     GT_LAUNCH_CHECK();
     *done = true;
     return nullptr;

@@ -1306,30 +1306,48 @@ __global__ void splitk_reduce_colsum_kernel(const float* __restrict__ ws, SplitP
   }
 }
 
-// The same with a ReLU bit mask: a thread finishes one column of 32 rows of
-// a split tile (consecutive threads, consecutive columns) and writes its word.
-__global__ void splitk_reduce_bits_kernel(const float* __restrict__ ws, SplitPlan sp, int tiles, int n_tiles,
-                                          int64_t M, int64_t N, Epi<float> epi) {
+// The split tiles of a GEMM whose epilogue also writes the ReLU bit mask: a
+// 256-thread block per 32 x 32 block of a split tile; thread (ty, tx) adds the
+// partials of rows ty, ty + 8, ty + 16, ty + 24 of column tx in split order
+// (coalesced along the columns), stores the finished values, and leaves their
+// signs in shared memory, from which warp 0 builds the column words.
+__global__ void __launch_bounds__(256) splitk_reduce_bits_kernel(const float* __restrict__ ws, SplitPlan sp,
+                                                                 int tiles, int n_tiles, int64_t M, int64_t N,
+                                                                 Epi<float> epi) {
+  __shared__ uint32_t pos[32][33];
   const int rest = tiles - sp.whole;
   const int64_t total = (int64_t)rest * TILE_ELEMS;
-  const int64_t units = total / 32;  // (tile, 32-row block, column)
-  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
-    const int r = (int)(u / (TILE_ELEMS / 32));
-    const int64_t v = u - (int64_t)r * (TILE_ELEMS / 32);
-    const int rb = (int)(v / BN), c = (int)(v % BN);
+  const int64_t blocks = total / 1024;  // (tile, 32-row block, 32-column block)
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int64_t u = blockIdx.x; u < blocks; u += gridDim.x) {
+    const int r = (int)(u / (TILE_ELEMS / 1024));
+    const int v = (int)(u - (int64_t)r * (TILE_ELEMS / 1024));
+    const int rb = v / (BN / 32), cb = v % (BN / 32);
     const int t = sp.whole + r;
-    const int64_t m0 = (int64_t)(t / n_tiles) * 2 * BM + 32 * rb, n = (int64_t)(t % n_tiles) * BN + c;
-    if (m0 >= M || n >= N) continue;
-    uint32_t w = 0;
-    for (int j = 0; j < 32 && m0 + j < M; j++) {
-      const int64_t i = (int64_t)r * TILE_ELEMS + (int64_t)(32 * rb + j) * BN + c;
-      float acc = ws[i];
-      for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
-      const float y = epi.finish(m0 + j, n, acc);
-      epi.put(m0 + j, n, y);
-      w |= (uint32_t)(y > 0.0f) << j;
+    const int64_t m0 = (int64_t)(t / n_tiles) * 2 * BM + 32 * rb, n = (int64_t)(t % n_tiles) * BN + 32 * cb + tx;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int j = ty + 8 * q;
+      uint32_t bit = 0;
+      if (m0 + j < M && n < N) {
+        const int64_t i = (int64_t)r * TILE_ELEMS + (int64_t)(32 * rb + j) * BN + 32 * cb + tx;
+        float acc = ws[i];
+#pragma unroll 4
+        for (int k = 1; k < sp.splits; k++) acc = __fadd_rn(acc, ws[(int64_t)k * total + i]);
+        const float y = epi.finish(m0 + j, n, acc);
+        epi.put(m0 + j, n, y);
+        bit = y > 0.0f;
+      }
+      pos[j][tx] = bit;
     }
-    epi.bits_out[(m0 >> 5) * epi.ldw + n] = w;
+    __syncthreads();
+    if (ty == 0 && m0 < M && n < N) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int j = 0; j < 32; j++) w |= pos[j][tx] << j;
+      epi.bits_out[(m0 >> 5) * epi.ldw + n] = w;
+    }
+    __syncthreads();
   }
 }
 
@@ -1410,7 +1428,8 @@ static char* run_planned(gt_ctx* ctx, const GemmShape& s, const Epi<float>& epi,
       splitk_reduce_pool_kernel<TBN><<<grid_for(ctx, rest * TE / 4, 256), 256, 0, ctx->stream>>>(
           sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi, ga->rows_pi, ga->OW);
     else if (epi.bits_out)
-      splitk_reduce_bits_kernel<<<grid_for(ctx, rest * TE / 32, 256), 256, 0, ctx->stream>>>(
+      splitk_reduce_bits_kernel<<<(unsigned)std::min<int64_t>(rest * TE / 1024, (int64_t)ctx->sm_count * 8), 256, 0,
+                                  ctx->stream>>>(
           sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
     else if (epi.colsum_ws)
       splitk_reduce_colsum_kernel<TBN><<<grid_for(ctx, rest * TE / 32, 256), 256, 0, ctx->stream>>>(
