@@ -558,7 +558,8 @@ def step_roofline(lib, model, steps, wl, key):
     names = {1: "SIMT (FFMA; float64 on DFMA or the FP64 tensor path, mma.sync f64)", 2: "tcgen05 3xTF32",
              4: "tcgen05 3xTF32 implicit-GEMM convolution",
              5: "SIMT weight gradient from the pooled gradient (first conv; window maxima only)",
-             6: "SIMT thin GEMM (a classifier's 10 classes: a warp per row, or a thread per column)"}
+             6: "SIMT thin GEMM (a classifier's 10 classes: a warp per row, or a thread per column)",
+             7: "SIMT direct convolution + ReLU + 2x2 pool (first conv, K = C*9)"}
     breakdown = {k: {"launches_per_step": v["launches"] // steps, "ms_per_launch": v["ms"] / v["launches"],
                      "tflops": v["flops"] * v["launches"] / (v["ms"] / 1e3) / 1e12,
                      "path": names.get(v["path"], str(v["path"]))} for k, v in shapes.items()}

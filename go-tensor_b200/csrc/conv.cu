@@ -495,6 +495,129 @@ static char* pool_wgrad_dispatch(const PoolWgradArgs& a) {
   return pool_wgrad_launch<T, 32, 0>(a.ctx, x, grad, a.idx, pooled, a.relu, *a.g, *a.pg, a.O, pw, pb);
 }
 
+// Conv2d (3 x 3 windows, stride 1, at most CM input channels: a first
+// convolution) [+ ReLU] then 2 x 2 / stride-2 max pooling, computed directly:
+// at K = C*9 a GEMM tile has nothing to hide its epilogue behind, and only the
+// pooled values are needed. A block stages one image (zero-padded), the
+// weights and the biases in shared memory; a thread takes a pooled position,
+// keeps the 4 x 4 x C input region its window's four patches cover in
+// registers, and for each output channel forms the four outputs as FMA
+// chains over (c, kh, kw) in order (the weights broadcast to the warp), adds
+// the bias, applies ReLU and stores the first maximum (MaxPool2d's v > best
+// rule, offsets kh * 2 + kw) and its offset.
+template <typename T, int CM>
+__global__ void __launch_bounds__(256)
+    conv_pool_small_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias, int relu,
+                           int C, int H, int W, int pad, int O, int PH, int PW, T* __restrict__ pooled,
+                           uint8_t* __restrict__ idx) {
+  extern __shared__ __align__(16) unsigned char conv_pool_smem[];
+  const int Hs = H + 2 * pad, Ws = W + 2 * pad, plane = Hs * Ws, CKK = C * 9;
+  T* wsm = reinterpret_cast<T*>(conv_pool_smem);  // O x CKK weights
+  T* bsm = wsm + O * CKK;                         // O biases
+  T* xs = bsm + O;                                // C x Hs x Ws padded image
+  const int tid = threadIdx.x;
+  const int64_t n = blockIdx.y;
+  const T* xn = x + n * C * H * W;
+  for (int e = tid; e < C * plane; e += blockDim.x) {
+    const int c = e / plane, r = e - c * plane, hs = r / Ws, ws = r - hs * Ws, h = hs - pad, ww = ws - pad;
+    xs[e] = (h >= 0 && h < H && ww >= 0 && ww < W) ? xn[((int64_t)c * H + h) * W + ww] : (T)0;
+  }
+  for (int e = tid; e < O * CKK; e += blockDim.x) wsm[e] = w[e];
+  for (int e = tid; e < O; e += blockDim.x) bsm[e] = bias ? bias[e] : (T)0;
+  __syncthreads();
+  const int P = PH * PW;
+  for (int pp = blockIdx.x * blockDim.x + tid; pp < P; pp += gridDim.x * blockDim.x) {
+    const int ph = pp / PW, pw = pp - ph * PW;
+    T v[CM][4][4];
+#pragma unroll
+    for (int c = 0; c < CM; c++)
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) v[c][r][q] = c < C ? xs[c * plane + (2 * ph + r) * Ws + 2 * pw + q] : (T)0;
+    for (int o = 0; o < O; o++) {
+      const T* wo = wsm + o * CKK;
+      T a[4] = {(T)0, (T)0, (T)0, (T)0};
+#pragma unroll
+      for (int c = 0; c < CM; c++) {
+        if (c >= C) break;
+#pragma unroll
+        for (int kh = 0; kh < 3; kh++)
+#pragma unroll
+          for (int kw = 0; kw < 3; kw++) {
+            const T wv = wo[c * 9 + kh * 3 + kw];
+            a[0] = fma(v[c][kh][kw], wv, a[0]);
+            a[1] = fma(v[c][kh][kw + 1], wv, a[1]);
+            a[2] = fma(v[c][kh + 1][kw], wv, a[2]);
+            a[3] = fma(v[c][kh + 1][kw + 1], wv, a[3]);
+          }
+      }
+      T best = (T)0;
+      int kb = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        T y = add_rn(a[j], bsm[o]);
+        if (relu) y = go_max(y, (T)0);
+        if (j == 0 || y > best) best = y, kb = j;
+      }
+      const int64_t out = (n * O + o) * P + pp;
+      pooled[out] = best;
+      idx[out] = (uint8_t)kb;
+    }
+  }
+}
+
+struct ConvPoolSmallArgs {
+  gt_ctx* ctx;
+  int dtype, relu;
+  const void *x, *w, *bias;
+  void* pooled;
+  uint8_t* idx;
+  const gt_geom *g, *pg;
+  int64_t O;
+};
+
+static size_t conv_pool_small_smem(const gt_geom& g, int64_t O, size_t es) {
+  return (size_t)(O * g.C * 9 + O + g.C * (g.H + 2 * g.pad) * (g.W + 2 * g.pad)) * es;
+}
+
+// Whether conv_pool_small_kernel takes this convolution and pooling.
+static bool conv_pool_small_fits(const gt_geom& g, const gt_geom& pg, int64_t O, int act, size_t es) {
+  return g.KH == 3 && g.KW == 3 && g.stride == 1 && g.C >= 1 && g.C <= 3 && g.pad <= 2 && pg.KH == 2 &&
+         pg.KW == 2 && pg.stride == 2 && g.OH % 2 == 0 && g.OW % 2 == 0 && (act == GT_ACT_NONE || act == GT_ACT_RELU) &&
+         g.N <= 65535 && O <= 4096 && conv_pool_small_smem(g, O, es) <= 96 * 1024 &&
+         (g.H + 2 * g.pad) * (g.W + 2 * g.pad) < (1 << 24) && O * pg.OH * pg.OW < INT32_MAX / 2;
+}
+
+template <typename T, int CM>
+static char* conv_pool_small_launch(const ConvPoolSmallArgs& a) {
+  const gt_geom &g = *a.g, &pg = *a.pg;
+  const size_t smem = conv_pool_small_smem(g, a.O, sizeof(T));
+  static bool configured[64] = {};
+  int dev = 0;
+  GT_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !configured[dev]) {
+    GT_CUDA(cudaFuncSetAttribute(conv_pool_small_kernel<T, CM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 96 * 1024));
+    configured[dev] = true;
+  }
+  const int64_t P = pg.OH * pg.OW;
+  const dim3 grid((unsigned)ceil_div(P, (int64_t)256), (unsigned)g.N);
+  conv_pool_small_kernel<T, CM><<<grid, 256, smem, a.ctx->stream>>>(
+      (const T*)a.x, (const T*)a.w, (const T*)a.bias, a.relu, (int)g.C, (int)g.H, (int)g.W, (int)g.pad, (int)a.O,
+      (int)pg.OH, (int)pg.OW, (T*)a.pooled, a.idx);
+  GT_LAUNCH_CHECK();
+  return nullptr;
+}
+
+static char* conv_pool_small_run(void* p) {
+  const ConvPoolSmallArgs& a = *(const ConvPoolSmallArgs*)p;
+  const int64_t C = a.g->C;
+  if (a.dtype == GT_FLOAT64)
+    return C == 1 ? conv_pool_small_launch<double, 1>(a) : conv_pool_small_launch<double, 3>(a);
+  return C == 1 ? conv_pool_small_launch<float, 1>(a) : conv_pool_small_launch<float, 3>(a);
+}
+
 // Whether gt_conv_bwd_weight_pool runs conv_wgrad_pool_kernel for these
 // geometries (otherwise it goes through the full-resolution gradient).
 static bool pool_wgrad_fits(const gt_geom& g, const gt_geom& pg, int64_t O, size_t es) {
@@ -868,6 +991,13 @@ char* gt_conv_fwd_pool(gt_ctx* ctx, int dtype, const void* x, const void* w, con
     return errorf("gt_conv_fwd_pool: the pooling geometry does not take the convolution's output");
   if (pg->stride < pg->KH || pg->stride < pg->KW) return errorf("gt_conv_fwd_pool: windows overlap");
   if (g->N * O * pg->OH * pg->OW == 0) return nullptr;
+  const size_t es0 = dtype == GT_FLOAT64 ? 8 : 4;
+  // a first convolution (3 x 3 over at most 3 channels): computed directly,
+  // timed like the GEMM it replaces (M = positions, N = O, K = C*9)
+  if (conv_pool_small_fits(*g, *pg, O, act, es0)) {
+    ConvPoolSmallArgs a{ctx, dtype, act == GT_ACT_RELU ? 1 : 0, x, w, bias, pooled, idx, g, pg, O};
+    return timed_gemm_like(ctx, g->N * g->OH * g->OW, O, g->C * 9, 7, conv_pool_small_run, &a);
+  }
   // 2 x 2 windows at stride 2 that tile the output: pooled in the epilogue
   if (dtype == GT_FLOAT32 && pg->KH == 2 && pg->KW == 2 && pg->stride == 2 && g->OH % 2 == 0 && g->OW % 2 == 0) {
     bool done = false;

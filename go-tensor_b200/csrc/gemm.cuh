@@ -152,7 +152,8 @@ char* conv_wgrad_gemm(gt_ctx* ctx, const float* x, const float* dy, float* dw, f
 
 // Runs run(arg) between the GEMM launch timer's events, recorded as an
 // M x N x K GEMM on `path`: kernels that compute a GEMM's result another way
-// (5: the fused pool-backward weight gradient, conv.cu).
+// (5: the fused pool-backward weight gradient, 7: the direct first-conv +
+// ReLU + pool forward, conv.cu).
 char* timed_gemm_like(gt_ctx* ctx, int64_t M, int64_t N, int64_t K, int path, char* (*run)(void*), void* arg);
 
 // Whether a float32 GEMM with this epilogue, if it runs on the tcgen05 path,
