@@ -123,7 +123,7 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;  // default limit, 2 s; a healthy
 // per image, channels, images) whose K index is image * L + position, or two
 // 2-D copies of an operand already split into tf32 planes (B_SPLIT2: hi rows
 // from 0, lo rows from Gather::b_lo_row), which the splitters leave alone.
-enum ASrc : int { A_TMA = 0, A_IM2COL_POS = 1, A_IM2COL_CK = 2 };
+enum ASrc : int { A_TMA = 0, A_IM2COL_POS = 1, A_IM2COL_CK = 2, A_IM2COL_POS_FULL = 3 };
 enum BSrc : int { B_TMA2 = 0, B_TMA3 = 1, B_SPLIT2 = 2 };
 
 // The im2col geometry of a gathered operand (stride 1): src (N, C, H, W) read
@@ -158,6 +158,12 @@ struct Gather {
   // (kh * 2 + kw) of 2 x 2 window w, so a window's four values sit in four
   // adjacent lanes. Set by the host for that kind; the kernel keys on EK.
   int pool2 = 0;
+  // A_IM2COL_POS_FULL (set with it): the halo holds whole unpadded image
+  // planes (box_w = W, box_h = H; box_c channels of box_n images from the
+  // image of the tile's first position), so a tile's 128 positions need not
+  // be whole rows; each row's plane offset and in-image taps are computed per
+  // tile, and the padding's zeros come from those masks.
+  int full = 0;
   int r16 = 1, w16 = 16;    // A_IM2COL_CK
   uint32_t halo_bytes = 0;  // box_w * box_h * box_c * box_n * 4
   int b_lo_row = 0;         // B_SPLIT2: first row of the lo plane
@@ -422,6 +428,42 @@ __device__ __forceinline__ void pos_rows(const Gather& g, int lane, int (&hb)[4]
   }
 }
 
+// pos_rows for A_IM2COL_POS_FULL: row r of the tile starting at position
+// a_row (window-major when POOL2: index 4 w + k = offset k of window w, windows
+// in pooled order, images contiguous). The halo holds box_n unpadded image
+// planes (H x W) of box_c channels from the image of the tile's first
+// position: hb[i] is the offset of the row's patch origin (oh - pad, ow - pad),
+// mk[i] the taps (kh, kw) that fall inside the image. A row past M gets no
+// taps: it only reaches rows of C that are never stored.
+template <bool POOL2>
+__device__ __forceinline__ void pos_rows_full(const Gather& g, int a_row, int64_t M, int lane, int (&hb)[4],
+                                              int (&mk)[4]) {
+  const int plane = g.box_w * g.box_h, n0 = a_row / g.L;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int p = a_row + lane + 32 * i;
+    hb[i] = 0, mk[i] = 0;
+    if (p >= M) continue;
+    const int n = p / g.L, rem = p - n * g.L;
+    int oh, ow;
+    if constexpr (POOL2) {
+      const int w = rem >> 2, k = rem & 3, pw = g.OW >> 1, ph = w / pw, pc = w - ph * pw;
+      oh = 2 * ph + (k >> 1), ow = 2 * pc + (k & 1);
+    } else {
+      oh = rem / g.OW, ow = rem - oh * g.OW;
+    }
+    const int ih = oh - g.pad, iw = ow - g.pad;
+    hb[i] = (n - n0) * g.box_c * plane + ih * g.box_w + iw;
+    uint32_t m = 0;
+    for (int kh = 0; kh < g.KH; kh++) {
+      if ((unsigned)(ih + kh) >= (unsigned)g.box_h) continue;
+      for (int kw = 0; kw < g.KW; kw++)
+        if ((unsigned)(iw + kw) < (unsigned)g.box_w) m |= 1u << (kh * g.KW + kw);
+    }
+    mk[i] = (int)m;
+  }
+}
+
 __device__ __forceinline__ void store_row4(uint8_t* hi, uint8_t* lo, uint32_t off, float a, float b, float c,
                                            float d) {
   if (lo)
@@ -432,8 +474,13 @@ __device__ __forceinline__ void store_row4(uint8_t* hi, uint8_t* lo, uint32_t of
 
 // lo NULL: raw values into the hi plane (split in place afterwards); else the
 // split planes directly.
+// FULL (A_IM2COL_POS_FULL): the halo holds unpadded image planes, hb[i] is
+// the plane offset of row i's patch origin (negative inside the padding) and
+// bit kh * KW + kw of mk[i] says whether that tap lies inside the image (the
+// others are the padding's zeros and are not read).
+template <bool FULL>
 __device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, uint8_t* lo, const float* halo, int rows,
-                                           int k0, int lane, const int (&hb)[4]) {
+                                           int k0, int lane, const int (&hb)[4], const int (&mk)[4]) {
   const int plane = g.box_w * g.box_h;
   const int c_lo = k0 / g.KHW;
   int c = 0;
@@ -446,8 +493,14 @@ __device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, uint8_t
     for (int kk = 0; kk < 4; kk++) {
       const bool kin = k0 + 4 * c4 + kk < g.CKK;
       const int koff = c * plane + kh * g.box_w + kw;
+      if constexpr (FULL) {
+        const int tap = kh * g.KW + kw;
 #pragma unroll
-      for (int i = 0; i < 4; i++) v[i][kk] = kin ? halo[hb[i] + koff] : 0.0f;
+        for (int i = 0; i < 4; i++) v[i][kk] = kin && ((mk[i] >> tap) & 1) ? halo[hb[i] + koff] : 0.0f;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i][kk] = kin ? halo[hb[i] + koff] : 0.0f;
+      }
       if (++kw == g.KW) {
         kw = 0;
         if (++kh == g.KH) kh = 0, ++c;
@@ -768,6 +821,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               const int n0 = a_row / ga.L, oh0 = (a_row - n0 * ga.L) / ga.OW;
               tma_load_4d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], -ga.rp, oh0 - ga.pad,
                           k0 / ga.KHW, n0);
+            } else if constexpr (AS == A_IM2COL_POS_FULL) {  // whole planes: the slice's channels, box_n images
+              tma_load_3d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], 0, k0 / ga.KHW,
+                          a_row / ga.L);
             } else if constexpr (AS == A_IM2COL_CK) {  // the halo of the slice's positions, this block's channels
               const int n = k0 / ga.L, l0 = k0 - n * ga.L, oh0 = l0 / ga.OW, ow0 = l0 - oh0 * ga.OW;
               tma_load_4d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], ow0 - ga.rp, oh0 - ga.pad,
@@ -866,6 +922,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         unit_of(u, tiles, sp, num_k, t, kb, ke);
         const int a_row = (t / n_tiles) * 2 * BM + (int)rank * BM;
         if constexpr (AS == A_IM2COL_CK) ck_rows(ga, a_row, lane, rows4, kind4);
+        if constexpr (AS == A_IM2COL_POS_FULL) pos_rows_full<EK == EK_NCHW_POOL>(ga, a_row, s.M, lane, rows4, kind4);
         for (int kt = kb; kt < ke; kt++, it++) {
           if (it % SPLITTERS != sw) continue;
           const int st = it % STAGES;
@@ -890,8 +947,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             // are: they only reach rows of C that are never stored.
             const float* halo = (const float*)(stage + (HSEP ? TL::HALO_OFFSET : A_BYTES));
             uint8_t* lo = HSEP ? stage + A_BYTES : nullptr;  // with its own halo region: split while gathering
-            if constexpr (AS == A_IM2COL_POS)
-              gather_pos(ga, stage, lo, halo, a_rows, kt * BK, lane, rows4);
+            if constexpr (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL)
+              gather_pos<AS == A_IM2COL_POS_FULL>(ga, stage, lo, halo, a_rows, kt * BK, lane, rows4, kind4);
             else
               gather_ck(ga, stage, lo, halo, a_rows, lane, rows4, kind4);
             if constexpr (!HSEP) {
@@ -1009,17 +1066,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const bool relu = epi.act == GT_ACT_RELU;
           const int64_t P4 = epi.nchw_L / 4;
           const int k = lane & 3, row0 = lane & ~3;
-          // lanes 4 w' .. 4 w' + 3 hold window 8 q + w' of the CTA's 32; its
-          // pooled output for channel c goes to pool_base + c * P4 (-1: past
-          // M). Recomputed per block to keep it out of the total's live range.
+          // lanes 4 w' .. 4 w' + 3 hold window 8 q + w' of the CTA's 32. M is
+          // window-major (row 4 w + k of an image's L rows = offset k of its
+          // pooled position w), so the window's first row p gives the pooled
+          // output: image p / L, position (p % L) / 4; channel c's goes to
+          // pool_base + c * P4 (-1: past M).
           int64_t pool_base = -1;
           {
-            const int w = (32 * q + lane) >> 2, per = ga.rows_pi >> 2, pw = ga.OW >> 1;
-            const int wn = w / per, rem = w - wn * per, pr = rem / pw, pc = rem - pr * pw;
-            const int64_t m_tl = (m0 - 32 * q) + (int64_t)wn * ga.rows_pi + (int64_t)(2 * pr) * ga.OW + 2 * pc;
-            if (m_tl < s.M) {
-              const int64_t img = m_tl / epi.nchw_L, pos = m_tl - img * epi.nchw_L, oh = pos / ga.OW;
-              pool_base = img * epi.nchw_M * P4 + (oh / 2) * pw + (pos - oh * ga.OW) / 2;
+            const int64_t p = (m0 - 32 * q) + 4 * ((32 * q + lane) >> 2);
+            if (p < s.M) {
+              const int64_t img = p / epi.nchw_L;
+              pool_base = img * epi.nchw_M * P4 + (p - img * epi.nchw_L) / 4;
             }
           }
 #pragma unroll 1
@@ -1124,6 +1181,17 @@ static char* make_map3(gt_ctx* ctx, CUtensorMap* map, const float* base, int64_t
 static char* make_halo_map(gt_ctx* ctx, CUtensorMap* map, const float* base, const gt_geom& g, const Gather& ga) {
   auto encode = (EncodeTiledFn)ctx->encode_tiled;
   if (!encode) return errorf("gemm_tc: cuTensorMapEncodeTiled is unavailable");
+  if (ga.full) {  // whole planes: dims {H * W, C, N}
+    cuuint64_t dims3[3] = {(cuuint64_t)(g.H * g.W), (cuuint64_t)g.C, (cuuint64_t)g.N};
+    cuuint64_t strides3[2] = {(cuuint64_t)(g.H * g.W) * 4, (cuuint64_t)(g.C * g.H * g.W) * 4};
+    cuuint32_t box3[3] = {(cuuint32_t)(g.H * g.W), (cuuint32_t)ga.box_c, (cuuint32_t)ga.box_n};
+    cuuint32_t estr3[3] = {1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims3, strides3, box3, estr3,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return errorf("gemm_tc: cuTensorMapEncodeTiled (planes) failed (%d)", (int)r);
+    return nullptr;
+  }
   cuuint64_t dims[4] = {(cuuint64_t)g.W, (cuuint64_t)g.H, (cuuint64_t)g.C, (cuuint64_t)g.N};
   cuuint64_t strides[3] = {(cuuint64_t)g.W * 4, (cuuint64_t)(g.H * g.W) * 4, (cuuint64_t)(g.C * g.H * g.W) * 4};
   cuuint32_t box[4] = {(cuuint32_t)ga.box_w, (cuuint32_t)ga.box_h, (cuuint32_t)ga.box_c, (cuuint32_t)ga.box_n};
@@ -1239,11 +1307,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, SplitPlan sp,
 // offset, as the kernel's own pooled epilogue does for whole tiles.
 template <int TBN>
 __global__ void splitk_reduce_pool_kernel(const float* __restrict__ ws, SplitPlan sp, int tiles, int n_tiles,
-                                          int64_t M, int64_t N, Epi<float> epi, int rows_pi, int OW) {
+                                          int64_t M, int64_t N, Epi<float> epi) {
   constexpr int64_t TE = Tile<TBN>::TILE_ELEMS;
   const int rest = tiles - sp.whole;
   const int64_t total = (int64_t)rest * TE, work = (int64_t)rest * 2 * (BM / 4) * TBN;
-  const int per = rows_pi >> 2, pw = OW >> 1;
   const int64_t L = epi.nchw_L, P4 = L / 4;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < work; i += (int64_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / (2 * (BM / 4) * TBN));
@@ -1253,9 +1320,7 @@ __global__ void splitk_reduce_pool_kernel(const float* __restrict__ ws, SplitPla
     const int64_t n = (int64_t)(t % n_tiles) * TBN + cl;
     if (n >= N) continue;
     const int rank = wg / (BM / 4), w = wg - rank * (BM / 4);
-    const int nl = w / per, rem = w - nl * per, pr = rem / pw, pc = rem - pr * pw;
-    const int64_t m_tl =
-        (int64_t)(t / n_tiles) * 2 * BM + rank * BM + (int64_t)nl * rows_pi + (int64_t)(2 * pr) * OW + 2 * pc;
+    const int64_t m_tl = (int64_t)(t / n_tiles) * 2 * BM + rank * BM + 4 * w;  // the window's first row (window-major)
     if (m_tl >= M) continue;
     float v[4];
 #pragma unroll
@@ -1270,8 +1335,8 @@ __global__ void splitk_reduce_pool_kernel(const float* __restrict__ ws, SplitPla
     if (v[1] > best) best = v[1], kb = 1;
     if (v[2] > best) best = v[2], kb = 2;
     if (v[3] > best) best = v[3], kb = 3;
-    const int64_t img = m_tl / L, pos = m_tl - img * L, oh = pos / OW;
-    const int64_t o = (img * epi.nchw_M + n) * P4 + (oh / 2) * pw + (pos - oh * OW) / 2;
+    const int64_t img = m_tl / L;
+    const int64_t o = (img * epi.nchw_M + n) * P4 + (m_tl - img * L) / 4;
     epi.out[o] = best;
     epi.pool_idx[o] = (uint8_t)kb;
   }
@@ -1426,7 +1491,7 @@ static char* run_planned(gt_ctx* ctx, const GemmShape& s, const Epi<float>& epi,
   if (!err) {
     if (epi.pool_idx)  // pooled implicit convolution (ga set by its launcher)
       splitk_reduce_pool_kernel<TBN><<<grid_for(ctx, rest * TE / 4, 256), 256, 0, ctx->stream>>>(
-          sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi, ga->rows_pi, ga->OW);
+          sp.ws, sp, (int)tiles, (int)n_tiles, s.M, s.N, epi);
     else if (epi.bits_out)
       splitk_reduce_bits_kernel<<<(unsigned)std::min<int64_t>(rest * TE / 1024, (int64_t)ctx->sm_count * 8), 256, 0,
                                   ctx->stream>>>(
@@ -1450,7 +1515,8 @@ static char* conv_fwd_launch(gt_ctx* ctx, const GemmShape& s, const CUtensorMap&
                              const Epi<float>& e, const Gather& ga) {
   const int64_t n_tiles = ceil_div(s.N, TBN), tiles = ceil_div(s.M, 2 * BM) * n_tiles;
   return run_planned<TBN>(ctx, s, e, tiles, n_tiles, [&](const SplitPlan& sp) {
-    return launch_kernel<false, false, EK_NCHW_POS, TBN, A_IM2COL_POS, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga);
+    return ga.full ? launch_kernel<false, false, EK_NCHW_POS, TBN, A_IM2COL_POS_FULL, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga)
+                   : launch_kernel<false, false, EK_NCHW_POS, TBN, A_IM2COL_POS, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga);
   });
 }
 
@@ -1464,7 +1530,9 @@ static char* conv_fwd_pool_launch(gt_ctx* ctx, const GemmShape& s, const CUtenso
   return run_planned<TBN>(
       ctx, s, e, tiles, n_tiles,
       [&](const SplitPlan& sp) {
-        return launch_kernel<false, false, EK_NCHW_POOL, TBN, A_IM2COL_POS, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga);
+        return ga.full
+                   ? launch_kernel<false, false, EK_NCHW_POOL, TBN, A_IM2COL_POS_FULL, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga)
+                   : launch_kernel<false, false, EK_NCHW_POOL, TBN, A_IM2COL_POS, B_SPLIT2>(ctx, s, ta, tb, e, sp, ga);
       },
       &ga);
 }
@@ -1503,8 +1571,10 @@ static bool halo_fits(Gather& ga) {
   return true;
 }
 
-// A_IM2COL_POS: a CTA's 128 positions must form whole output rows of one
-// image (L % 128 == 0 and 128 % OW == 0) or whole images (128 % L == 0).
+// A_IM2COL_POS: a CTA's 128 positions are whole output rows of one image
+// (L % 128 == 0 and 128 % OW == 0) or whole images (128 % L == 0), and the
+// halo box covers just them; otherwise (Gather::full) the box holds the whole
+// padded images that any 128 consecutive positions touch, if that fits.
 static bool halo_pos(const gt_geom& g, Gather& ga) {
   if (!halo_common(g, ga)) return false;
   const int64_t L = g.OH * g.OW;
@@ -1537,6 +1607,22 @@ static bool halo_ck(const gt_geom& g, Gather& ga) {
   ga.box_h = ga.r16 + ga.KH - 1;
   ga.box_c = channels_spanned(BM, ga.KHW, ga.C);
   ga.box_n = 1;
+  return halo_fits(ga);
+}
+
+// A_IM2COL_POS_FULL: whole image planes of H x W <= 256 elements (a
+// multiple of 4, so that each plane starts 16-byte aligned), loaded by a 3-D
+// map over (H * W, C, N) for any 128 consecutive positions, if they fit.
+static bool halo_pos_full(const gt_geom& g, Gather& ga) {
+  const int64_t plane = g.H * g.W, L = g.OH * g.OW;
+  if (g.stride != 1 || plane > 256 || plane % 4 || g.KH * g.KW > 32 || g.pad > 64 || L < 1) return false;
+  ga.C = (int)g.C, ga.H = (int)g.H, ga.W = (int)g.W, ga.KH = (int)g.KH, ga.KW = (int)g.KW, ga.OW = (int)g.OW;
+  ga.pad = (int)g.pad, ga.L = (int)L, ga.KHW = (int)(g.KH * g.KW), ga.CKK = (int)(g.C * g.KH * g.KW);
+  ga.rp = 0, ga.full = 1;
+  ga.bh = (int)g.OH, ga.rows_pi = (int)L;
+  ga.box_w = (int)g.W, ga.box_h = (int)g.H;
+  ga.box_c = channels_spanned(BK, ga.KHW, ga.C);
+  ga.box_n = (int)(1 + (127 + L - 1) / L);
   return halo_fits(ga);
 }
 
@@ -1599,11 +1685,15 @@ char* conv_fwd_tc(gt_ctx* ctx, const float* x, const float* ws, int64_t w_pitch,
   // C (P, O) = cols (P, CKK) @ w (O, CKK)^T: A gathered, B(k, n) = w[n * w_pitch + k].
   GemmShape s{P, O, CKK, false, true, 0, w_pitch};
   tc::Gather ga;
-  if (!tc::halo_pos(g, ga) || ((uintptr_t)x & 15)) return nullptr;
+  if ((uintptr_t)x & 15) return nullptr;
+  if (!tc::halo_pos(g, ga)) {
+    ga = tc::Gather();
+    if (!tc::halo_pos_full(g, ga)) return nullptr;
+  }
   if (pool_idx) {
     // windows must not straddle CTAs: a CTA's 128 positions are whole row
     // pairs of one image (an even number of rows) or whole images
-    if (g.OH % 2 || g.OW % 2 || (ga.box_n == 1 && ga.bh % 2)) return nullptr;
+    if (g.OH % 2 || g.OW % 2 || (!ga.full && ga.box_n == 1 && ga.bh % 2)) return nullptr;
     ga.pool2 = 1;
   }
   ga.b_lo_row = (int)conv_weight_rows(O);

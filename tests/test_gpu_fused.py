@@ -608,16 +608,61 @@ def test_conv_bwd_weight_pool_non_finite_input(dt, npdt, tol):
     assert_close(db, db2, tol, "db")
 
 
+@pytest.mark.parametrize("cs", [(4, 32, 14, 14, 64, 3, 1, 1), (3, 16, 10, 10, 32, 3, 1, 1), (2, 64, 14, 14, 32, 3, 1, 1)])
+def test_conv_implicit_whole_image_halo_against_float64(cs):
+    """Images whose positions do not split into whole-row 128-position tiles
+    (14 x 14, 10 x 10): the implicit forward and input gradient take halo
+    boxes of whole image planes (two or three images per tile) with the
+    padding masked in the gather, checked against float64 results. The bound
+    is that of a float32 dot product: 8x the oracle's own float32 error or
+    2^-19 of the sum of absolute products (3xTF32 drops lo * lo and the tensor
+    core's accumulation truncates; a wrong or missing tap would be ~1e-3)."""
+    N, C, H, W, O, k, s, p = cs
+    rng = np.random.default_rng(sum(cs) + 7)
+    x = rng.standard_normal((N, C, H, W)).astype(np.float32)
+    w = rng.standard_normal((O, C, k, k)).astype(np.float32)
+    b = rng.standard_normal(O).astype(np.float32)
+    g = T.conv_geom("Conv2d", [N, C, H, W], k, k, s, p)
+    gg = ctypes.byref(_lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_]))
+    dy = rng.standard_normal((N, O, g.OH, g.OW)).astype(np.float32)
+    y, dx = new(N * O * g.OH * g.OW, T.Float32), new(N * C * H * W, T.Float32)
+    check(lib().gt_conv_fwd(ctx(), 0, dev(x).ptr, dev(w).ptr, dev(b).ptr, y.ptr, gg, O, 0))
+    assert lib().gt_gemm_path_taken() == 4
+    check(lib().gt_conv_bwd_data(ctx(), 0, dev(dy).ptr, dev(w).ptr, dx.ptr, gg, O))
+    assert lib().gt_gemm_path_taken() == 4
+
+    def run(dt, absolute=False):
+        def t(a, *shape):
+            a = np.abs(a) if absolute else a
+            return T.FromFloat64(a.astype(np.float64).reshape(-1), *shape).ToDType(dt).SetRequiresGrad(True)
+        xs, ws, bs = t(x, N, C, H, W), t(w, O, C, k, k), t(b, O)
+        out = T.Conv2d(xs, ws, bs, s, p)
+        out.Backward(t(dy, N, O, g.OH, g.OW))
+        return [out.Float64s(), xs.Grad().Float64s()]
+
+    T.SetDefaultDType(T.Float64)
+    try:
+        exact, scale = run(T.Float64), run(T.Float64, absolute=True)
+    finally:
+        T.SetDefaultDType(T.Float32)
+    oracle32 = run(T.Float32)
+    for name, got, ex, sc, o32 in zip(("y", "dx"), (host(y), host(dx)), exact, scale, oracle32):
+        err = np.abs(got.astype(np.float64) - ex) / np.maximum(sc, 1e-30)
+        err32 = np.abs(o32 - ex) / np.maximum(sc, 1e-30)
+        assert err.max() <= max(8 * err32.max(), 2.0 ** -19), (name, cs, float(err.max()), float(err32.max()))
+
+
 # (N, C, H, W, O, kernel, pad, pool window): the conv stack's four layers
 # (whole-row and whole-image position tiles, an odd image count that leaves
 # half of the last tile empty), a 64-wide image, and geometries that take the
 # unfused path (a 128-wide image, 3 x 3 windows); the first conv of each
 # benchmark config, a two-channel one without padding and a 5 x 5 window take
-# the direct kernel or not by their patch size.
+# the direct kernel or not by their patch size; the CNN's second conv (14 x 14)
+# and a 10 x 10 one pool in the epilogue of tiles whose halo holds whole images.
 CONV_POOLS = [(2, 3, 32, 32, 64, 3, 1, 2), (3, 64, 16, 16, 128, 3, 1, 2), (3, 128, 8, 8, 256, 3, 1, 2),
               (5, 256, 4, 4, 512, 3, 1, 2), (1, 8, 64, 64, 32, 3, 1, 2), (1, 4, 128, 128, 16, 3, 1, 2),
               (2, 1, 28, 28, 32, 3, 1, 2), (2, 3, 12, 12, 16, 3, 1, 3), (2, 2, 10, 10, 8, 3, 0, 2),
-              (2, 3, 12, 12, 8, 5, 2, 2)]
+              (2, 3, 12, 12, 8, 5, 2, 2), (4, 32, 14, 14, 64, 3, 1, 2), (3, 16, 10, 10, 32, 3, 1, 2)]
 
 
 def _direct(cs):
