@@ -156,7 +156,10 @@ def clocks_sampler(index: int):
 
 def clocks_summary(proc, path, windows):
     """Median SM clock, max clock and active throttle reasons over the samples
-    taken inside `windows` (host-time intervals of the timed regions)."""
+    taken inside `windows` (host-time intervals of the timed regions). A
+    timed region shorter than the 50 ms sampling period (the small configs)
+    may hold no sample: then the samples within 100 ms of a region are used,
+    and the line says so (`window_margin_ms`)."""
     import datetime as _dt
     if proc is None:
         return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -165,8 +168,8 @@ def clocks_summary(proc, path, windows):
         proc.wait(timeout=5)
     except subprocess.TimeoutExpired:
         proc.kill()
-    sm, smax, power, reasons = [], [], [], set()
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    rows = []
     with open(path) as f:
         for line in f:
             c = [x.strip() for x in line.split(",")]
@@ -177,22 +180,28 @@ def clocks_summary(proc, path, windows):
                 mhz, mx = float(c[2]), float(c[3])
             except ValueError:
                 continue
-            if not any(lo <= t <= hi for lo, hi in windows):
-                continue
-            sm.append(mhz)
-            smax.append(mx)
             try:
-                power.append(float(c[4]))
+                pw = float(c[4])
             except ValueError:
-                pass
-            for n, v in zip(names, c[6:10]):
-                if v.lower() == "active":
-                    reasons.add(n)
+                pw = None
+            rows.append((t, mhz, mx, pw, {n for n, v in zip(names, c[6:10]) if v.lower() == "active"}))
     os.unlink(path)
-    if not sm:
-        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples inside the timed regions"]}
-    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-            "samples": len(sm), "sm_mhz_min": min(sm), "power_w_max": max(power) if power else None}
+    out = {}
+    for margin in (0.0, 0.1):
+        picked = [r for r in rows if any(lo - margin <= r[0] <= hi + margin for lo, hi in windows)]
+        if picked:
+            if margin:
+                out["window_margin_ms"] = 1000 * margin
+            break
+    else:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples near the timed regions"]}
+    sm = [r[1] for r in picked]
+    power = [r[3] for r in picked if r[3] is not None]
+    reasons = set().union(*(r[4] for r in picked))
+    out.update({"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[2] for r in picked),
+                "reasons": sorted(reasons), "samples": len(sm), "sm_mhz_min": min(sm),
+                "power_w_max": max(power) if power else None})
+    return out
 
 
 # ---------------------------------------------------------------------------
