@@ -57,6 +57,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <type_traits>
 
 #include "gemm.cuh"
 
@@ -69,7 +70,7 @@ namespace tc {
 constexpr int BM = 128;    // A rows per CTA (a pair covers 256)
 constexpr int BK = 16;     // K elements per slice
 constexpr int STAGES = 6;
-constexpr int MAX_STAGES = 6;
+constexpr int MAX_STAGES = 12;  // the deepest ring (a gathered A in tensor memory, 64-wide tiles)
 // One splitter warp per ring slot: splitter w takes slices w, w + 6, ...,
 // all of which land in slot w, so its waits on that slot's barrier come in
 // phase order. (A barrier's parity wait cannot tell a phase from the one two
@@ -96,6 +97,11 @@ struct Tile {
   // operand's halo, so the gather writes both split planes in one pass.
   static constexpr uint32_t HALO_OFFSET = 2 * (A_BYTES + B_BYTES);
   static constexpr uint32_t STAGE_BYTES = HALO_OFFSET + (HALO ? A_BYTES : 0u);
+  static constexpr uint32_t B_OFF = 2 * A_BYTES;                        // B hi (B lo follows)
+  static constexpr uint32_t HALO_OFF = HALO ? HALO_OFFSET : A_BYTES;  // a gathered operand's halo
+  static constexpr uint32_t A_COL0 = 0;                               // unused: A is in shared memory
+  static constexpr bool NCAT = false;
+  static constexpr int ACC = BN;
   static constexpr int STAGES = tc::STAGES;
   static constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
   static constexpr uint32_t EPI_OFFSET = BAR_OFFSET + 512;
@@ -105,6 +111,43 @@ struct Tile {
   static constexpr int64_t TILE_ELEMS = 2 * BM * BN;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(STAGES <= MAX_STAGES && STAGES == SPLITTERS, "one splitter warp per slot");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+// Layout of an instantiation whose gathered A operand goes to tensor memory
+// (tile widths 64 and 128): the two partial accumulators take columns
+// 0 .. 2 ACC - 1, and ring slot s keeps its slice's A hi and A lo (16 columns
+// each, lane = row, column = k, the layout the MMA reads A from tensor memory
+// in) at columns A_COL0 + 32 s. Shared memory holds per slot only B's two
+// planes and the halo, so the ring is as deep as the columns allow.
+// NCAT (width 64): each CTA's B hi and B lo rows are adjacent, so one MMA of
+// width 2 BN multiplies an A plane by both: two MMAs per K step (A hi and
+// A lo against [B hi | B lo]) instead of three, whose issue bounds the narrow
+// tile. An accumulator then holds each output column twice, the products
+// with B hi and with B lo, which the promoters add.
+template <int BN>
+struct TileT {
+  static_assert(BN == 64 || BN == 128, "tile width");
+  static constexpr int BNH = BN / 2;
+  static constexpr bool NCAT = BN == 64;
+  static constexpr int ACC = NCAT ? 2 * BN : BN;  // accumulator columns per partial buffer
+  static constexpr uint32_t B_BYTES = BNH * BK * 4;
+  static constexpr uint32_t B_OFF = 0;
+  static constexpr uint32_t HALO_OFF = 2 * B_BYTES;
+  static constexpr uint32_t STAGE_BYTES = HALO_OFF + A_BYTES;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t A_COL0 = 2 * ACC;
+  static constexpr int STAGES = (int)((TMEM_COLS - A_COL0) / 32) < MAX_STAGES ? (int)((TMEM_COLS - A_COL0) / 32)
+                                                                              : MAX_STAGES;
+  static constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr uint32_t EPI_OFFSET = BAR_OFFSET + 512;
+  static constexpr uint32_t TAB_OFFSET = EPI_OFFSET + EPI_BYTES;  // the gather's tap table (KH * KW <= 64)
+  static constexpr uint32_t SMEM_BYTES = TAB_OFFSET + 64 * 16 * 4 + 1024;
+  static constexpr int HC = BN / 2;
+  static constexpr int64_t TILE_ELEMS = 2 * BM * BN;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(TAB_OFFSET % 16 == 0, "the table is read as int4");
+  static_assert(A_COL0 + 32u * STAGES <= TMEM_COLS, "A slots fit the allocation");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 constexpr int BN = 256;  // the plain GEMMs' tile width
@@ -315,17 +358,30 @@ __device__ __forceinline__ uint32_t instr_desc() {
   return d;
 }
 
+// (The form without a disable-output-lane mask: every lane is written.)
 __device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                               uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
-          tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0),
-      "r"(0)
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+
+// The same MMA with A read from tensor memory at column `tmem_a` (in each CTA
+// of the pair, its 128 rows on the 128 lanes; A K-major).
+__device__ __forceinline__ void mma_tf32_pair_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Arrives on `bar` in both CTAs of the pair once the MMAs issued so far complete.
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
@@ -408,59 +464,117 @@ __device__ __forceinline__ void split_store4(uint8_t* hi, uint8_t* lo, uint32_t 
 // C*KH*KW are zero; taps in the padding read the halo's zero fill
 // (internal/cpu/linalg.go:130-139).
 template <bool POOL2>
-__device__ __forceinline__ void pos_rows(const Gather& g, int lane, int (&hb)[4]) {
+__device__ __forceinline__ int pos_row(const Gather& g, int r) {
   const int plane = g.box_w * g.box_h;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int r = lane + 32 * i;
-    int n, oh, ow;
-    if constexpr (POOL2) {
-      const int w = r >> 2, k = r & 3, per = g.rows_pi >> 2, pw = g.OW >> 1;
-      n = w / per;
-      const int rem = w - n * per, pr = rem / pw, pc = rem - pr * pw;
-      oh = 2 * pr + (k >> 1), ow = 2 * pc + (k & 1);
-    } else {
-      n = r / g.rows_pi;
-      const int rem = r - n * g.rows_pi;
-      oh = rem / g.OW, ow = rem - oh * g.OW;
-    }
-    hb[i] = n * g.box_c * plane + oh * g.box_w + ow + g.rp - g.pad;
+  int n, oh, ow;
+  if constexpr (POOL2) {
+    const int w = r >> 2, k = r & 3, per = g.rows_pi >> 2, pw = g.OW >> 1;
+    n = w / per;
+    const int rem = w - n * per, pr = rem / pw, pc = rem - pr * pw;
+    oh = 2 * pr + (k >> 1), ow = 2 * pc + (k & 1);
+  } else {
+    n = r / g.rows_pi;
+    const int rem = r - n * g.rows_pi;
+    oh = rem / g.OW, ow = rem - oh * g.OW;
   }
+  return n * g.box_c * plane + oh * g.box_w + ow + g.rp - g.pad;
+}
+
+template <bool POOL2>
+__device__ __forceinline__ void pos_rows(const Gather& g, int lane, int (&hb)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; i++) hb[i] = pos_row<POOL2>(g, lane + 32 * i);
 }
 
 // pos_rows for A_IM2COL_POS_FULL: row r of the tile starting at position
 // a_row (window-major when POOL2: index 4 w + k = offset k of window w, windows
 // in pooled order, images contiguous). The halo holds box_n unpadded image
 // planes (H x W) of box_c channels from the image of the tile's first
-// position: hb[i] is the offset of the row's patch origin (oh - pad, ow - pad),
-// mk[i] the taps (kh, kw) that fall inside the image. A row past M gets no
+// position: hb is the offset of the row's patch origin (oh - pad, ow - pad),
+// mk the taps (kh, kw) that fall inside the image. A row past M gets no
 // taps: it only reaches rows of C that are never stored.
+template <bool POOL2>
+__device__ __forceinline__ void pos_row_full(const Gather& g, int a_row, int64_t M, int r, int& hb, int& mk) {
+  const int plane = g.box_w * g.box_h, n0 = a_row / g.L;
+  const int p = a_row + r;
+  hb = 0, mk = 0;
+  if (p >= M) return;
+  const int n = p / g.L, rem = p - n * g.L;
+  int oh, ow;
+  if constexpr (POOL2) {
+    const int w = rem >> 2, k = rem & 3, pw = g.OW >> 1, ph = w / pw, pc = w - ph * pw;
+    oh = 2 * ph + (k >> 1), ow = 2 * pc + (k & 1);
+  } else {
+    oh = rem / g.OW, ow = rem - oh * g.OW;
+  }
+  const int ih = oh - g.pad, iw = ow - g.pad;
+  hb = (n - n0) * g.box_c * plane + ih * g.box_w + iw;
+  uint32_t m = 0;
+  for (int kh = 0; kh < g.KH; kh++) {
+    if ((unsigned)(ih + kh) >= (unsigned)g.box_h) continue;
+    for (int kw = 0; kw < g.KW; kw++)
+      if ((unsigned)(iw + kw) < (unsigned)g.box_w) m |= 1u << (kh * g.KW + kw);
+  }
+  mk = (int)m;
+}
+
 template <bool POOL2>
 __device__ __forceinline__ void pos_rows_full(const Gather& g, int a_row, int64_t M, int lane, int (&hb)[4],
                                               int (&mk)[4]) {
-  const int plane = g.box_w * g.box_h, n0 = a_row / g.L;
+#pragma unroll
+  for (int i = 0; i < 4; i++) pos_row_full<POOL2>(g, a_row, M, lane + 32 * i, hb[i], mk[i]);
+}
+
+// The tap table of a gathered operand in tensor memory. A slice's 16 patch
+// entries start at entry k0; with m = k0 % KHW, entry j is (channel
+// k0 / KHW + dc, tap) for t = m + j, dc = t / KHW, tap = t % KHW, and
+// tab[16 m + j] packs tap << 16 | (dc * plane + kh * box_w + kw), its offset
+// in the slice's halo (below 2^16: a halo holds at most 2048 values). Built
+// once per kernel, so the gather itself needs no index arithmetic.
+__device__ __forceinline__ void build_tap_table(const Gather& g, int* tab, int tid, int nthreads) {
+  const int plane = g.box_w * g.box_h;
+  for (int i = tid; i < g.KHW * 16; i += nthreads) {
+    const int m = i >> 4, t = m + (i & 15), dc = t / g.KHW, tap = t - dc * g.KHW;
+    const int kh = tap / g.KW, kw = tap - kh * g.KW;
+    tab[i] = (tap << 16) | (dc * plane + kh * g.box_w + kw);
+  }
+}
+
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+  float x;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(addr) : "memory");
+  return x;
+}
+
+__device__ __forceinline__ int4 ld_shared_v4(uint32_t addr) {
+  int4 v;
+  asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// A gathered operand in tensor memory: the lane's own row (hb, mk as above;
+// live false for a row past M, which gets zeros) over the slice's 16 patch
+// entries from k0, whose table entries start at shared address `tab16`,
+// split into v[0..15] = hi and v[16..31] = lo, the order of the slot's 32
+// columns. The warp's halo reads are 32 consecutive positions.
+template <bool FULL>
+__device__ __forceinline__ void gather_row_split(const Gather& g, uint32_t halo, uint32_t tab16, bool live, int k0,
+                                                 int hb, int mk, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    const int p = a_row + lane + 32 * i;
-    hb[i] = 0, mk[i] = 0;
-    if (p >= M) continue;
-    const int n = p / g.L, rem = p - n * g.L;
-    int oh, ow;
-    if constexpr (POOL2) {
-      const int w = rem >> 2, k = rem & 3, pw = g.OW >> 1, ph = w / pw, pc = w - ph * pw;
-      oh = 2 * ph + (k >> 1), ow = 2 * pc + (k & 1);
-    } else {
-      oh = rem / g.OW, ow = rem - oh * g.OW;
+    const int4 q = ld_shared_v4(tab16 + 16 * i);
+    const int e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int kk = 4 * i + j;
+      bool take = live && k0 + kk < g.CKK;
+      if constexpr (FULL) take = take && ((mk >> (e[j] >> 16)) & 1);
+      const float x = take ? ld_shared_f32(halo + 4u * (uint32_t)(hb + (e[j] & 0xFFFF))) : 0.0f;
+      const float h = tf32_round(x);
+      v[kk] = h;
+      v[16 + kk] = tf32_round(__fsub_rn(x, h));
     }
-    const int ih = oh - g.pad, iw = ow - g.pad;
-    hb[i] = (n - n0) * g.box_c * plane + ih * g.box_w + iw;
-    uint32_t m = 0;
-    for (int kh = 0; kh < g.KH; kh++) {
-      if ((unsigned)(ih + kh) >= (unsigned)g.box_h) continue;
-      for (int kw = 0; kw < g.KW; kw++)
-        if ((unsigned)(iw + kw) < (unsigned)g.box_w) m |= 1u << (kh * g.KW + kw);
-    }
-    mk[i] = (int)m;
   }
 }
 
@@ -481,29 +595,32 @@ __device__ __forceinline__ void store_row4(uint8_t* hi, uint8_t* lo, uint32_t of
 template <bool FULL>
 __device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, uint8_t* lo, const float* halo, int rows,
                                            int k0, int lane, const int (&hb)[4], const int (&mk)[4]) {
-  const int plane = g.box_w * g.box_h;
-  const int c_lo = k0 / g.KHW;
-  int c = 0;
-  const int rem = k0 - c_lo * g.KHW;
-  int kh = rem / g.KW, kw = rem - kh * g.KW;
+  // Lane j < 16 packs entry k0 + j as the tap table does (tap << 16 | halo
+  // offset); the warp reads entry kk from lane kk, so the loads need no
+  // serial index arithmetic.
+  int my_e;
+  {
+    const int plane = g.box_w * g.box_h, m = k0 % g.KHW, t = m + (lane & 15), dc = t / g.KHW;
+    const int tap = t - dc * g.KHW, kh = tap / g.KW, kw = tap - kh * g.KW;
+    my_e = (tap << 16) | (dc * plane + kh * g.box_w + kw);
+  }
+  const uint32_t hs = smem_u32(halo);
 #pragma unroll 1
   for (int c4 = 0; c4 < 4; c4++) {
     float v[4][4];
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
+      const int e = __shfl_sync(0xffffffffu, my_e, 4 * c4 + kk);
       const bool kin = k0 + 4 * c4 + kk < g.CKK;
-      const int koff = c * plane + kh * g.box_w + kw;
+      const int koff = e & 0xFFFF;
       if constexpr (FULL) {
-        const int tap = kh * g.KW + kw;
+        const int tap = e >> 16;
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i][kk] = kin && ((mk[i] >> tap) & 1) ? halo[hb[i] + koff] : 0.0f;
+        for (int i = 0; i < 4; i++)
+          v[i][kk] = kin && ((mk[i] >> tap) & 1) ? ld_shared_f32(hs + 4u * (uint32_t)(hb[i] + koff)) : 0.0f;
       } else {
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i][kk] = kin ? halo[hb[i] + koff] : 0.0f;
-      }
-      if (++kw == g.KW) {
-        kw = 0;
-        if (++kh == g.KH) kh = 0, ++c;
+        for (int i = 0; i < 4; i++) v[i][kk] = kin ? ld_shared_f32(hs + 4u * (uint32_t)(hb[i] + koff)) : 0.0f;
       }
     }
 #pragma unroll
@@ -745,12 +862,36 @@ constexpr bool halo_region() {
   return AS != A_TMA && TBN <= 128;
 }
 
+// A position-gathered operand (A_IM2COL_POS, A_IM2COL_POS_FULL) of a tile up
+// to 128 wide goes to tensor memory: four gather warps (one per lane quarter)
+// write each slice's split rows with tcgen05.st, the MMA reads A from there
+// and B from shared memory. Shared memory then carries no A planes, whose
+// stores and the MMA's reads of them bound the narrow tiles.
+template <int TBN, int AS>
+constexpr bool a_in_tmem() {
+  return (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL) && TBN <= 128;
+}
+
+template <int TBN, int AS>
+using LayoutOf = std::conditional_t<a_in_tmem<TBN, AS>(), TileT<(TBN > 128 ? 128 : TBN)>,
+                                    Tile<TBN, halo_region<TBN, AS>()>>;
+constexpr int GATHER_WARP0 = 4;  // warps 4..7 (lane quarters 0..3) gather into tensor memory
+
 template <bool A_MN, bool B_MN, int EK, int TBN, int AS, int BS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             GemmShape s, Epi<float> epi, SplitPlan sp, Gather ga) {
   constexpr bool HSEP = halo_region<TBN, AS>();
-  using TL = Tile<TBN, HSEP>;
+  constexpr bool ATM = a_in_tmem<TBN, AS>();
+  using TL = LayoutOf<TBN, AS>;
+  constexpr bool NCAT = TL::NCAT;
+  constexpr int ACC = TL::ACC;
+  // Slices per barrier round: with A in tensor memory two ring slots fill,
+  // gather and free together (one wait and one commit per two slices: the
+  // single MMA thread's fixed costs per round bound the narrow tiles).
+  constexpr int SS = ATM ? 2 : 1;
+  constexpr int NBAR = TL::STAGES / SS;
+  static_assert(TL::STAGES % SS == 0 && GROUP % SS == 0, "whole rounds; groups start a round");
   constexpr int HC = TL::HC;
   constexpr int STAGES = TL::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -771,7 +912,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; i++) {
       mbar_init(&sh->full[i], 1);
-      mbar_init(&sh->split[i], 2 * 32);  // one splitter warp per CTA per slice
+      mbar_init(&sh->split[i], ATM ? 2 * 4 : 2 * 32);  // per CTA: a splitter warp's lanes, or lane 0 of 4 gather warps
       mbar_init(&sh->empty[i], 1);
     }
     for (int b = 0; b < 2; b++) {
@@ -799,106 +940,126 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_LOW));
     if (warp == 0) {
       if (lane == 0) {  // ---- TMA producer (both CTAs)
-        int it = 0, issued_to = 0;
+        int it = 0, issued_to = 0;  // barrier rounds (SS slices each)
         for (int u = pair; u < units && !*failed; u += pairs) {
           int t, kb, ke;
           unit_of(u, tiles, sp, num_k, t, kb, ke);
           const int mt = t / n_tiles, nt = t % n_tiles;
           const int a_row = mt * 2 * BM + (int)rank * BM;
           const int b_row = nt * TBN + (int)rank * TL::BNH;
-          for (int kt = kb; kt < ke; kt++, it++) {
-            const int st = it % STAGES;
-            if (!mbar_wait(&sh->empty[st], ((it / STAGES) & 1) ^ 1, 1, sp.wait_limit_ns)) {
+          for (int kt = kb; kt < ke; kt += SS, it++) {
+            const int nb = it % NBAR, n_in = ke - kt < SS ? ke - kt : SS;
+            if (!mbar_wait(&sh->empty[nb], ((it / NBAR) & 1) ^ 1, 1, sp.wait_limit_ns)) {
               *failed = 1;
               break;
             }
-            uint8_t* a_hi = smem + st * TL::STAGE_BYTES;
-            uint8_t* b_hi = a_hi + 2 * A_BYTES;
-            mbar_expect_tx(&sh->full[st],
-                           (AS == A_TMA ? A_BYTES : ga.halo_bytes) + (BS == B_SPLIT2 ? 2u : 1u) * TL::B_BYTES);
-            const int k0 = kt * BK;
-            if constexpr (AS == A_IM2COL_POS) {  // the halo of this block's positions, the slice's channels
-              const int n0 = a_row / ga.L, oh0 = (a_row - n0 * ga.L) / ga.OW;
-              tma_load_4d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], -ga.rp, oh0 - ga.pad,
-                          k0 / ga.KHW, n0);
-            } else if constexpr (AS == A_IM2COL_POS_FULL) {  // whole planes: the slice's channels, box_n images
-              tma_load_3d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], 0, k0 / ga.KHW,
-                          a_row / ga.L);
-            } else if constexpr (AS == A_IM2COL_CK) {  // the halo of the slice's positions, this block's channels
-              const int n = k0 / ga.L, l0 = k0 - n * ga.L, oh0 = l0 / ga.OW, ow0 = l0 - oh0 * ga.OW;
-              tma_load_4d(a_hi + (HSEP ? TL::HALO_OFFSET : A_BYTES), &tmA, &sh->full[st], ow0 - ga.rp, oh0 - ga.pad,
-                          a_row / ga.KHW, n);
-            }
-            if constexpr (AS == A_TMA) {
-              if (A_MN) {
-#pragma unroll
-                for (int j = 0; j < BM / 32; j++)
-                  tma_load_2d(a_hi + j * kLboMN, &tmA, &sh->full[st], a_row + 32 * j, k0);
-              } else {
-                tma_load_2d(a_hi, &tmA, &sh->full[st], k0, a_row);
+            uint64_t* bar = &sh->full[nb];
+            mbar_expect_tx(bar, (uint32_t)n_in * ((AS == A_TMA ? A_BYTES : ga.halo_bytes) +
+                                                  (BS == B_SPLIT2 ? 2u : 1u) * TL::B_BYTES));
+            for (int i = 0; i < n_in; i++) {
+              const int st = nb * SS + i;
+              uint8_t* a_hi = smem + st * TL::STAGE_BYTES;
+              uint8_t* b_hi = a_hi + TL::B_OFF;
+              const int k0 = (kt + i) * BK;
+              if constexpr (AS == A_IM2COL_POS) {  // the halo of this block's positions, the slice's channels
+                const int n0 = a_row / ga.L, oh0 = (a_row - n0 * ga.L) / ga.OW;
+                tma_load_4d(a_hi + TL::HALO_OFF, &tmA, bar, -ga.rp, oh0 - ga.pad, k0 / ga.KHW, n0);
+              } else if constexpr (AS == A_IM2COL_POS_FULL) {  // whole planes: the slice's channels, box_n images
+                tma_load_3d(a_hi + TL::HALO_OFF, &tmA, bar, 0, k0 / ga.KHW, a_row / ga.L);
+              } else if constexpr (AS == A_IM2COL_CK) {  // the halo of the slice's positions, this block's channels
+                const int n = k0 / ga.L, l0 = k0 - n * ga.L, oh0 = l0 / ga.OW, ow0 = l0 - oh0 * ga.OW;
+                tma_load_4d(a_hi + TL::HALO_OFF, &tmA, bar, ow0 - ga.rp, oh0 - ga.pad, a_row / ga.KHW, n);
               }
-            }
-            if constexpr (BS == B_TMA3) {  // K index = image * L + position
-              const int img = k0 / ga.L;
-              tma_load_3d(b_hi, &tmB, &sh->full[st], k0 - img * ga.L, b_row, img);
-            } else if constexpr (BS == B_SPLIT2) {  // both planes, already split
-              tma_load_2d(b_hi, &tmB, &sh->full[st], k0, b_row);
-              tma_load_2d(b_hi + TL::B_BYTES, &tmB, &sh->full[st], k0, ga.b_lo_row + b_row);
-            } else if (B_MN) {
+              if constexpr (AS == A_TMA) {
+                if (A_MN) {
 #pragma unroll
-              for (int j = 0; j < TL::BNH / 32; j++)
-                tma_load_2d(b_hi + j * kLboMN, &tmB, &sh->full[st], b_row + 32 * j, k0);
-            } else {
-              tma_load_2d(b_hi, &tmB, &sh->full[st], k0, b_row);
+                  for (int j = 0; j < BM / 32; j++) tma_load_2d(a_hi + j * kLboMN, &tmA, bar, a_row + 32 * j, k0);
+                } else {
+                  tma_load_2d(a_hi, &tmA, bar, k0, a_row);
+                }
+              }
+              if constexpr (BS == B_TMA3) {  // K index = image * L + position
+                const int img = k0 / ga.L;
+                tma_load_3d(b_hi, &tmB, bar, k0 - img * ga.L, b_row, img);
+              } else if constexpr (BS == B_SPLIT2) {  // both planes, already split
+                tma_load_2d(b_hi, &tmB, bar, k0, b_row);
+                tma_load_2d(b_hi + TL::B_BYTES, &tmB, bar, k0, ga.b_lo_row + b_row);
+              } else if (B_MN) {
+#pragma unroll
+                for (int j = 0; j < TL::BNH / 32; j++) tma_load_2d(b_hi + j * kLboMN, &tmB, bar, b_row + 32 * j, k0);
+              } else {
+                tma_load_2d(b_hi, &tmB, bar, k0, b_row);
+              }
             }
             issued_to = it + 1;
           }
         }
         if (*failed) {  // let copies in flight land before the CTA tears down
-          for (int i = issued_to > STAGES ? issued_to - STAGES : 0; i < issued_to; i++)
-            mbar_wait(&sh->full[i % STAGES], (i / STAGES) & 1, 5, kTimeoutNs);  // copies land in microseconds
+          for (int i = issued_to > NBAR ? issued_to - NBAR : 0; i < issued_to; i++)
+            mbar_wait(&sh->full[i % NBAR], (i / NBAR) & 1, 5, kTimeoutNs);  // copies land in microseconds
         }
       }
     } else if (warp == 1) {
       if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
-        const uint32_t idesc = instr_desc<A_MN, B_MN, TBN>();
+        const uint32_t idesc = instr_desc<A_MN, B_MN, NCAT ? 2 * TBN : TBN>();
+        // Descriptors of slot 0's planes; another slot or K step only moves
+        // the start address (bits 0-13, in 16-byte units; shared addresses
+        // stay below 256 KB, so the sum never carries out of the field).
+        const uint64_t adesc0 = operand_desc<A_MN>(smem_u32(smem), 0);
+        const uint64_t bdesc0 = operand_desc<B_MN>(smem_u32(smem) + TL::B_OFF, 0);
         int it = 0, group = 0;
         bool stop = false;
         for (int u = pair; u < units && !stop; u += pairs) {
           int t, kb, ke;
           unit_of(u, tiles, sp, num_k, t, kb, ke);
-          for (int kt = kb; kt < ke; kt++, it++) {
-            const bool group_start = (kt - kb) % GROUP == 0;
-            const uint32_t buf = (uint32_t)(group & 1);
-            if (group_start) {  // the promoters must have read this buffer's previous partial
-              if (!mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2, sp.wait_limit_ns)) {
-                stop = true;
-                break;
-              }
-              tc_fence_after();
-            }
-            const int st = it % STAGES;
-            if (!mbar_wait(&sh->split[st], (it / STAGES) & 1, 3, sp.wait_limit_ns)) {
+          for (int kt = kb; kt < ke; kt += SS, it++) {
+            const int nb = it % NBAR, n_in = ke - kt < SS ? ke - kt : SS;
+            if (!mbar_wait(&sh->split[nb], (it / NBAR) & 1, 3, sp.wait_limit_ns)) {
               stop = true;
               break;
             }
             tc_fence_after();
-            const uint32_t a_hi = smem_u32(smem + st * TL::STAGE_BYTES), a_lo = a_hi + A_BYTES;
-            const uint32_t b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + TL::B_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < BK / 8; kk++) {
-              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
-              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
-              const uint32_t d = tmem + buf * TBN;
-              mma_tf32_pair(d, dal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
-              mma_tf32_pair(d, dah, dbl, idesc, 1u);
-              mma_tf32_pair(d, dah, dbh, idesc, 1u);
+            for (int i = 0; i < n_in; i++) {
+              const int kq = kt + i, st = nb * SS + i;
+              const bool group_start = (kq - kb) % GROUP == 0;  // GROUP is a multiple of SS
+              const uint32_t buf = (uint32_t)(group & 1);
+              if (group_start) {  // the promoters must have read this buffer's previous partial
+                if (!mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2, sp.wait_limit_ns)) {
+                  stop = true;
+                  break;
+                }
+                tc_fence_after();
+              }
+              const uint64_t slot = (uint64_t)((st * TL::STAGE_BYTES) >> 4);
+              const uint32_t d = tmem + buf * ACC;
+  #pragma unroll
+              for (int kk = 0; kk < BK / 8; kk++) {
+                const uint64_t dbh = bdesc0 + slot + (uint64_t)((B_MN ? kk * 1024 : kk * 32) >> 4);
+                const uint64_t dbl = dbh + (TL::B_BYTES >> 4);
+                if constexpr (NCAT) {  // [B hi | B lo] from dbh: the CTA's 2 BNH rows
+                  const uint32_t tah = tmem + TL::A_COL0 + 32 * st + 8 * kk, tal = tah + 16;
+                  mma_tf32_pair_tmem_a(d, tal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
+                  mma_tf32_pair_tmem_a(d, tah, dbh, idesc, 1u);
+                } else if constexpr (ATM) {  // A hi at the slot's columns 0-15, A lo at 16-31; 8 columns per K step
+                  const uint32_t tah = tmem + TL::A_COL0 + 32 * st + 8 * kk, tal = tah + 16;
+                  mma_tf32_pair_tmem_a(d, tal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
+                  mma_tf32_pair_tmem_a(d, tah, dbl, idesc, 1u);
+                  mma_tf32_pair_tmem_a(d, tah, dbh, idesc, 1u);
+                } else {
+                  const uint64_t dah = adesc0 + slot + (uint64_t)((A_MN ? kk * 1024 : kk * 32) >> 4);
+                  const uint64_t dal = dah + (A_BYTES >> 4);
+                  mma_tf32_pair(d, dal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
+                  mma_tf32_pair(d, dah, dbl, idesc, 1u);
+                  mma_tf32_pair(d, dah, dbh, idesc, 1u);
+                }
+              }
+              if ((kq - kb) % GROUP == GROUP - 1 || kq == ke - 1) {
+                mma_commit_pair(&sh->pfull[buf]);
+                group++;
+              }
             }
-            mma_commit_pair(&sh->empty[st]);  // frees the slot in both CTAs
-            if ((kt - kb) % GROUP == GROUP - 1 || kt == ke - 1) {
-              mma_commit_pair(&sh->pfull[buf]);
-              group++;
-            }
+            if (stop) break;
+            mma_commit_pair(&sh->empty[nb]);  // frees the round's slots in both CTAs
           }
         }
         if (stop) *failed = 1;
@@ -909,58 +1070,115 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         mbar_wait(&sh->mma_done, 0, 6, kTimeoutNs);
       }
     } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + SPLITTERS) {
-      // ---- splitters (both CTAs): splitter w takes every SPLITTERS-th slice,
-      // starting with slice w, whichever ring slot it lands in; a gathered A
-      // operand is built here from its halo.
-      const int sw = warp - SPLIT_WARP0;
-      int it = 0;
-      bool stop = false;
-      int rows4[4] = {0, 0, 0, 0}, kind4[4] = {0, 0, 0, 0};
-      if constexpr (AS == A_IM2COL_POS) pos_rows<EK == EK_NCHW_POOL>(ga, lane, rows4);
-      for (int u = pair; u < units && !stop; u += pairs) {
-        int t, kb, ke;
-        unit_of(u, tiles, sp, num_k, t, kb, ke);
-        const int a_row = (t / n_tiles) * 2 * BM + (int)rank * BM;
-        if constexpr (AS == A_IM2COL_CK) ck_rows(ga, a_row, lane, rows4, kind4);
-        if constexpr (AS == A_IM2COL_POS_FULL) pos_rows_full<EK == EK_NCHW_POOL>(ga, a_row, s.M, lane, rows4, kind4);
-        for (int kt = kb; kt < ke; kt++, it++) {
-          if (it % SPLITTERS != sw) continue;
-          const int st = it % STAGES;
-          if (__shfl_sync(0xffffffffu, *failed, 0)) {
-            stop = true;
-            break;
-          }
-          uint8_t* stage = smem + st * TL::STAGE_BYTES;
-          // rows of this CTA's A block that the output uses
-          const int a_rows = (int)(s.M - a_row < BM ? (s.M - a_row > 0 ? s.M - a_row : 0) : BM);
-          if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4, sp.wait_limit_ns)) {
-            *failed = 1;
-            stop = true;
-            break;
-          }
-          if constexpr (AS == A_TMA) {
-            split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
-          } else {
-            // im2col tile from the halo in the lo plane into the hi plane,
-            // then split in place (the lo plane is overwritten only after
-            // every lane has read the halo). Rows past M are left as they
-            // are: they only reach rows of C that are never stored.
-            const float* halo = (const float*)(stage + (HSEP ? TL::HALO_OFFSET : A_BYTES));
-            uint8_t* lo = HSEP ? stage + A_BYTES : nullptr;  // with its own halo region: split while gathering
-            if constexpr (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL)
-              gather_pos<AS == A_IM2COL_POS_FULL>(ga, stage, lo, halo, a_rows, kt * BK, lane, rows4, kind4);
-            else
-              gather_ck(ga, stage, lo, halo, a_rows, lane, rows4, kind4);
-            if constexpr (!HSEP) {
+      if constexpr (ATM) {
+        // ---- gather warps (both CTAs): warp GATHER_WARP0 + q builds rows
+        // 32 q .. 32 q + 31 of every slice's A block in its lane quarter of
+        // tensor memory (lane = row), at the slot's 32 columns; warps 2-3
+        // have no part.
+        if (warp >= GATHER_WARP0) {
+          const int q = warp & 3, r = 32 * q + lane;
+          const uint32_t a_lanes = tmem + ((uint32_t)(32 * q) << 16) + TL::A_COL0;
+          int* tab = (int*)(smem + TL::TAB_OFFSET);
+          build_tap_table(ga, tab, r, 128);
+          asm volatile("bar.sync 1, 128;" ::: "memory");  // the four gather warps
+          const uint32_t tab_base = smem_u32(tab);
+          const int r16 = 16 % ga.KHW;
+          int it = 0, hb = 0, mk = 0;
+          bool stop = false;
+          if constexpr (AS == A_IM2COL_POS) hb = pos_row<EK == EK_NCHW_POOL>(ga, r);
+          for (int u = pair; u < units && !stop; u += pairs) {
+            int t, kb, ke;
+            unit_of(u, tiles, sp, num_k, t, kb, ke);
+            const int a_row = (t / n_tiles) * 2 * BM + (int)rank * BM;
+            if constexpr (AS == A_IM2COL_POS_FULL) pos_row_full<EK == EK_NCHW_POOL>(ga, a_row, s.M, r, hb, mk);
+            const bool live = (int64_t)a_row + r < s.M;  // a row past M gets zeros
+            int m = (kb * BK) % ga.KHW;                   // the slice's first entry's tap
+            for (int kt = kb; kt < ke; kt += SS, it++) {
+              const int nb = it % NBAR, n_in = ke - kt < SS ? ke - kt : SS;
+              if (__shfl_sync(0xffffffffu, *failed, 0)) {
+                stop = true;
+                break;
+              }
+              if (!__all_sync(0xffffffffu, mbar_wait(&sh->full[nb], (it / NBAR) & 1, 4, sp.wait_limit_ns))) {
+                *failed = 1;
+                stop = true;
+                break;
+              }
+              // The MMAs that last read these slots' columns completed before
+              // the producer refilled the slots (their empty barrier), and so
+              // before the copies this wait saw land.
+              tc_fence_after();
+              for (int i = 0; i < n_in; i++) {
+                const int st = nb * SS + i;
+                float v[32];
+                gather_row_split<AS == A_IM2COL_POS_FULL>(ga, smem_u32(smem + st * TL::STAGE_BYTES + TL::HALO_OFF),
+                                                          tab_base + 64u * m, live, (kt + i) * BK, hb, mk, v);
+                __syncwarp();
+                tmem_store32(a_lanes + 32 * st, v);
+                m = m + r16 >= ga.KHW ? m + r16 - ga.KHW : m + r16;
+              }
+              tmem_wait_st();
+              tc_fence_before();
               __syncwarp();
-              split_tf32((float4*)stage, (float4*)(stage + A_BYTES), a_rows * 64 / 16, lane);
+              if (lane == 0 && !(sp.withhold_arrive && it == 0 && leader)) mbar_arrive_rank(&sh->split[nb], 0);
             }
           }
-          if constexpr (BS != B_SPLIT2)
-            split_tf32((float4*)(stage + 2 * A_BYTES), (float4*)(stage + 2 * A_BYTES + TL::B_BYTES),
-                       TL::B_BYTES / 16, lane);
-          fence_async_shared();  // generic-proxy writes -> visible to the tensor core
-          if (!(sp.withhold_arrive && it == 0 && leader)) mbar_arrive_rank(&sh->split[st], 0);
+        }
+      } else {
+        // ---- splitters (both CTAs): splitter w takes every SPLITTERS-th slice,
+        // starting with slice w, whichever ring slot it lands in; a gathered A
+        // operand is built here from its halo.
+        static_assert(SS == 1, "the splitters take single slices");
+        const int sw = warp - SPLIT_WARP0;
+        int it = 0;
+        bool stop = false;
+        int rows4[4] = {0, 0, 0, 0}, kind4[4] = {0, 0, 0, 0};
+        if constexpr (AS == A_IM2COL_POS) pos_rows<EK == EK_NCHW_POOL>(ga, lane, rows4);
+        for (int u = pair; u < units && !stop; u += pairs) {
+          int t, kb, ke;
+          unit_of(u, tiles, sp, num_k, t, kb, ke);
+          const int a_row = (t / n_tiles) * 2 * BM + (int)rank * BM;
+          if constexpr (AS == A_IM2COL_CK) ck_rows(ga, a_row, lane, rows4, kind4);
+          if constexpr (AS == A_IM2COL_POS_FULL) pos_rows_full<EK == EK_NCHW_POOL>(ga, a_row, s.M, lane, rows4, kind4);
+          for (int kt = kb; kt < ke; kt++, it++) {
+            if (it % SPLITTERS != sw) continue;
+            const int st = it % STAGES;
+            if (__shfl_sync(0xffffffffu, *failed, 0)) {
+              stop = true;
+              break;
+            }
+            uint8_t* stage = smem + st * TL::STAGE_BYTES;
+            // rows of this CTA's A block that the output uses
+            const int a_rows = (int)(s.M - a_row < BM ? (s.M - a_row > 0 ? s.M - a_row : 0) : BM);
+            if (!mbar_wait(&sh->full[st], (it / STAGES) & 1, 4, sp.wait_limit_ns)) {
+              *failed = 1;
+              stop = true;
+              break;
+            }
+            if constexpr (AS == A_TMA) {
+              split_tf32((float4*)stage, (float4*)(stage + A_BYTES), A_BYTES / 16, lane);
+            } else {
+              // im2col tile from the halo in the lo plane into the hi plane,
+              // then split in place (the lo plane is overwritten only after
+              // every lane has read the halo). Rows past M are left as they
+              // are: they only reach rows of C that are never stored.
+              const float* halo = (const float*)(stage + TL::HALO_OFF);
+              uint8_t* lo = HSEP ? stage + A_BYTES : nullptr;  // with its own halo region: split while gathering
+              if constexpr (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL)
+                gather_pos<AS == A_IM2COL_POS_FULL>(ga, stage, lo, halo, a_rows, kt * BK, lane, rows4, kind4);
+              else
+                gather_ck(ga, stage, lo, halo, a_rows, lane, rows4, kind4);
+              if constexpr (!HSEP) {
+                __syncwarp();
+                split_tf32((float4*)stage, (float4*)(stage + A_BYTES), a_rows * 64 / 16, lane);
+              }
+            }
+            if constexpr (BS != B_SPLIT2)
+              split_tf32((float4*)(stage + TL::B_OFF), (float4*)(stage + TL::B_OFF + TL::B_BYTES), TL::B_BYTES / 16,
+                         lane);
+            fence_async_shared();  // generic-proxy writes -> visible to the tensor core
+            if (!(sp.withhold_arrive && it == 0 && leader)) mbar_arrive_rank(&sh->split[st], 0);
+          }
         }
       }
     }
@@ -970,7 +1188,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // this warp's rows, columns [HC*h, HC*h + HC) its half of the tile.
     // Every decision below is warp-uniform: tcgen05.ld is .sync.aligned.
     const int q = warp & 3, h = (warp - 8) >> 2;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + HC * h;
+    // (NCAT: this half's columns with B hi at h * TBN, those with B lo HC after)
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (NCAT ? TBN * h : HC * h);
     float* xpose = (float*)(smem + TL::EPI_OFFSET) + (warp - 8) * 32 * EPI_LD;
     int group = 0;
     for (int u = pair; u < units && !__shfl_sync(0xffffffffu, *failed, 0); u += pairs) {
@@ -996,12 +1215,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
+        if constexpr (NCAT) {
+          static_assert(HC == 32, "one chunk per half");
+          float p[32], pl[32];
+          tmem_load32(lane_base + buf * ACC, p);
+          tmem_load32(lane_base + buf * ACC + HC, pl);
 #pragma unroll
-        for (int j = 0; j < HC / 32; j++) {
-          float p[32];
-          tmem_load32(lane_base + buf * TBN + 32 * j, p);
+          for (int i = 0; i < 32; i++) tot[i] = __fadd_rn(tot[i], __fadd_rn(p[i], pl[i]));
+        } else {
 #pragma unroll
-          for (int i = 0; i < 32; i++) tot[32 * j + i] = __fadd_rn(tot[32 * j + i], p[i]);
+          for (int j = 0; j < HC / 32; j++) {
+            float p[32];
+            tmem_load32(lane_base + buf * ACC + 32 * j, p);
+#pragma unroll
+            for (int i = 0; i < 32; i++) tot[32 * j + i] = __fadd_rn(tot[32 * j + i], p[i]);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -1214,7 +1442,7 @@ template <bool A_MN, bool B_MN, int EK, int TBN = BN, int AS = A_TMA, int BS = B
 static char* launch_kernel(gt_ctx* ctx, const GemmShape& s, const CUtensorMap& ta, const CUtensorMap& tb,
                            const Epi<float>& epi, const SplitPlan& sp, const Gather& ga) {
   auto kern = gemm_tf32x3_pair_kernel<A_MN, B_MN, EK, TBN, AS, BS>;
-  using TL = Tile<TBN, halo_region<TBN, AS>()>;
+  using TL = LayoutOf<TBN, AS>;
   static bool configured[64] = {};
   if (ctx->device < 0 || ctx->device >= 64 || !configured[ctx->device]) {
     GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TL::SMEM_BYTES));
@@ -1576,7 +1804,7 @@ static bool halo_fits(Gather& ga) {
 // halo box covers just them; otherwise (Gather::full) the box holds the whole
 // padded images that any 128 consecutive positions touch, if that fits.
 static bool halo_pos(const gt_geom& g, Gather& ga) {
-  if (!halo_common(g, ga)) return false;
+  if (!halo_common(g, ga) || ga.KHW > 64) return false;  // the tap table holds 64 taps
   const int64_t L = g.OH * g.OW;
   if (L % 128 == 0 && 128 % g.OW == 0) {
     ga.bh = (int)(128 / g.OW), ga.box_n = 1;
@@ -1615,7 +1843,7 @@ static bool halo_ck(const gt_geom& g, Gather& ga) {
 // map over (H * W, C, N) for any 128 consecutive positions, if they fit.
 static bool halo_pos_full(const gt_geom& g, Gather& ga) {
   const int64_t plane = g.H * g.W, L = g.OH * g.OW;
-  if (g.stride != 1 || plane > 256 || plane % 4 || g.KH * g.KW > 32 || g.pad > 64 || L < 1) return false;
+  if (g.stride != 1 || plane > 256 || plane % 4 || g.KH * g.KW > 32 || g.pad > 64 || L < 1) return false;  // 32 mask bits
   ga.C = (int)g.C, ga.H = (int)g.H, ga.W = (int)g.W, ga.KH = (int)g.KH, ga.KW = (int)g.KW, ga.OW = (int)g.OW;
   ga.pad = (int)g.pad, ga.L = (int)L, ga.KHW = (int)(g.KH * g.KW), ga.CKK = (int)(g.C * g.KH * g.KW);
   ga.rp = 0, ga.full = 1;
