@@ -552,13 +552,18 @@ def step_roofline(lib, model, steps, wl, key):
         if i >= n.value - n.value // steps:
             last_step.append((key_s, round(ms.value, 4)))
         flops = 2.0 * mnk[0] * mnk[1] * mnk[2]
-        e = shapes.setdefault(key_s, {"launches": 0, "ms": 0.0, "flops": flops, "path": path.value})
+        e = shapes.setdefault(key_s, {"launches": 0, "times": [], "flops": flops, "path": path.value})
         e["launches"] += 1
-        e["ms"] += ms.value
-        total_ms += ms.value
+        e["times"].append(ms.value)
         total_flops += flops
         paths.add(path.value)
     check(lib.gt_gemm_timer_stop(ctx))
+    # A shape's time per launch is the median over its launches in the pass:
+    # a launch whose bracket caught a one-off stall (the pool growing its
+    # workspace, say) does not stand for the kernel.
+    for v in shapes.values():
+        v["ms"] = statistics.median(v["times"]) * v["launches"]
+        total_ms += v["ms"]
     per_step = n.value // steps
     achieved = total_flops / (total_ms / 1e3) / 1e12
     traffic = None
@@ -570,6 +575,7 @@ def step_roofline(lib, model, steps, wl, key):
              6: "SIMT thin GEMM (a classifier's 10 classes: a warp per row, or a thread per column)",
              7: "SIMT direct convolution + ReLU + 2x2 pool (first conv, K = C*9)"}
     breakdown = {k: {"launches_per_step": v["launches"] // steps, "ms_per_launch": v["ms"] / v["launches"],
+                     "ms_max": max(v["times"]),
                      "tflops": v["flops"] * v["launches"] / (v["ms"] / 1e3) / 1e12,
                      "path": names.get(v["path"], str(v["path"]))} for k, v in shapes.items()}
     step_ms = pass_ms.value / steps

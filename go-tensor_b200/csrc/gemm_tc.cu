@@ -100,7 +100,6 @@ struct Tile {
   static constexpr uint32_t B_OFF = 2 * A_BYTES;                        // B hi (B lo follows)
   static constexpr uint32_t HALO_OFF = HALO ? HALO_OFFSET : A_BYTES;  // a gathered operand's halo
   static constexpr uint32_t A_COL0 = 0;                               // unused: A is in shared memory
-  static constexpr bool NCAT = false;
   static constexpr int ACC = BN;
   static constexpr int STAGES = tc::STAGES;
   static constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
@@ -115,22 +114,21 @@ struct Tile {
 };
 
 // Layout of an instantiation whose gathered A operand goes to tensor memory
-// (tile widths 64 and 128): the two partial accumulators take columns
-// 0 .. 2 ACC - 1, and ring slot s keeps its slice's A hi and A lo (16 columns
-// each, lane = row, column = k, the layout the MMA reads A from tensor memory
-// in) at columns A_COL0 + 32 s. Shared memory holds per slot only B's two
-// planes and the halo, so the ring is as deep as the columns allow.
-// NCAT (width 64): each CTA's B hi and B lo rows are adjacent, so one MMA of
-// width 2 BN multiplies an A plane by both: two MMAs per K step (A hi and
-// A lo against [B hi | B lo]) instead of three, whose issue bounds the narrow
-// tile. An accumulator then holds each output column twice, the products
-// with B hi and with B lo, which the promoters add.
+// (tile width 64): the two partial accumulators take columns 0 .. 2 ACC - 1,
+// and ring slot s keeps its slice's A hi and A lo (16 columns each, lane =
+// row, column = k, the layout the MMA reads A from tensor memory in) at
+// columns A_COL0 + 32 s. Shared memory holds per slot only B's two planes and
+// the halo, so the ring is as deep as the columns allow.
+// Each CTA's B hi and B lo rows are adjacent, so one MMA of width 2 BN
+// multiplies an A plane by both: two MMAs per K step (A hi and A lo against
+// [B hi | B lo]) instead of three, whose issue bounds the narrow tile. An
+// accumulator then holds each output column twice, the products with B hi
+// and with B lo, which the promoters add.
 template <int BN>
 struct TileT {
-  static_assert(BN == 64 || BN == 128, "tile width");
+  static_assert(BN == 64, "tile width");
   static constexpr int BNH = BN / 2;
-  static constexpr bool NCAT = BN == 64;
-  static constexpr int ACC = NCAT ? 2 * BN : BN;  // accumulator columns per partial buffer
+  static constexpr int ACC = 2 * BN;  // accumulator columns per partial buffer
   static constexpr uint32_t B_BYTES = BNH * BK * 4;
   static constexpr uint32_t B_OFF = 0;
   static constexpr uint32_t HALO_OFF = 2 * B_BYTES;
@@ -862,19 +860,18 @@ constexpr bool halo_region() {
   return AS != A_TMA && TBN <= 128;
 }
 
-// A position-gathered operand (A_IM2COL_POS, A_IM2COL_POS_FULL) of a tile up
-// to 128 wide goes to tensor memory: four gather warps (one per lane quarter)
-// write each slice's split rows with tcgen05.st, the MMA reads A from there
-// and B from shared memory. Shared memory then carries no A planes, whose
-// stores and the MMA's reads of them bound the narrow tiles.
+// A position-gathered operand (A_IM2COL_POS, A_IM2COL_POS_FULL) of a 64-wide
+// tile goes to tensor memory: four gather warps (one per lane quarter) write
+// each slice's split rows with tcgen05.st, the MMA reads A from there and B
+// from shared memory, two MMAs per K step. (Measured: at width 128 the
+// shared-memory path, three MMAs per K step, is as fast or faster.)
 template <int TBN, int AS>
 constexpr bool a_in_tmem() {
-  return (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL) && TBN <= 128;
+  return (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL) && TBN == 64;
 }
 
 template <int TBN, int AS>
-using LayoutOf = std::conditional_t<a_in_tmem<TBN, AS>(), TileT<(TBN > 128 ? 128 : TBN)>,
-                                    Tile<TBN, halo_region<TBN, AS>()>>;
+using LayoutOf = std::conditional_t<a_in_tmem<TBN, AS>(), TileT<64>, Tile<TBN, halo_region<TBN, AS>()>>;
 constexpr int GATHER_WARP0 = 4;  // warps 4..7 (lane quarters 0..3) gather into tensor memory
 
 template <bool A_MN, bool B_MN, int EK, int TBN, int AS, int BS>
@@ -884,7 +881,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   constexpr bool HSEP = halo_region<TBN, AS>();
   constexpr bool ATM = a_in_tmem<TBN, AS>();
   using TL = LayoutOf<TBN, AS>;
-  constexpr bool NCAT = TL::NCAT;
   constexpr int ACC = TL::ACC;
   // Slices per barrier round: with A in tensor memory two ring slots fill,
   // gather and free together (one wait and one commit per two slices: the
@@ -1001,7 +997,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
     } else if (warp == 1) {
       if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
-        const uint32_t idesc = instr_desc<A_MN, B_MN, NCAT ? 2 * TBN : TBN>();
+        const uint32_t idesc = instr_desc<A_MN, B_MN, ATM ? 2 * TBN : TBN>();
         // Descriptors of slot 0's planes; another slot or K step only moves
         // the start address (bits 0-13, in 16-byte units; shared addresses
         // stay below 256 KB, so the sum never carries out of the field).
@@ -1036,14 +1032,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               for (int kk = 0; kk < BK / 8; kk++) {
                 const uint64_t dbh = bdesc0 + slot + (uint64_t)((B_MN ? kk * 1024 : kk * 32) >> 4);
                 const uint64_t dbl = dbh + (TL::B_BYTES >> 4);
-                if constexpr (NCAT) {  // [B hi | B lo] from dbh: the CTA's 2 BNH rows
+                if constexpr (ATM) {
+                  // A hi at the slot's columns 0-15, A lo at 16-31 (8 columns
+                  // per K step), each against [B hi | B lo] from dbh: the
+                  // CTA's 2 BNH rows
                   const uint32_t tah = tmem + TL::A_COL0 + 32 * st + 8 * kk, tal = tah + 16;
                   mma_tf32_pair_tmem_a(d, tal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
-                  mma_tf32_pair_tmem_a(d, tah, dbh, idesc, 1u);
-                } else if constexpr (ATM) {  // A hi at the slot's columns 0-15, A lo at 16-31; 8 columns per K step
-                  const uint32_t tah = tmem + TL::A_COL0 + 32 * st + 8 * kk, tal = tah + 16;
-                  mma_tf32_pair_tmem_a(d, tal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
-                  mma_tf32_pair_tmem_a(d, tah, dbl, idesc, 1u);
                   mma_tf32_pair_tmem_a(d, tah, dbh, idesc, 1u);
                 } else {
                   const uint64_t dah = adesc0 + slot + (uint64_t)((A_MN ? kk * 1024 : kk * 32) >> 4);
@@ -1188,8 +1182,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // this warp's rows, columns [HC*h, HC*h + HC) its half of the tile.
     // Every decision below is warp-uniform: tcgen05.ld is .sync.aligned.
     const int q = warp & 3, h = (warp - 8) >> 2;
-    // (NCAT: this half's columns with B hi at h * TBN, those with B lo HC after)
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (NCAT ? TBN * h : HC * h);
+    // (A in tensor memory: this half's columns with B hi at h * TBN, those
+    // with B lo HC after)
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (ATM ? TBN * h : HC * h);
     float* xpose = (float*)(smem + TL::EPI_OFFSET) + (warp - 8) * 32 * EPI_LD;
     int group = 0;
     for (int u = pair; u < units && !__shfl_sync(0xffffffffu, *failed, 0); u += pairs) {
@@ -1215,7 +1210,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        if constexpr (NCAT) {
+        if constexpr (ATM) {
           static_assert(HC == 32, "one chunk per half");
           float p[32], pl[32];
           tmem_load32(lane_base + buf * ACC, p);
