@@ -232,3 +232,47 @@ def test_timed_out_wait_returns_an_error_and_the_context_recovers():
     assert lib.gt_gemm_path_taken() == 2
     want = cpu_backend().MatMul(T.CPUStorage(a), T.CPUStorage(b), m, k, n, False, False).data
     assert_close(got, want, 1e-4, "GEMM after the timed-out one")
+
+
+def test_timed_out_wait_in_the_tensor_memory_conv_kernel():
+    """The same error path in the implicit convolution whose gathered A
+    operand goes to tensor memory (a 64-wide input gradient: four gather
+    warps per CTA, pairs of slices per barrier round, 512 tensor-memory
+    columns). The leader CTA's gather warps withhold their arrival for the
+    first round; the MMA issuer's wait runs out, the kernel frees its tensor
+    memory and returns, gt_sync reports the site, and the same convolution
+    then gives its earlier result bit for bit."""
+    import ctypes
+    import time
+
+    from gotensor._lib import GTError, check
+    lib = _lib.cuda_lib()
+    be = cuda_backend()
+    be.Sync()
+    N, C, H, W, O = 4, 64, 16, 16, 128
+    g = T.conv_geom("Conv2d", [N, C, H, W], 3, 3, 1, 1)
+    gg = ctypes.byref(_lib.GtGeom(*[getattr(g, f) for f, _ in _lib.GtGeom._fields_]))
+    rng = np.random.default_rng(10)
+    dy = be.FromHost(rng.standard_normal(N * O * H * W).astype(np.float32))
+    w = be.FromHost(rng.standard_normal(O * C * 9).astype(np.float32))
+    dx = be.Zeros(T.Float32, N * C * H * W)
+
+    def run():
+        check(lib.gt_conv_bwd_data(be.ctx.ptr, 0, dy.ptr, w.ptr, dx.ptr, gg, O))
+        assert lib.gt_gemm_path_taken() == 4
+
+    run()
+    want = be.ToHost(dx)
+    lib.gt_debug_set_tc_wait_limit_us(20000)
+    try:
+        lib.gt_debug_tc_withhold_arrive()
+        t0 = time.time()
+        run()
+        with pytest.raises(GTError, match=r"pipeline wait timed out \(site \d\)"):
+            be.Sync()
+        assert time.time() - t0 < 10
+        be.Sync()
+    finally:
+        lib.gt_debug_set_tc_wait_limit_us(0)
+    run()
+    assert np.array_equal(be.ToHost(dx), want)
