@@ -381,6 +381,15 @@ __device__ __forceinline__ void mma_tf32_pair_tmem_a(uint32_t tmem_d, uint32_t t
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// One lane of the converged warp (elect.sync): the producer and MMA warps run
+// their loops warp-wide, so addresses and descriptors stay warp-uniform, and
+// only the elected lane issues the copies, MMAs and commits.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(e));
+  return e != 0;
+}
+
 // Arrives on `bar` in both CTAs of the pair once the MMAs issued so far complete.
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
   asm volatile(
@@ -935,9 +944,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (warp < 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_LOW));
     if (warp == 0) {
-      if (lane == 0) {  // ---- TMA producer (both CTAs)
+      {  // ---- TMA producer (both CTAs): the warp runs the loop, the elected lane issues
+        const bool issuer = elect_one();
         int it = 0, issued_to = 0;  // barrier rounds (SS slices each)
-        for (int u = pair; u < units && !*failed; u += pairs) {
+        for (int u = pair; u < units && !__shfl_sync(0xffffffffu, *failed, 0); u += pairs) {
           int t, kb, ke;
           unit_of(u, tiles, sp, num_k, t, kb, ke);
           const int mt = t / n_tiles, nt = t % n_tiles;
@@ -945,58 +955,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const int b_row = nt * TBN + (int)rank * TL::BNH;
           for (int kt = kb; kt < ke; kt += SS, it++) {
             const int nb = it % NBAR, n_in = ke - kt < SS ? ke - kt : SS;
-            if (!mbar_wait(&sh->empty[nb], ((it / NBAR) & 1) ^ 1, 1, sp.wait_limit_ns)) {
-              *failed = 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&sh->empty[nb], ((it / NBAR) & 1) ^ 1, 1, sp.wait_limit_ns))) {
+              if (lane == 0) *failed = 1;
               break;
             }
-            uint64_t* bar = &sh->full[nb];
-            mbar_expect_tx(bar, (uint32_t)n_in * ((AS == A_TMA ? A_BYTES : ga.halo_bytes) +
-                                                  (BS == B_SPLIT2 ? 2u : 1u) * TL::B_BYTES));
-            for (int i = 0; i < n_in; i++) {
-              const int st = nb * SS + i;
-              uint8_t* a_hi = smem + st * TL::STAGE_BYTES;
-              uint8_t* b_hi = a_hi + TL::B_OFF;
-              const int k0 = (kt + i) * BK;
-              if constexpr (AS == A_IM2COL_POS) {  // the halo of this block's positions, the slice's channels
-                const int n0 = a_row / ga.L, oh0 = (a_row - n0 * ga.L) / ga.OW;
-                tma_load_4d(a_hi + TL::HALO_OFF, &tmA, bar, -ga.rp, oh0 - ga.pad, k0 / ga.KHW, n0);
-              } else if constexpr (AS == A_IM2COL_POS_FULL) {  // whole planes: the slice's channels, box_n images
-                tma_load_3d(a_hi + TL::HALO_OFF, &tmA, bar, 0, k0 / ga.KHW, a_row / ga.L);
-              } else if constexpr (AS == A_IM2COL_CK) {  // the halo of the slice's positions, this block's channels
-                const int n = k0 / ga.L, l0 = k0 - n * ga.L, oh0 = l0 / ga.OW, ow0 = l0 - oh0 * ga.OW;
-                tma_load_4d(a_hi + TL::HALO_OFF, &tmA, bar, ow0 - ga.rp, oh0 - ga.pad, a_row / ga.KHW, n);
-              }
-              if constexpr (AS == A_TMA) {
-                if (A_MN) {
+            if (issuer) {
+              uint64_t* bar = &sh->full[nb];
+              mbar_expect_tx(bar, (uint32_t)n_in * ((AS == A_TMA ? A_BYTES : ga.halo_bytes) +
+                                                    (BS == B_SPLIT2 ? 2u : 1u) * TL::B_BYTES));
+              for (int i = 0; i < n_in; i++) {
+                const int st = nb * SS + i;
+                uint8_t* a_hi = smem + st * TL::STAGE_BYTES;
+                uint8_t* b_hi = a_hi + TL::B_OFF;
+                const int k0 = (kt + i) * BK;
+                if constexpr (AS == A_IM2COL_POS) {  // the halo of this block's positions, the slice's channels
+                  const int n0 = a_row / ga.L, oh0 = (a_row - n0 * ga.L) / ga.OW;
+                  tma_load_4d(a_hi + TL::HALO_OFF, &tmA, bar, -ga.rp, oh0 - ga.pad, k0 / ga.KHW, n0);
+                } else if constexpr (AS == A_IM2COL_POS_FULL) {  // whole planes: the slice's channels, box_n images
+                  tma_load_3d(a_hi + TL::HALO_OFF, &tmA, bar, 0, k0 / ga.KHW, a_row / ga.L);
+                } else if constexpr (AS == A_IM2COL_CK) {  // the halo of the slice's positions, this block's channels
+                  const int n = k0 / ga.L, l0 = k0 - n * ga.L, oh0 = l0 / ga.OW, ow0 = l0 - oh0 * ga.OW;
+                  tma_load_4d(a_hi + TL::HALO_OFF, &tmA, bar, ow0 - ga.rp, oh0 - ga.pad, a_row / ga.KHW, n);
+                }
+                if constexpr (AS == A_TMA) {
+                  if (A_MN) {
 #pragma unroll
-                  for (int j = 0; j < BM / 32; j++) tma_load_2d(a_hi + j * kLboMN, &tmA, bar, a_row + 32 * j, k0);
+                    for (int j = 0; j < BM / 32; j++) tma_load_2d(a_hi + j * kLboMN, &tmA, bar, a_row + 32 * j, k0);
+                  } else {
+                    tma_load_2d(a_hi, &tmA, bar, k0, a_row);
+                  }
+                }
+                if constexpr (BS == B_TMA3) {  // K index = image * L + position
+                  const int img = k0 / ga.L;
+                  tma_load_3d(b_hi, &tmB, bar, k0 - img * ga.L, b_row, img);
+                } else if constexpr (BS == B_SPLIT2) {  // both planes, already split
+                  tma_load_2d(b_hi, &tmB, bar, k0, b_row);
+                  tma_load_2d(b_hi + TL::B_BYTES, &tmB, bar, k0, ga.b_lo_row + b_row);
+                } else if (B_MN) {
+#pragma unroll
+                  for (int j = 0; j < TL::BNH / 32; j++) tma_load_2d(b_hi + j * kLboMN, &tmB, bar, b_row + 32 * j, k0);
                 } else {
-                  tma_load_2d(a_hi, &tmA, bar, k0, a_row);
+                  tma_load_2d(b_hi, &tmB, bar, k0, b_row);
                 }
               }
-              if constexpr (BS == B_TMA3) {  // K index = image * L + position
-                const int img = k0 / ga.L;
-                tma_load_3d(b_hi, &tmB, bar, k0 - img * ga.L, b_row, img);
-              } else if constexpr (BS == B_SPLIT2) {  // both planes, already split
-                tma_load_2d(b_hi, &tmB, bar, k0, b_row);
-                tma_load_2d(b_hi + TL::B_BYTES, &tmB, bar, k0, ga.b_lo_row + b_row);
-              } else if (B_MN) {
-#pragma unroll
-                for (int j = 0; j < TL::BNH / 32; j++) tma_load_2d(b_hi + j * kLboMN, &tmB, bar, b_row + 32 * j, k0);
-              } else {
-                tma_load_2d(b_hi, &tmB, bar, k0, b_row);
-              }
             }
+            __syncwarp();
             issued_to = it + 1;
           }
         }
-        if (*failed) {  // let copies in flight land before the CTA tears down
+        if (__shfl_sync(0xffffffffu, *failed, 0)) {  // let copies in flight land before the CTA tears down
           for (int i = issued_to > NBAR ? issued_to - NBAR : 0; i < issued_to; i++)
             mbar_wait(&sh->full[i % NBAR], (i / NBAR) & 1, 5, kTimeoutNs);  // copies land in microseconds
         }
       }
     } else if (warp == 1) {
-      if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
+      if (leader) {  // ---- MMA issuer (leader CTA only): the warp runs the loop, the elected lane issues
+        const bool issuer = elect_one();
         const uint32_t idesc = instr_desc<A_MN, B_MN, ATM ? 2 * TBN : TBN>();
         // Descriptors of slot 0's planes; another slot or K step only moves
         // the start address (bits 0-13, in 16-byte units; shared addresses
@@ -1010,7 +1024,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           unit_of(u, tiles, sp, num_k, t, kb, ke);
           for (int kt = kb; kt < ke; kt += SS, it++) {
             const int nb = it % NBAR, n_in = ke - kt < SS ? ke - kt : SS;
-            if (!mbar_wait(&sh->split[nb], (it / NBAR) & 1, 3, sp.wait_limit_ns)) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&sh->split[nb], (it / NBAR) & 1, 3, sp.wait_limit_ns))) {
               stop = true;
               break;
             }
@@ -1020,7 +1034,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               const bool group_start = (kq - kb) % GROUP == 0;  // GROUP is a multiple of SS
               const uint32_t buf = (uint32_t)(group & 1);
               if (group_start) {  // the promoters must have read this buffer's previous partial
-                if (!mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2, sp.wait_limit_ns)) {
+                if (!__all_sync(0xffffffffu,
+                                mbar_wait(&sh->pempty[buf], ((group >> 1) & 1) ^ 1, 2, sp.wait_limit_ns))) {
                   stop = true;
                   break;
                 }
@@ -1028,39 +1043,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               }
               const uint64_t slot = (uint64_t)((st * TL::STAGE_BYTES) >> 4);
               const uint32_t d = tmem + buf * ACC;
-  #pragma unroll
+              // the slice's operands, computed by the whole warp (uniform)
+              uint64_t dbh[BK / 8], dbl[BK / 8], dah[BK / 8], dal[BK / 8];
+              uint32_t tah[BK / 8], tal[BK / 8];
+#pragma unroll
               for (int kk = 0; kk < BK / 8; kk++) {
-                const uint64_t dbh = bdesc0 + slot + (uint64_t)((B_MN ? kk * 1024 : kk * 32) >> 4);
-                const uint64_t dbl = dbh + (TL::B_BYTES >> 4);
-                if constexpr (ATM) {
-                  // A hi at the slot's columns 0-15, A lo at 16-31 (8 columns
-                  // per K step), each against [B hi | B lo] from dbh: the
-                  // CTA's 2 BNH rows
-                  const uint32_t tah = tmem + TL::A_COL0 + 32 * st + 8 * kk, tal = tah + 16;
-                  mma_tf32_pair_tmem_a(d, tal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
-                  mma_tf32_pair_tmem_a(d, tah, dbh, idesc, 1u);
-                } else {
-                  const uint64_t dah = adesc0 + slot + (uint64_t)((A_MN ? kk * 1024 : kk * 32) >> 4);
-                  const uint64_t dal = dah + (A_BYTES >> 4);
-                  mma_tf32_pair(d, dal, dbh, idesc, (group_start && kk == 0) ? 0u : 1u);
-                  mma_tf32_pair(d, dah, dbl, idesc, 1u);
-                  mma_tf32_pair(d, dah, dbh, idesc, 1u);
+                dbh[kk] = bdesc0 + slot + (uint64_t)((B_MN ? kk * 1024 : kk * 32) >> 4);
+                dbl[kk] = dbh[kk] + (TL::B_BYTES >> 4);
+                dah[kk] = adesc0 + slot + (uint64_t)((A_MN ? kk * 1024 : kk * 32) >> 4);
+                dal[kk] = dah[kk] + (A_BYTES >> 4);
+                // A in tensor memory: hi at the slot's columns 0-15, lo at
+                // 16-31, 8 columns per K step
+                tah[kk] = tmem + TL::A_COL0 + 32 * st + 8 * kk;
+                tal[kk] = tah[kk] + 16;
+              }
+              if (issuer) {
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; kk++) {
+                  const uint32_t acc0 = (group_start && kk == 0) ? 0u : 1u;
+                  if constexpr (ATM) {  // each A plane against [B hi | B lo] from dbh: the CTA's 2 BNH rows
+                    mma_tf32_pair_tmem_a(d, tal[kk], dbh[kk], idesc, acc0);
+                    mma_tf32_pair_tmem_a(d, tah[kk], dbh[kk], idesc, 1u);
+                  } else {
+                    mma_tf32_pair(d, dal[kk], dbh[kk], idesc, acc0);
+                    mma_tf32_pair(d, dah[kk], dbl[kk], idesc, 1u);
+                    mma_tf32_pair(d, dah[kk], dbh[kk], idesc, 1u);
+                  }
                 }
               }
+              __syncwarp();
               if ((kq - kb) % GROUP == GROUP - 1 || kq == ke - 1) {
-                mma_commit_pair(&sh->pfull[buf]);
+                if (issuer) mma_commit_pair(&sh->pfull[buf]);
+                __syncwarp();
                 group++;
               }
             }
             if (stop) break;
-            mma_commit_pair(&sh->empty[nb]);  // frees the round's slots in both CTAs
+            if (issuer) mma_commit_pair(&sh->empty[nb]);  // frees the round's slots in both CTAs
+            __syncwarp();
           }
         }
-        if (stop) *failed = 1;
-        // Every MMA must be complete before the pair frees its tensor memory.
-        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                         smem_u32(&sh->mma_done))
-                     : "memory");
+        if (stop && lane == 0) *failed = 1;
+        // Every MMA must be complete before the pair frees its tensor memory
+        // (the commit tracks the issuing lane's MMAs).
+        if (issuer)
+          asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                           smem_u32(&sh->mma_done))
+                       : "memory");
+        __syncwarp();
         mbar_wait(&sh->mma_done, 0, 6, kTimeoutNs);
       }
     } else if (warp >= SPLIT_WARP0 && warp < SPLIT_WARP0 + SPLITTERS) {
