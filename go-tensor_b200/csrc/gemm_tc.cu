@@ -100,6 +100,7 @@ struct Tile {
   static constexpr uint32_t B_OFF = 2 * A_BYTES;                        // B hi (B lo follows)
   static constexpr uint32_t HALO_OFF = HALO ? HALO_OFFSET : A_BYTES;  // a gathered operand's halo
   static constexpr uint32_t A_COL0 = 0;                               // unused: A is in shared memory
+  static constexpr bool NCAT = false;
   static constexpr int ACC = BN;
   static constexpr int STAGES = tc::STAGES;
   static constexpr uint32_t BAR_OFFSET = STAGES * STAGE_BYTES;
@@ -114,21 +115,22 @@ struct Tile {
 };
 
 // Layout of an instantiation whose gathered A operand goes to tensor memory
-// (tile width 64): the two partial accumulators take columns 0 .. 2 ACC - 1,
-// and ring slot s keeps its slice's A hi and A lo (16 columns each, lane =
-// row, column = k, the layout the MMA reads A from tensor memory in) at
-// columns A_COL0 + 32 s. Shared memory holds per slot only B's two planes and
-// the halo, so the ring is as deep as the columns allow.
-// Each CTA's B hi and B lo rows are adjacent, so one MMA of width 2 BN
-// multiplies an A plane by both: two MMAs per K step (A hi and A lo against
-// [B hi | B lo]) instead of three, whose issue bounds the narrow tile. An
-// accumulator then holds each output column twice, the products with B hi
-// and with B lo, which the promoters add.
+// (tile widths 64 and 128): the two partial accumulators take columns
+// 0 .. 2 ACC - 1, and ring slot s keeps its slice's A hi and A lo (16 columns
+// each, lane = row, column = k, the layout the MMA reads A from tensor memory
+// in) at columns A_COL0 + 32 s. Shared memory holds per slot only B's two
+// planes and the halo, so the ring is as deep as the columns allow.
+// NCAT (width 64): each CTA's B hi and B lo rows are adjacent, so one MMA of
+// width 2 BN multiplies an A plane by both: two MMAs per K step (A hi and
+// A lo against [B hi | B lo]) instead of three, whose issue bounds the
+// narrow tile. An accumulator then holds each output column twice, the
+// products with B hi and with B lo, which the promoters add.
 template <int BN>
 struct TileT {
-  static_assert(BN == 64, "tile width");
+  static_assert(BN == 64 || BN == 128, "tile width");
   static constexpr int BNH = BN / 2;
-  static constexpr int ACC = 2 * BN;  // accumulator columns per partial buffer
+  static constexpr bool NCAT = BN == 64;
+  static constexpr int ACC = NCAT ? 2 * BN : BN;  // accumulator columns per partial buffer
   static constexpr uint32_t B_BYTES = BNH * BK * 4;
   static constexpr uint32_t B_OFF = 0;
   static constexpr uint32_t HALO_OFF = 2 * B_BYTES;
@@ -869,18 +871,20 @@ constexpr bool halo_region() {
   return AS != A_TMA && TBN <= 128;
 }
 
-// A position-gathered operand (A_IM2COL_POS, A_IM2COL_POS_FULL) of a 64-wide
-// tile goes to tensor memory: four gather warps (one per lane quarter) write
-// each slice's split rows with tcgen05.st, the MMA reads A from there and B
-// from shared memory, two MMAs per K step. (Measured: at width 128 the
-// shared-memory path, three MMAs per K step, is as fast or faster.)
+// A position-gathered operand (A_IM2COL_POS, A_IM2COL_POS_FULL) of a tile up
+// to 128 wide goes to tensor memory: four gather warps (one per lane quarter)
+// write each slice's split rows with tcgen05.st, the MMA reads A from there
+// and B from shared memory. Shared memory then carries no A planes, whose
+// stores and the MMAs' reads of them (three reads of A per K step) bound
+// these tiles on the shared-memory path.
 template <int TBN, int AS>
 constexpr bool a_in_tmem() {
-  return (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL) && TBN == 64;
+  return (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL) && TBN <= 128;
 }
 
 template <int TBN, int AS>
-using LayoutOf = std::conditional_t<a_in_tmem<TBN, AS>(), TileT<64>, Tile<TBN, halo_region<TBN, AS>()>>;
+using LayoutOf = std::conditional_t<a_in_tmem<TBN, AS>(), TileT<(TBN > 128 ? 128 : TBN)>,
+                                    Tile<TBN, halo_region<TBN, AS>()>>;
 constexpr int GATHER_WARP0 = 4;  // warps 4..7 (lane quarters 0..3) gather into tensor memory
 
 template <bool A_MN, bool B_MN, int EK, int TBN, int AS, int BS>
@@ -890,6 +894,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   constexpr bool HSEP = halo_region<TBN, AS>();
   constexpr bool ATM = a_in_tmem<TBN, AS>();
   using TL = LayoutOf<TBN, AS>;
+  constexpr bool NCAT = TL::NCAT;
   constexpr int ACC = TL::ACC;
   // Slices per barrier round: with A in tensor memory two ring slots fill,
   // gather and free together (one wait and one commit per two slices: the
@@ -1011,7 +1016,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
       if (leader) {  // ---- MMA issuer (leader CTA only): the warp runs the loop, the elected lane issues
         const bool issuer = elect_one();
-        const uint32_t idesc = instr_desc<A_MN, B_MN, ATM ? 2 * TBN : TBN>();
+        const uint32_t idesc = instr_desc<A_MN, B_MN, NCAT ? 2 * TBN : TBN>();
         // Descriptors of slot 0's planes; another slot or K step only moves
         // the start address (bits 0-13, in 16-byte units; shared addresses
         // stay below 256 KB, so the sum never carries out of the field).
@@ -1061,8 +1066,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; kk++) {
                   const uint32_t acc0 = (group_start && kk == 0) ? 0u : 1u;
-                  if constexpr (ATM) {  // each A plane against [B hi | B lo] from dbh: the CTA's 2 BNH rows
+                  if constexpr (NCAT) {  // each A plane against [B hi | B lo] from dbh: the CTA's 2 BNH rows
                     mma_tf32_pair_tmem_a(d, tal[kk], dbh[kk], idesc, acc0);
+                    mma_tf32_pair_tmem_a(d, tah[kk], dbh[kk], idesc, 1u);
+                  } else if constexpr (ATM) {
+                    mma_tf32_pair_tmem_a(d, tal[kk], dbh[kk], idesc, acc0);
+                    mma_tf32_pair_tmem_a(d, tah[kk], dbl[kk], idesc, 1u);
                     mma_tf32_pair_tmem_a(d, tah[kk], dbh[kk], idesc, 1u);
                   } else {
                     mma_tf32_pair(d, dal[kk], dbh[kk], idesc, acc0);
@@ -1212,9 +1221,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // this warp's rows, columns [HC*h, HC*h + HC) its half of the tile.
     // Every decision below is warp-uniform: tcgen05.ld is .sync.aligned.
     const int q = warp & 3, h = (warp - 8) >> 2;
-    // (A in tensor memory: this half's columns with B hi at h * TBN, those
-    // with B lo HC after)
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (ATM ? TBN * h : HC * h);
+    // (NCAT: this half's columns with B hi at h * TBN, those with B lo HC after)
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (NCAT ? TBN * h : HC * h);
     float* xpose = (float*)(smem + TL::EPI_OFFSET) + (warp - 8) * 32 * EPI_LD;
     int group = 0;
     for (int u = pair; u < units && !__shfl_sync(0xffffffffu, *failed, 0); u += pairs) {
@@ -1240,7 +1248,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        if constexpr (ATM) {
+        if constexpr (NCAT) {
           static_assert(HC == 32, "one chunk per half");
           float p[32], pl[32];
           tmem_load32(lane_base + buf * ACC, p);
