@@ -646,14 +646,35 @@ __device__ __forceinline__ void gather_pos(const Gather& g, uint8_t* hi, uint8_t
 // the halo (channel relative to the block's first) and its kind (gathered,
 // zero past C*KH*KW, or the row of ones that makes that row of the product
 // the bias gradient). A row's 16 positions go out as four 16-byte stores.
-__device__ __forceinline__ void ck_rows(const Gather& g, int row0, int lane, int (&koff)[4], int (&kind)[4]) {
+__device__ __forceinline__ void ck_row(const Gather& g, int row0, int r, int& koff, int& kind) {
   const int plane = g.box_w * g.box_h, c_lo = row0 / g.KHW;
+  const int ck = row0 + r;
+  const int c = ck / g.KHW, rem = ck - c * g.KHW, kh = rem / g.KW, kw = rem - kh * g.KW;
+  koff = (c - c_lo) * plane + kh * g.box_w + kw + g.rp - g.pad;
+  kind = ck < g.CKK ? 1 : ck == g.ones_row ? 2 : 0;
+}
+
+__device__ __forceinline__ void ck_rows(const Gather& g, int row0, int lane, int (&koff)[4], int (&kind)[4]) {
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int ck = row0 + lane + 32 * i;
-    const int c = ck / g.KHW, rem = ck - c * g.KHW, kh = rem / g.KW, kw = rem - kh * g.KW;
-    koff[i] = (c - c_lo) * plane + kh * g.box_w + kw + g.rp - g.pad;
-    kind[i] = ck < g.CKK ? 1 : ck == g.ones_row ? 2 : 0;
+  for (int i = 0; i < 4; i++) ck_row(g, row0, lane + 32 * i, koff[i], kind[i]);
+}
+
+// A_IM2COL_CK in tensor memory: the lane's own patch row (koff, kind from
+// ck_row) over the slice's 16 positions, split into v[0..15] = hi and
+// v[16..31] = lo. The slice's positions are rows of w16 (a power of two)
+// positions box_w apart in the halo, so each offset is independent of the
+// others. Only gathered rows (kind 1) read the halo.
+__device__ __forceinline__ void gather_ck_row_split(const Gather& g, uint32_t halo, int koff, int kind,
+                                                    float (&v)[32]) {
+  const int lw = __ffs(g.w16) - 1;
+  const float fill = kind == 2 ? 1.0f : 0.0f;
+#pragma unroll
+  for (int p = 0; p < 16; p++) {
+    const int off = (p >> lw) * g.box_w + (p & (g.w16 - 1));
+    const float x = kind == 1 ? ld_shared_f32(halo + 4u * (uint32_t)(koff + off)) : fill;
+    const float h = tf32_round(x);
+    v[p] = h;
+    v[16 + p] = tf32_round(__fsub_rn(x, h));
   }
 }
 
@@ -879,7 +900,7 @@ constexpr bool halo_region() {
 // these tiles on the shared-memory path.
 template <int TBN, int AS>
 constexpr bool a_in_tmem() {
-  return (AS == A_IM2COL_POS || AS == A_IM2COL_POS_FULL) && TBN <= 128;
+  return AS != A_TMA && TBN <= 128;
 }
 
 template <int TBN, int AS>
@@ -1112,8 +1133,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const int q = warp & 3, r = 32 * q + lane;
           const uint32_t a_lanes = tmem + ((uint32_t)(32 * q) << 16) + TL::A_COL0;
           int* tab = (int*)(smem + TL::TAB_OFFSET);
-          build_tap_table(ga, tab, r, 128);
-          asm volatile("bar.sync 1, 128;" ::: "memory");  // the four gather warps
+          if constexpr (AS != A_IM2COL_CK) {  // (a weight gradient's rows carry their own offsets)
+            build_tap_table(ga, tab, r, 128);
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four gather warps
+          }
           const uint32_t tab_base = smem_u32(tab);
           const int r16 = 16 % ga.KHW;
           int it = 0, hb = 0, mk = 0;
@@ -1124,6 +1147,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             unit_of(u, tiles, sp, num_k, t, kb, ke);
             const int a_row = (t / n_tiles) * 2 * BM + (int)rank * BM;
             if constexpr (AS == A_IM2COL_POS_FULL) pos_row_full<EK == EK_NCHW_POOL>(ga, a_row, s.M, r, hb, mk);
+            if constexpr (AS == A_IM2COL_CK) ck_row(ga, a_row, r, hb, mk);  // offset and kind of the patch row
             const bool live = (int64_t)a_row + r < s.M;  // a row past M gets zeros
             int m = (kb * BK) % ga.KHW;                   // the slice's first entry's tap
             for (int kt = kb; kt < ke; kt += SS, it++) {
@@ -1143,14 +1167,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               tc_fence_after();
               for (int i = 0; i < n_in; i++) {
                 const int st = nb * SS + i;
+                if constexpr (BS != B_SPLIT2) {  // B arrives unsplit: each gather warp splits a quarter in place
+                  constexpr int per = (int)(TL::B_BYTES / 16) / 4;
+                  float4* bh = (float4*)(smem + st * TL::STAGE_BYTES + TL::B_OFF);
+                  split_tf32(bh + q * per, bh + TL::B_BYTES / 16 + q * per, per, lane);
+                }
                 float v[32];
-                gather_row_split<AS == A_IM2COL_POS_FULL>(ga, smem_u32(smem + st * TL::STAGE_BYTES + TL::HALO_OFF),
-                                                          tab_base + 64u * m, live, (kt + i) * BK, hb, mk, v);
+                const uint32_t halo = smem_u32(smem + st * TL::STAGE_BYTES + TL::HALO_OFF);
+                if constexpr (AS == A_IM2COL_CK)
+                  gather_ck_row_split(ga, halo, hb, mk, v);
+                else
+                  gather_row_split<AS == A_IM2COL_POS_FULL>(ga, halo, tab_base + 64u * m, live, (kt + i) * BK, hb,
+                                                            mk, v);
                 __syncwarp();
                 tmem_store32(a_lanes + 32 * st, v);
                 m = m + r16 >= ga.KHW ? m + r16 - ga.KHW : m + r16;
               }
               tmem_wait_st();
+              if constexpr (BS != B_SPLIT2) fence_async_shared();  // generic-proxy writes -> the tensor core
               tc_fence_before();
               __syncwarp();
               if (lane == 0 && !(sp.withhold_arrive && it == 0 && leader)) mbar_arrive_rank(&sh->split[nb], 0);
