@@ -18,7 +18,9 @@
 //   warp 0      TMA producer: fp32 slices of A and B (16 elements of K) into
 //               a 6-stage shared-memory ring, K-major or M/N-major;
 //   warp 1      (leader CTA) MMA issuer: 3 x 2 tcgen05.mma per slice into a
-//               partial accumulator, commits that free the slot in both CTAs;
+//               partial accumulator, commits that free the slot in both CTAs
+//               (both warps run their loops warp-wide; one elected lane
+//               issues);
 //   warps 2-7   splitters, one per ring slot: warp 2+j rewrites every slice
 //               landing in slot j as tf32 hi (in place) and lo (beside it),
 //               then signals the leader's MMA, so six slices are split
@@ -39,7 +41,9 @@
 // materialising its im2col columns: the splitter warps, which rewrite every
 // staged tile anyway, instead read the im2col values of the A operand
 // straight from the NCHW tensor (x, or dy for the input gradient) and write
-// them, split, into the swizzled shared-memory layout the MMA reads. Two
+// them, split, into the swizzled shared-memory layout the MMA reads. For
+// tiles up to 128 wide, four gather warps write them to tensor memory
+// instead, and the MMA reads A from there (TileT, a_in_tmem). Two
 // orientations: positions on M with the input channels' patches on K (the
 // forward pass, and the input gradient as the forward convolution of dy with
 // the flipped, transposed weight), and patches on M with positions on K (the
@@ -176,11 +180,12 @@ enum BSrc : int { B_TMA2 = 0, B_TMA3 = 1, B_SPLIT2 = 2 };
 // A_IM2COL_CK orientation) is a row of ones (-1: none).
 //
 // Per K-slice the producer copies, with one 4-D TMA load over src's
-// (W, H, C, N) dimensions, the "halo" the slice needs into the stage's lo
-// plane: box_w columns from x0 (rounded down to a 16-byte boundary, so the
-// TMA's innermost coordinate stays aligned), box_h rows, box_c channels,
-// box_n images, zero outside the tensor (the convolution's padding). The
-// splitter warps build the slice's im2col tile from it in shared memory.
+// (W, H, C, N) dimensions, the "halo" the slice needs into the stage's halo
+// region (the lo plane at BN 256): box_w columns from x0 (rounded down to a
+// 16-byte boundary, so the TMA's innermost coordinate stays aligned), box_h
+// rows, box_c channels, box_n images, zero outside the tensor (the
+// convolution's padding). The splitter warps build the slice's im2col tile
+// from it in shared memory, or the gather warps in tensor memory.
 //   A_IM2COL_POS: a CTA's 128 rows are 128 consecutive positions forming a
 //     rectangle: rows_pi (= bh * OW) positions of each of box_n images, bh
 //     output rows each. The halo holds the channels of the slice's 16 patch
